@@ -1,0 +1,165 @@
+// cis2b_ref -- command-line front end of libcis2b.so that prints the
+// reference's stdout contract, so harnesses that parse the reference's
+// lines by regex keep working unchanged:
+//   weights_sha256= / tokenizer_sha256= / config_sha256= / table_digest= /
+//   inv_freq_table_digest= / prompt_idx=N prompt_tokens=[..] / run1_tokens= /
+//   run1_witness_digest= / run1_argmax_digest= / reduction_mode= /
+//   CIS2_REF digest=<hex> prompt_idx=N prompt_toks=N gen_toks=N dtype=fp32 reduction_mode=M
+// (code/cis2-fp/gpu/cis2_host.cpp:222-245; src/main.rs:1231-1262) and, in
+// sampled mode, the E23 line
+//   CIS2_SAMPLE digest=<hex> mode=sampled seed=S temperature=T top_p=P prompt_idx=N ...
+// (code/patches/cis2-fp__cm_e23-pinned-sampling.patch:770-779).
+//
+//   cis2b_ref --weights-dir D --ids F [--gen-toks N] [--reduction sequential|tree]
+//             [--mode greedy|sampled --seed S --temperature T --top-p P]
+//             [--device I] [--prompt-idx I] [--step-digests]
+// Each non-empty line of F is one prompt (decimal ids); all prompts are
+// decoded as one batch and reported in file order.
+#include "cis2b.h"
+
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+static std::string hexs(const uint8_t *b, size_t n) {
+  static const char *d = "0123456789abcdef";
+  std::string s;
+  for (size_t i = 0; i < n; ++i) { s.push_back(d[b[i] >> 4]); s.push_back(d[b[i] & 15]); }
+  return s;
+}
+
+static std::string ids_list(const uint32_t *v, size_t n) {
+  std::string s = "[";
+  for (size_t i = 0; i < n; ++i) {
+    if (i) s += ", ";
+    s += std::to_string(v[i]);
+  }
+  return s + "]";
+}
+
+// Shortest decimal that reads back as the same f32 (how Rust prints f32).
+static std::string f32_str(float x) {
+  char buf[64];
+  for (int p = 1; p <= 9; ++p) {
+    snprintf(buf, sizeof buf, "%.*g", p, (double)x);
+    if (strtof(buf, nullptr) == x) break;
+  }
+  return buf;
+}
+
+int main(int argc, char **argv) {
+  std::string weights_dir = "weights", ids_path;
+  int gen = 16, device = 0, prompt_idx = 0;
+  bool tree = false, sampled = false, step_digests = false;
+  cis2b_sample smp{0, 0.8f, 0.95f};
+  for (int i = 1; i < argc; ++i) {
+    std::string a = argv[i];
+    auto next = [&]() -> const char * {
+      if (i + 1 >= argc) { fprintf(stderr, "FATAL: %s needs a value\n", a.c_str()); exit(2); }
+      return argv[++i];
+    };
+    if (a == "--weights-dir") weights_dir = next();
+    else if (a == "--ids") ids_path = next();
+    else if (a == "--gen-toks") gen = atoi(next());
+    else if (a == "--device") device = atoi(next());
+    else if (a == "--prompt-idx") prompt_idx = atoi(next());
+    else if (a == "--step-digests") step_digests = true;
+    else if (a == "--reduction") {
+      std::string v = next();
+      if (v == "tree") tree = true;
+      else if (v != "sequential") { fprintf(stderr, "FATAL: --reduction sequential|tree\n"); return 2; }
+    } else if (a == "--mode") {
+      std::string v = next();
+      if (v == "sampled") sampled = true;
+      else if (v != "greedy") { fprintf(stderr, "FATAL: --mode greedy|sampled\n"); return 2; }
+    } else if (a == "--seed") smp.seed = strtoull(next(), nullptr, 10);
+    else if (a == "--temperature") smp.temperature = strtof(next(), nullptr);
+    else if (a == "--top-p") smp.top_p = strtof(next(), nullptr);
+    else { fprintf(stderr, "FATAL: unknown CLI argument: %s\n", a.c_str()); return 2; }
+  }
+  if (ids_path.empty() || gen < 0) { fprintf(stderr, "FATAL: --ids FILE is required\n"); return 2; }
+
+  std::vector<std::vector<uint32_t>> prompts;
+  {
+    FILE *f = fopen(ids_path.c_str(), "rb");
+    if (!f) { fprintf(stderr, "FATAL: cannot open %s\n", ids_path.c_str()); return 2; }
+    std::vector<uint32_t> cur;
+    std::string num;
+    int c;
+    auto flush_num = [&]() {
+      if (!num.empty()) { cur.push_back((uint32_t)strtoul(num.c_str(), nullptr, 10)); num.clear(); }
+    };
+    while ((c = fgetc(f)) != EOF) {
+      if (c >= '0' && c <= '9') num.push_back((char)c);
+      else if (c == '\n') { flush_num(); if (!cur.empty()) prompts.push_back(cur); cur.clear(); }
+      else if (c == ' ' || c == '\t' || c == ',' || c == '\r') flush_num();
+      else { fprintf(stderr, "FATAL: %s: unexpected character\n", ids_path.c_str()); return 2; }
+    }
+    flush_num();
+    if (!cur.empty()) prompts.push_back(cur);
+    fclose(f);
+  }
+  if (prompts.empty()) { fprintf(stderr, "FATAL: %s: no token ids\n", ids_path.c_str()); return 2; }
+
+  cis2b_opts o{};
+  o.device = device;
+  o.reduction = tree ? CIS2B_REDUCTION_TREE : CIS2B_REDUCTION_SEQUENTIAL;
+  size_t maxp = 0;
+  for (auto &p : prompts) maxp = p.size() > maxp ? p.size() : maxp;
+  o.max_positions = (int32_t)(maxp + (size_t)gen > 4096 ? maxp + (size_t)gen : 4096);
+  cis2b_model *m = nullptr;
+  if (cis2b_load(weights_dir.c_str(), &o, &m) != CIS2B_OK) {
+    fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
+    return 2;
+  }
+  cis2b_info info;
+  cis2b_info_get(m, &info);
+
+  const uint32_t n = (uint32_t)prompts.size();
+  std::vector<uint32_t> flat, lens;
+  for (auto &p : prompts) { flat.insert(flat.end(), p.begin(), p.end()); lens.push_back((uint32_t)p.size()); }
+  std::vector<uint32_t> toks((size_t)n * gen);
+  std::vector<uint8_t> steps((size_t)n * gen * 32), wit((size_t)n * 32), arg((size_t)n * 32);
+  if (cis2b_generate(m, flat.data(), lens.data(), n, (uint32_t)gen, sampled ? &smp : nullptr, toks.data(),
+                     steps.data(), wit.data(), arg.data()) != CIS2B_OK) {
+    fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
+    cis2b_free(m);
+    return 2;
+  }
+  printf("weights_sha256=%s\n", hexs(info.weights_sha256, 32).c_str());
+  printf("tokenizer_sha256=%s\n", hexs(info.tokenizer_sha256, 32).c_str());
+  printf("config_sha256=%s\n", hexs(info.config_sha256, 32).c_str());
+  printf("table_digest=%s\n", hexs(info.table_digest, 32).c_str());
+  printf("inv_freq_table_digest=%s\n", hexs(info.inv_freq_table_digest, 32).c_str());
+  const char *mode = tree ? "tree" : "sequential";
+  size_t off = 0;
+  for (uint32_t s = 0; s < n; ++s) {
+    const int pi = prompt_idx + (int)s;
+    const uint32_t *p = flat.data() + off;
+    off += lens[s];
+    std::vector<uint32_t> all(p, p + lens[s]);
+    all.insert(all.end(), toks.begin() + (size_t)s * gen, toks.begin() + (size_t)(s + 1) * gen);
+    printf("prompt_idx=%d prompt_tokens=%s\n", pi, ids_list(p, lens[s]).c_str());
+    printf("prompt_idx=%d run1_tokens=%s\n", pi, ids_list(all.data(), all.size()).c_str());
+    printf("prompt_idx=%d run1_witness_digest=%s\n", pi, hexs(&wit[(size_t)s * 32], 32).c_str());
+    printf("prompt_idx=%d run1_argmax_digest=%s\n", pi, hexs(&arg[(size_t)s * 32], 32).c_str());
+    if (step_digests)
+      for (int t = 0; t < gen; ++t)
+        printf("prompt_idx=%d step=%d witness=%s\n", pi, t,
+               hexs(&steps[((size_t)s * gen + t) * 32], 32).c_str());
+    printf("prompt_idx=%d reduction_mode=%s\n", pi, mode);
+    if (sampled)
+      printf("CIS2_SAMPLE digest=%s mode=sampled seed=%llu temperature=%s top_p=%s prompt_idx=%d "
+             "prompt_toks=%u gen_toks=%d dtype=fp32\n",
+             hexs(&wit[(size_t)s * 32], 32).c_str(), (unsigned long long)smp.seed,
+             f32_str(smp.temperature).c_str(), f32_str(smp.top_p).c_str(), pi, lens[s], gen);
+    else
+      printf("CIS2_REF digest=%s prompt_idx=%d prompt_toks=%u gen_toks=%d dtype=fp32 reduction_mode=%s\n",
+             hexs(&wit[(size_t)s * 32], 32).c_str(), pi, lens[s], gen, mode);
+  }
+  cis2b_free(m);
+  return 0;
+}

@@ -1,0 +1,1005 @@
+// cis2b_kernels.cu -- sm_100a kernels of the CIS-2 deterministic decode path.
+//
+// Arithmetic contract (what makes every output bit-identical to the
+// reference CPU path, code/cis2-fp/gpu/cis2_model.h:503-760):
+//   * one output element is produced by ONE thread walking its reduction in
+//     the pinned order -- sequential (spec §5.1/§5.3) or the v0.4 32-leaf
+//     tree (cis2_math.h:212-265) -- and no reduction is ever split across
+//     threads except as the tree prescribes (warp butterflies reproduce the
+//     pairwise rounds exactly because IEEE addition is commutative);
+//   * every multiply and add is a separately rounded .rn.ftz instruction
+//     (cis2b_pinned.cuh);
+//   * order-free steps (max, argmax with lowest-index ties, element-wise
+//     maps) use parallel reductions with the reference's tie and NaN rules.
+// No tensor cores: their fp32 accumulation order is unspecified.
+#include "cis2b_kernels.h"
+#include "cis2b_pinned.cuh"
+#include "cis2b_sha256.cuh"
+
+#include <stdio.h>
+
+namespace cis2b {
+
+static constexpr unsigned FULL = 0xffffffffu;
+
+// ============================================================ reductions
+
+// Pairwise 32-leaf tree across a warp: after round s every lane holds the
+// sum of its aligned 2^(s+1)-lane group, built exactly as
+// leaf[i] = leaf[2i] + leaf[2i+1] (cis2_math.h:218-228).
+__device__ __forceinline__ float warp_tree32(float v) {
+#pragma unroll
+  for (int s = 1; s < 32; s <<= 1) v = fadd(v, __shfl_xor_sync(FULL, v, s));
+  return v;
+}
+
+// Thread-local pinned dot of two smem/global vectors.
+__device__ __forceinline__ float dot_seq(const float *a, const float *b, int n) {
+  float acc = 0.0f;
+  for (int i = 0; i < n; ++i) acc = fadd(acc, fmul(a[i], b[i]));
+  return acc;
+}
+__device__ __forceinline__ float tree32_local(float *leaf) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) leaf[i] = fadd(leaf[2 * i], leaf[2 * i + 1]);
+  return leaf[0];
+}
+__device__ __forceinline__ float dot_tree(const float *a, const float *b, int n) {
+  float acc = 0.0f;
+  for (int s = 0; s < n; s += 32) {
+    float leaf[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) leaf[i] = (s + i < n) ? fmul(a[s + i], b[s + i]) : 0.0f;
+    acc = fadd(acc, tree32_local(leaf));
+  }
+  return acc;
+}
+
+// RMSNorm of one row by one warp (cis2_model.h:511-523):
+// sq = x*x; ss = fold(sq); mean = ss/n; inv = 1/sqrt(mean+eps); out = (x*inv)*w.
+// `sq` is warp-private scratch of n floats.  out may alias x.
+__device__ __forceinline__ void warp_rmsnorm(const float *x, const uint16_t *w, float eps, int n,
+                                             bool tree, float *sq, float *out) {
+  const int lane = threadIdx.x & 31;
+  float ss;
+  if (!tree) {
+    for (int i = lane; i < n; i += 32) sq[i] = fmul(x[i], x[i]);
+    __syncwarp();
+    float acc = 0.0f;
+    if (lane == 0)
+      for (int i = 0; i < n; ++i) acc = fadd(acc, sq[i]);
+    ss = __shfl_sync(FULL, acc, 0);
+  } else {
+    float acc = 0.0f;
+    for (int s = 0; s < n; s += 32) {
+      float v = (s + lane < n) ? fmul(x[s + lane], x[s + lane]) : 0.0f;
+      acc = fadd(acc, warp_tree32(v));
+    }
+    ss = acc;
+  }
+  float mean = fdiv(ss, __int2float_rn(n));
+  float inv = rsqrt_cr(fadd(mean, eps));
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) out[i] = fmul(fmul(x[i], inv), widen_bf16(w[i]));
+  __syncwarp();
+}
+
+// ============================================================ tables
+
+__global__ void k_inv_freq(float theta, int hd, float *out) {
+  int i = threadIdx.x + blockIdx.x * blockDim.x;
+  if (i >= hd / 2) return;
+  // cis2_model.h:456-465: ln of theta narrowed once; frac = (2i)/hd.
+  float ln_theta = ln_pinned(theta);
+  float frac = fdiv(__int2float_rn(2 * i), __int2float_rn(hd));
+  float a = fmul(frac, ln_theta);
+  out[i] = exp_pinned(fneg(a));
+}
+
+__global__ void k_rope_table(const float *inv_freq, int half, int max_pos, float *cos_t, float *sin_t) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)half * (size_t)max_pos) return;
+  int pos = (int)(idx / half), i = (int)(idx % half);
+  // angle = (f32)pos * inv_freq[i] (cis2_model.h:554); cos/sin pinned.
+  float angle = fmul(__int2float_rn(pos), inv_freq[i]);
+  cos_t[idx] = cos_pinned(angle);
+  sin_t[idx] = sin_pinned(angle);
+}
+
+void launch_inv_freq(float theta, int hd, float *inv_freq, cudaStream_t s) {
+  k_inv_freq<<<1, 256, 0, s>>>(theta, hd, inv_freq);
+}
+void launch_rope_table(const float *inv_freq, int half, int max_pos, float *cos_t, float *sin_t,
+                       cudaStream_t s) {
+  size_t n = (size_t)half * (size_t)max_pos;
+  k_rope_table<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(inv_freq, half, max_pos, cos_t, sin_t);
+}
+
+// ============================================================ embed / norm / elementwise
+
+__global__ void k_embed(const uint16_t *E, int H, const uint32_t *tokens, int rows, float *h) {
+  int r = blockIdx.x;
+  const uint16_t *src = E + (size_t)tokens[r] * (size_t)H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) h[(size_t)r * H + i] = widen_bf16(src[i]);
+}
+void launch_embed(const uint16_t *E, int H, const uint32_t *tokens, int rows, float *h,
+                  cudaStream_t s) {
+  if (rows <= 0) return;
+  k_embed<<<rows, 256, 0, s>>>(E, H, tokens, rows, h);
+}
+
+__global__ void k_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows,
+                          int tree, float *out, int ldo) {
+  extern __shared__ float sm[];
+  int warp = threadIdx.x >> 5;
+  int r = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (r >= rows) return;
+  warp_rmsnorm(x + (size_t)r * ldx, w, eps, n, tree != 0, sm + (size_t)warp * n,
+               out + (size_t)r * ldo);
+}
+void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
+                    float *out, int ldo, cudaStream_t s) {
+  if (rows <= 0) return;
+  const int wpb = 4;
+  k_rmsnorm<<<(rows + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * n * sizeof(float), s>>>(
+      x, ldx, w, eps, n, rows, tree ? 1 : 0, out, ldo);
+}
+
+__global__ void k_silu_mul(const float *gu, int I, int rows, float *hid) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)rows * I) return;
+  size_t r = idx / I, i = idx % I;
+  const float *row = gu + r * 2 * (size_t)I;
+  hid[idx] = fmul(silu_pinned(row[i]), row[I + i]);  // silu(g)*up (cis2_model.h:619-623)
+}
+void launch_silu_mul(const float *gu, int I, int rows, float *hid, cudaStream_t s) {
+  size_t n = (size_t)rows * I;
+  if (!n) return;
+  k_silu_mul<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(gu, I, rows, hid);
+}
+
+__global__ void k_add_bias(float *x, int ld, int rows, const uint16_t *b, int n) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)rows * n) return;
+  size_t r = idx / n, i = idx % n;
+  float *p = x + r * ld + i;
+  *p = fadd(*p, widen_bf16(b[i]));  // cis2_model.h:535-538
+}
+void launch_add_bias(float *x, int ld, int rows, const uint16_t *b, int n, cudaStream_t s) {
+  size_t tot = (size_t)rows * n;
+  if (!b || !tot) return;
+  k_add_bias<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(x, ld, rows, b, n);
+}
+
+__global__ void k_pinned_map(int fn, const float *x, float *y, size_t n) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float v = x[i], r;
+  switch (fn) {
+    case 0: r = exp_pinned(v); break;
+    case 1: r = sin_pinned(v); break;
+    case 2: r = cos_pinned(v); break;
+    case 3: r = ln_pinned(v); break;
+    case 4: r = silu_pinned(v); break;
+    default: r = rsqrt_cr(v); break;
+  }
+  y[i] = r;
+}
+void launch_pinned_map(int fn, const float *x, float *y, size_t n, cudaStream_t s) {
+  if (!n) return;
+  k_pinned_map<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(fn, x, y, n);
+}
+
+// ============================================================ GEMM
+//
+// Y[m][n] = dot(W[n][:], X[m][:]).  One thread owns a TM x TN tile of
+// outputs and walks k = 0..K-1 in order for all of them: the register
+// tiling reuses smem loads across outputs without ever splitting a dot
+// product.  W arrives as bf16 and is widened exactly (bits << 16) while it
+// is staged into shared memory, so HBM carries half the reference's fp32
+// bytes.  Padding past K contributes +0 products, which leave a sequential
+// accumulator unchanged (it starts at +0 and can never be -0) and are the
+// spec's own zero leaves in tree mode.
+template <int BM, int BN, int TM, int TN, bool TREE>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+k_gemm(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ W, int K, int N, int M,
+       float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
+       size_t y_slot_stride) {
+  constexpr int NT = (BM / TM) * (BN / TN);
+  constexpr int BK = 32;
+  constexpr int WS = BN + 4;  // smem row strides (floats), keep 16-byte alignment
+  constexpr int XS = BM + 4;
+  constexpr int WCH = (BN * 4 + NT - 1) / NT;  // 16-byte W chunks per thread
+  constexpr int XCH = (BM * 8 + NT - 1) / NT;  // 16-byte X chunks per thread
+  extern __shared__ __align__(16) float smem[];
+  float *Ws = smem;                 // [2][BK][WS]
+  float *Xs = smem + 2 * BK * WS;   // [2][BK][XS]
+
+  const int tid = threadIdx.x;
+  const int tn = tid % (BN / TN), tm = tid / (BN / TN);
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+
+  uint4 wreg[WCH];
+  float4 xreg[XCH];
+  auto gload = [&](int k0) {
+#pragma unroll
+    for (int c = 0; c < WCH; ++c) {
+      int id = tid + c * NT;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (id < BN * 4) {
+        int r = id >> 2, k = k0 + (id & 3) * 8, n = n0 + r;
+        if (n < N && k < K) v = __ldg(reinterpret_cast<const uint4 *>(W + (size_t)n * K + k));
+      }
+      wreg[c] = v;
+    }
+#pragma unroll
+    for (int c = 0; c < XCH; ++c) {
+      int id = tid + c * NT;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (id < BM * 8) {
+        int r = id >> 3, k = k0 + (id & 7) * 4, m = m0 + r;
+        if (m < M && k < K) v = *reinterpret_cast<const float4 *>(X + (size_t)m * ldx + k);
+      }
+      xreg[c] = v;
+    }
+  };
+  auto sstore = [&](int buf) {
+    float *ws = Ws + buf * BK * WS;
+    float *xs = Xs + buf * BK * XS;
+#pragma unroll
+    for (int c = 0; c < WCH; ++c) {
+      int id = tid + c * NT;
+      if (id < BN * 4) {
+        int r = id >> 2, q = (id & 3) * 8;
+        uint32_t u[4] = {wreg[c].x, wreg[c].y, wreg[c].z, wreg[c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          ws[(q + 2 * e) * WS + r] = __uint_as_float(u[e] << 16);
+          ws[(q + 2 * e + 1) * WS + r] = __uint_as_float(u[e] & 0xffff0000u);
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < XCH; ++c) {
+      int id = tid + c * NT;
+      if (id < BM * 8) {
+        int r = id >> 3, q = (id & 7) * 4;
+        xs[(q + 0) * XS + r] = xreg[c].x;
+        xs[(q + 1) * XS + r] = xreg[c].y;
+        xs[(q + 2) * XS + r] = xreg[c].z;
+        xs[(q + 3) * XS + r] = xreg[c].w;
+      }
+    }
+  };
+  // Column owned by output j of this thread.
+  auto ncol = [&](int j) -> int {
+    if (TN == 8) return (j < 4) ? tn * 4 + j : BN / 2 + tn * 4 + (j - 4);
+    return tn * TN + j;
+  };
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  const int nk = (K + BK - 1) / BK;
+  for (int kt = 0; kt < nk; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < nk) gload((kt + 1) * BK);
+    const float *ws = Ws + buf * BK * WS;
+    const float *xs = Xs + buf * BK * XS;
+    if (!TREE) {
+#pragma unroll 4
+      for (int kk = 0; kk < BK; ++kk) {
+        float w[TN], x[TM];
+#pragma unroll
+        for (int j = 0; j < TN; ++j) w[j] = ws[kk * WS + ncol(j)];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) x[i] = xs[kk * XS + tm * TM + i];
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) acc[i][j] = fadd(acc[i][j], fmul(w[j], x[i]));
+      }
+    } else {
+      // Streaming pairwise tree over the 32 leaves of this k tile: level L
+      // keeps the pending left operand; leaf kk closes as many levels as kk
+      // has trailing one bits.  Same adds, same operands as tree32.
+      float lv[5][TM][TN];
+#pragma unroll
+      for (int kk = 0; kk < BK; ++kk) {
+        float w[TN], x[TM];
+#pragma unroll
+        for (int j = 0; j < TN; ++j) w[j] = ws[kk * WS + ncol(j)];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) x[i] = xs[kk * XS + tm * TM + i];
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) {
+            float v = fmul(w[j], x[i]);
+            int t = kk, lvl = 0;
+#pragma unroll
+            for (int q = 0; q < 5; ++q) {
+              if (t & 1) { v = fadd(lv[lvl][i][j], v); t >>= 1; ++lvl; }
+              else break;
+            }
+            if (lvl < 5) lv[lvl][i][j] = v;
+            else acc[i][j] = fadd(acc[i][j], v);
+          }
+      }
+    }
+    if (kt + 1 < nk) sstore(buf ^ 1);
+    __syncthreads();
+  }
+
+  float *Yb = Y + (y_slot ? (size_t)(*y_slot) * y_slot_stride : 0);
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    int m = m0 + tm * TM + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      int n = n0 + ncol(j);
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if (R) v = fadd(R[(size_t)m * ldr + n], v);  // residual h + o (cis2_model.h:540-542)
+      Yb[(size_t)m * ldy + n] = v;
+    }
+  }
+}
+
+template <int BM, int BN, int TM, int TN, bool TREE>
+static void run_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
+                     const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride,
+                     cudaStream_t s) {
+  constexpr int NT = (BM / TM) * (BN / TN);
+  size_t smem = (size_t)2 * 32 * ((BN + 4) + (BM + 4)) * sizeof(float);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_gemm<BM, BN, TM, TN, TREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    attr_set = true;
+  }
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  k_gemm<BM, BN, TM, TN, TREE><<<grid, NT, smem, s>>>(X, ldx, W, K, N, M, Y, ldy, R, ldr, y_slot,
+                                                      y_slot_stride);
+}
+
+// Tile choice: the largest tile that still gives >= 2 CTAs per SM without
+// wasting more than half of a row tile; small problems fall back to one
+// output per thread so that every SM has dot products to walk.
+void launch_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
+                 const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
+                 cudaStream_t s) {
+  if (M <= 0 || N <= 0) return;
+  const long target = 2 * 148;
+  auto ctas = [&](int bm, int bn) { return (long)((N + bn - 1) / bn) * ((M + bm - 1) / bm); };
+  auto fits = [&](int bm) { return M >= bm / 2 || bm == 1; };
+#define CIS2B_GEMM(BM_, BN_, TM_, TN_)                                                         \
+  do {                                                                                         \
+    if (tree)                                                                                  \
+      run_gemm<BM_, BN_, TM_, TN_, true>(X, ldx, W, K, N, M, Y, ldy, resid, ldr, y_slot,        \
+                                         y_slot_stride, s);                                   \
+    else                                                                                       \
+      run_gemm<BM_, BN_, TM_, TN_, false>(X, ldx, W, K, N, M, Y, ldy, resid, ldr, y_slot,       \
+                                          y_slot_stride, s);                                  \
+    return;                                                                                    \
+  } while (0)
+  if (!tree && fits(64) && ctas(64, 128) >= target) CIS2B_GEMM(64, 128, 4, 8);
+  if (fits(32) && ctas(32, 64) >= target) CIS2B_GEMM(32, 64, 2, 4);
+  if (fits(16) && ctas(16, 64) >= target) CIS2B_GEMM(16, 64, 1, 4);
+  if (fits(8) && ctas(8, 64) >= target) CIS2B_GEMM(8, 64, 1, 2);
+  if (M >= 4) CIS2B_GEMM(4, 64, 1, 1);
+  CIS2B_GEMM(1, 256, 1, 1);
+#undef CIS2B_GEMM
+}
+
+// ============================================================ attention
+
+// Per row: optional per-head q/k RMSNorm (qwen3-port.diff:66-80), RoPE of
+// every q and k head from the pinned cos/sin table (cis2_model.h:547-568),
+// then the KV-cache append of post-RoPE k and raw v (cis2_model.h:718-721).
+__global__ void k_qkv_post(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, int nh,
+                           int nkv, int hd, const uint16_t *qn, const uint16_t *kn, float eps,
+                           int tree, const float *cos_t, const float *sin_t, float *kc, float *vc,
+                           int max_pos) {
+  extern __shared__ float sm[];
+  const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  float *row = qkv + (size_t)r * ld;
+  const int seq = rseq[r], pos = rpos[r];
+  const int half = hd / 2, QD = nh * hd, KV = nkv * hd;
+  const float *ct = cos_t + (size_t)pos * half;
+  const float *st = sin_t + (size_t)pos * half;
+  float *sq = sm + (size_t)warp * hd;
+  for (int h = warp; h < nh + nkv; h += nw) {
+    const bool is_k = h >= nh;
+    float *x = is_k ? row + QD + (size_t)(h - nh) * hd : row + (size_t)h * hd;
+    const uint16_t *nwt = is_k ? kn : qn;
+    if (nwt) warp_rmsnorm(x, nwt, eps, hd, tree != 0, sq, x);
+    for (int i = lane; i < half; i += 32) {
+      float x1 = x[i], x2 = x[i + half], c = ct[i], s = st[i];
+      float o1 = fadd(fmul(x1, c), fmul(fneg(x2), s));
+      float o2 = fadd(fmul(x2, c), fmul(x1, s));
+      x[i] = o1;
+      x[i + half] = o2;
+    }
+    __syncwarp();
+    if (is_k) {
+      float *dst = kc + ((size_t)seq * max_pos + pos) * KV + (size_t)(h - nh) * hd;
+      for (int i = lane; i < hd; i += 32) dst[i] = x[i];
+    }
+  }
+  float *vdst = vc + ((size_t)seq * max_pos + pos) * KV;
+  for (int i = threadIdx.x; i < KV; i += blockDim.x) vdst[i] = row[QD + KV + i];
+}
+
+void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
+                     const uint16_t *q_norm, const uint16_t *k_norm, float eps, bool tree,
+                     const float *cos_t, const float *sin_t, float *kcache, float *vcache,
+                     int max_pos, cudaStream_t s) {
+  if (rows <= 0) return;
+  const int threads = 128;
+  k_qkv_post<<<rows, threads, (size_t)(threads / 32) * hd * sizeof(float), s>>>(
+      qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, q_norm, k_norm, eps, tree ? 1 : 0, cos_t, sin_t,
+      kcache, vcache, max_pos);
+}
+
+// NaN-aware max combine reproducing the serial "if (v > max) max = v" scan
+// started at element 0: NaNs after element 0 are never selected.
+__device__ __forceinline__ float max_comb(float a, float b) {
+  if (is_nan(a)) return b;
+  if (is_nan(b)) return a;
+  return (b > a) ? b : a;
+}
+
+// One CTA per (row, query head): scores (dot * scale, cis2_model.h:571-585),
+// softmax (max scan, pinned exp, pinned-order denominator, divide;
+// cis2_math.h:442-467), V-mix serial over key positions (cis2_model.h:599-617).
+__global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
+                            int nh, int nkv, int hd, const float *kc, const float *vc, int max_pos,
+                            int tree, float *att, int ld_att, int max_len) {
+  extern __shared__ float sm[];
+  const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+  const int seq = rseq[r], pos = rpos[r], len = pos + 1;
+  const int group = nh / nkv, kvh = h / group, KV = nkv * hd;
+  float *q = sm;                 // [hd]
+  float *sc = q + hd;            // [max_len]
+  float *part = sc + max_len;    // [max_len/32 + 1]
+  float *red = part + (max_len / 32 + 1);  // [32]
+  for (int d = tid; d < hd; d += nt) q[d] = qkv[(size_t)r * ld + (size_t)h * hd + d];
+  __syncthreads();
+  const float scale = rsqrt_cr(__int2float_rn(hd));
+  const float *kbase = kc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
+  for (int j = tid; j < len; j += nt) {
+    const float *kj = kbase + (size_t)j * KV;
+    float d = tree ? dot_tree(q, kj, hd) : dot_seq(q, kj, hd);
+    sc[j] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
+  }
+  __syncthreads();
+  // max
+  float m = bitsf(0x7fc00000u);
+  for (int j = tid; j < len; j += nt) m = max_comb(m, sc[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max_comb(m, __shfl_xor_sync(FULL, m, o));
+  if ((tid & 31) == 0) red[tid >> 5] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float mm = red[0];
+    for (int w = 1; w < nt / 32; ++w) mm = max_comb(mm, red[w]);
+    if (is_nan(sc[0])) mm = sc[0];
+    red[0] = mm;
+  }
+  __syncthreads();
+  const float mx = red[0];
+  for (int j = tid; j < len; j += nt) sc[j] = exp_pinned(fsub(sc[j], mx));
+  __syncthreads();
+  if (!tree) {
+    if (tid == 0) {
+      float acc = 0.0f;
+      for (int j = 0; j < len; ++j) acc = fadd(acc, sc[j]);
+      red[1] = acc;
+    }
+  } else {
+    const int nb = (len + 31) / 32, warp = tid >> 5, lane = tid & 31;
+    for (int b = warp; b < nb; b += nt / 32) {
+      int j = b * 32 + lane;
+      float v = warp_tree32(j < len ? sc[j] : 0.0f);
+      if (lane == 0) part[b] = v;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float acc = 0.0f;
+      for (int b = 0; b < nb; ++b) acc = fadd(acc, part[b]);
+      red[1] = acc;
+    }
+  }
+  __syncthreads();
+  const float den = red[1];
+  for (int j = tid; j < len; j += nt) sc[j] = fdiv(sc[j], den);
+  __syncthreads();
+  const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
+  for (int d = tid; d < hd; d += nt) {
+    float acc = 0.0f;
+    for (int j = 0; j < len; ++j) acc = fadd(acc, fmul(sc[j], vbase[(size_t)j * KV + d]));
+    att[(size_t)r * ld_att + (size_t)h * hd + d] = acc;
+  }
+}
+
+void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
+                      const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
+                      int ld_att, int max_len, cudaStream_t s) {
+  if (rows <= 0) return;
+  size_t smem = (size_t)(hd + max_len + max_len / 32 + 1 + 32) * sizeof(float);
+  static size_t attr = 0;
+  if (smem > 48 * 1024 && smem > attr) {
+    cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = smem;
+  }
+  dim3 grid(rows, n_heads);
+  k_attention<<<grid, 128, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache,
+                                      max_pos, tree ? 1 : 0, att, ld_att, max_len);
+}
+
+// ============================================================ token selection
+
+struct ArgBest { float v; int i; };
+// Lowest index among the maximal non-NaN values (the serial strict-'>' scan
+// from index 0 of cis2_model.h:764-774, given element 0 is not NaN).
+__device__ __forceinline__ ArgBest arg_comb(ArgBest a, ArgBest b) {
+  if (a.i < 0) return b;
+  if (b.i < 0) return a;
+  if (b.v > a.v) return b;
+  if (a.v > b.v) return a;
+  return (b.i < a.i) ? b : a;
+}
+
+__global__ void k_argmax(const float *logits, int V, const int32_t *slot, size_t slot_stride,
+                         uint32_t *next) {
+  __shared__ ArgBest red[32];
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const float *row = logits + (slot ? (size_t)(*slot) * slot_stride : 0) + (size_t)r * V;
+  ArgBest b = {0.0f, -1};
+  for (int i = tid; i < V; i += blockDim.x) {
+    float v = row[i];
+    if (is_nan(v)) continue;
+    if (b.i < 0 || v > b.v) { b.v = v; b.i = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgBest c;
+    c.v = __shfl_xor_sync(FULL, b.v, o);
+    c.i = __shfl_xor_sync(FULL, b.i, o);
+    b = arg_comb(b, c);
+  }
+  if ((tid & 31) == 0) red[tid >> 5] = b;
+  __syncthreads();
+  if (tid == 0) {
+    ArgBest a = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) a = arg_comb(a, red[w]);
+    uint32_t idx = (a.i < 0 || is_nan(row[0])) ? 0u : (uint32_t)a.i;
+    next[r] = idx;
+  }
+}
+void launch_argmax(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
+                   uint32_t *next, cudaStream_t s) {
+  if (rows <= 0) return;
+  k_argmax<<<rows, 1024, 0, s>>>(logits, V, slot, slot_stride, next);
+}
+
+// ---- E23 pinned sampler (e23 patch, src/sampling.rs hunk :650-725) ----
+//
+// One CTA per row.  Element-wise steps run on all threads; the four
+// order-pinned folds (softmax denominator, nucleus cumulative sum,
+// renormalisation total, CDF walk) run in thread 0 over chunks that the
+// other threads stage into shared memory.  The (probability desc, index asc)
+// order is a stable LSD radix sort of key = ~bits(p) (p >= +0, so bit order
+// is value order) over ascending indices.
+constexpr int SAMPLE_THREADS = 1024;
+constexpr int FOLD_CHUNK = 1024;
+
+__device__ __forceinline__ uint64_t sm64_round(uint64_t x) {
+  uint64_t z = x + 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Serial fold driver: thread 0 calls op(i, value) for i = 0..n-1 in order,
+// op returns true to stop early.  Other threads stage the next chunk.
+template <class Load, class Op>
+__device__ void serial_fold(int n, Load load, Op op, float *buf, int *stop_flag) {
+  const int tid = threadIdx.x;
+  if (tid == 0) *stop_flag = 0;
+  for (int i = tid; i < FOLD_CHUNK && i < n; i += blockDim.x) buf[i] = load(i);
+  __syncthreads();
+  const int nch = (n + FOLD_CHUNK - 1) / FOLD_CHUNK;
+  for (int c = 0; c < nch; ++c) {
+    float *cur = buf + (c & 1) * FOLD_CHUNK;
+    float *nxt = buf + ((c + 1) & 1) * FOLD_CHUNK;
+    const int base = c * FOLD_CHUNK, cnt = min(FOLD_CHUNK, n - base);
+    if (tid == 0) {
+      if (!*stop_flag)
+        for (int i = 0; i < cnt; ++i)
+          if (op(base + i, cur[i])) { *stop_flag = 1; break; }
+    } else if (c + 1 < nch) {
+      const int nb = base + FOLD_CHUNK, ncnt = min(FOLD_CHUNK, n - nb);
+      for (int i = tid - 1; i < ncnt; i += blockDim.x - 1) nxt[i] = load(nb + i);
+    }
+    __syncthreads();
+    if (*stop_flag) break;
+  }
+}
+
+__global__ void __launch_bounds__(SAMPLE_THREADS)
+k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, float temperature,
+         float top_p, uint64_t seed, const int32_t *position, float *scratch, uint32_t *next) {
+  __shared__ float buf[2 * FOLD_CHUNK];
+  __shared__ int hist[256];
+  __shared__ int base[256];
+  __shared__ int wcnt[SAMPLE_THREADS / 32][256];
+  __shared__ float redf[32];
+  __shared__ float shared_f[4];
+  __shared__ int shared_i[4];
+  const int r = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const float *row = logits + (slot ? (size_t)(*slot) * slot_stride : 0) + (size_t)r * V;
+  float *p = scratch + (size_t)r * 5 * V;                   // probabilities
+  uint32_t *kA = reinterpret_cast<uint32_t *>(p + V), *vA = kA + V;
+  uint32_t *kB = vA + V, *vB = kB + V;
+
+  // Step 1-2: scale by temperature, max scan.
+  float m = bitsf(0x7fc00000u);
+  for (int i = tid; i < V; i += nt) {
+    float s = fdiv(row[i], temperature);
+    p[i] = s;
+    m = max_comb(m, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max_comb(m, __shfl_xor_sync(FULL, m, o));
+  if ((tid & 31) == 0) redf[tid >> 5] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float mm = redf[0];
+    for (int w = 1; w < nt / 32; ++w) mm = max_comb(mm, redf[w]);
+    if (is_nan(p[0])) mm = p[0];
+    shared_f[0] = mm;
+  }
+  __syncthreads();
+  const float mx = shared_f[0];
+  for (int i = tid; i < V; i += nt) p[i] = exp_pinned(fsub(p[i], mx));
+  __syncthreads();
+  // Step 2b: denominator, strict left-to-right over index order.
+  float den_acc = 0.0f;
+  serial_fold(V, [&](int i) { return p[i]; },
+              [&](int, float v) { den_acc = fadd(den_acc, v); return false; }, buf, &shared_i[0]);
+  if (tid == 0) shared_f[1] = den_acc;
+  __syncthreads();
+  const float den = shared_f[1];
+  for (int i = tid; i < V; i += nt) {
+    float pv = fdiv(p[i], den);
+    p[i] = pv;
+    kA[i] = ~__float_as_uint(pv);
+    vA[i] = (uint32_t)i;
+  }
+  __syncthreads();
+  // Step 3: stable LSD radix sort, 4 passes of 8 bits.
+  const int warp = tid >> 5, lane = tid & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  uint32_t *ki = kA, *vi = vA, *ko = kB, *vo = vB;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int sh = 8 * pass;
+    for (int d = tid; d < 256; d += nt) hist[d] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += nt) atomicAdd(&hist[(ki[i] >> sh) & 255], 1);
+    __syncthreads();
+    if (tid == 0) {
+      int run = 0;
+      for (int d = 0; d < 256; ++d) { base[d] = run; run += hist[d]; }
+    }
+    __syncthreads();
+    for (int t0 = 0; t0 < V; t0 += nt) {
+      for (int d = tid; d < (nt / 32) * 256; d += nt) (&wcnt[0][0])[d] = 0;
+      __syncthreads();
+      const int i = t0 + tid;
+      const bool valid = i < V;
+      uint32_t key = valid ? ki[i] : 0u, val = valid ? vi[i] : 0u;
+      int dg = valid ? (int)((key >> sh) & 255) : 256;
+      unsigned same = __match_any_sync(FULL, dg);
+      int rank = __popc(same & lt_mask);
+      if (valid && rank == 0) wcnt[warp][dg] = __popc(same);
+      __syncthreads();
+      // exclusive prefix over warps, per digit; then tile totals into base
+      if (tid < 256) {
+        int run = 0;
+        for (int w = 0; w < nt / 32; ++w) { int c = wcnt[w][tid]; wcnt[w][tid] = run; run += c; }
+        hist[tid] = run;  // tile total for digit tid
+      }
+      __syncthreads();
+      if (valid) {
+        int dst = base[dg] + wcnt[warp][dg] + rank;
+        ko[dst] = key;
+        vo[dst] = val;
+      }
+      __syncthreads();
+      if (tid < 256) base[tid] += hist[tid];
+      __syncthreads();
+    }
+    uint32_t *t;
+    t = ki; ki = ko; ko = t;
+    t = vi; vi = vo; vo = t;
+  }
+  // After 4 passes the sorted keys/indices are back in (kA, vA).
+  // Step 4: nucleus = shortest prefix with cumulative sum >= top_p.
+  float cum = 0.0f;
+  int nuc = V;
+  serial_fold(V, [&](int i) { return __uint_as_float(~ki[i]); },
+              [&](int i, float v) {
+                cum = fadd(cum, v);
+                if (cum >= top_p) { nuc = i + 1; return true; }
+                return false;
+              },
+              buf, &shared_i[0]);
+  if (tid == 0) shared_i[1] = nuc;
+  __syncthreads();
+  nuc = shared_i[1];
+  // Step 5: renormalisation total over the nucleus.
+  float total = 0.0f;
+  serial_fold(nuc, [&](int i) { return __uint_as_float(~ki[i]); },
+              [&](int, float v) { total = fadd(total, v); return false; }, buf, &shared_i[0]);
+  if (tid == 0) shared_f[2] = total;
+  __syncthreads();
+  total = shared_f[2];
+  // Step 6: draw u = (word >> 11) * 2^-53, walk the CDF.
+  const uint64_t pos64 = (uint64_t)(int64_t)position[r];
+  const uint64_t word = sm64_round(seed ^ sm64_round(pos64));
+  const double u = __dmul_rn((double)(word >> 11), 1.0 / 9007199254740992.0);
+  float cdf = 0.0f;
+  int pick = nuc - 1;
+  serial_fold(nuc, [&](int i) { return __uint_as_float(~ki[i]); },
+              [&](int i, float v) {
+                cdf = fadd(cdf, fdiv(v, total));
+                if ((double)cdf > u) { pick = i; return true; }
+                return false;
+              },
+              buf, &shared_i[0]);
+  if (tid == 0) next[r] = vi[pick];
+}
+
+void launch_sample(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
+                   float temperature, float top_p, uint64_t seed, const int32_t *position,
+                   float *scratch, uint32_t *next, cudaStream_t s) {
+  if (rows <= 0) return;
+  k_sample<<<rows, SAMPLE_THREADS, 0, s>>>(logits, V, slot, slot_stride, temperature, top_p, seed,
+                                           position, scratch, next);
+}
+
+// After token selection: record the token, advance the row's position and
+// the logits ring slot for the next step.
+__global__ void k_step_advance(const uint32_t *next, int rows, const int32_t *step, int gen,
+                               uint32_t *tokens_out, uint32_t *ids_hist, int32_t *pos,
+                               int32_t *sample_pos, int32_t *slot, int ring, int32_t *step_ctr) {
+  const int t = *step;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    tokens_out[(size_t)r * gen + t] = next[r];
+    ids_hist[(size_t)t * rows + r] = next[r];
+    pos[r] += 1;
+    if (sample_pos) sample_pos[r] += 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (slot) *slot = (t + 1) % ring;
+    if (step_ctr) *step_ctr = t + 1;
+  }
+}
+void launch_step_advance(const uint32_t *next, int rows, const int32_t *step, int gen,
+                         uint32_t *tokens_out, uint32_t *ids_hist, int32_t *pos, int32_t *sample_pos,
+                         int32_t *slot, int ring, int32_t *step_ctr, cudaStream_t s) {
+  // one block so that the counter update is ordered after every row's read
+  k_step_advance<<<1, 1024, 0, s>>>(next, rows, step, gen, tokens_out, ids_hist, pos, sample_pos,
+                                    slot, ring, step_ctr);
+}
+
+__global__ void k_gather_rows(const float *src, int ld, const int32_t *src_idx,
+                              const int32_t *dst_idx, int H, float *dst) {
+  int r = blockIdx.x;
+  const float *s = src + (size_t)src_idx[r] * ld;
+  float *d = dst + (size_t)dst_idx[r] * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) d[i] = s[i];
+}
+void launch_gather_rows(const float *src, int ld, const int32_t *src_idx, const int32_t *dst_idx,
+                        int n, int H, float *dst, cudaStream_t s) {
+  if (n <= 0) return;
+  k_gather_rows<<<n, 256, 0, s>>>(src, ld, src_idx, dst_idx, H, dst);
+}
+
+// ============================================================ witness SHA-256
+
+// Header / short input absorb: one thread per sequence, byte-serial.
+__global__ void k_sha_absorb_bytes(ShaState *st, const uint8_t *bytes, const uint32_t *offsets,
+                                   int n_seq) {
+  int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n_seq) return;
+  ShaState S = st[s];
+  uint32_t bn = S.carry_n;
+  const uint8_t *b = bytes + offsets[s];
+  uint32_t n = offsets[s + 1] - offsets[s];
+  for (uint32_t i = 0; i < n; ++i) sha_absorb_byte(S.h, S.carry, bn, b[i]);
+  S.carry_n = bn;
+  S.len += n;
+  st[s] = S;
+}
+void launch_sha_absorb_bytes(ShaState *st, const uint8_t *bytes, const uint32_t *offsets, int n_seq,
+                             cudaStream_t s) {
+  if (n_seq <= 0) return;
+  k_sha_absorb_bytes<<<(n_seq + 63) / 64, 64, 0, s>>>(st, bytes, offsets, n_seq);
+}
+
+// Step stream of one sequence = carry bytes || V logits (u32 LE) || next id.
+__device__ __forceinline__ uint32_t step_dword(const uint32_t *data, int nd, uint32_t id, int i) {
+  return i < nd ? data[i] : (i == nd ? id : 0u);
+}
+__device__ __forceinline__ uint8_t step_byte(const uint8_t *carry, int c, const uint32_t *data, int nd,
+                                             uint32_t id, int p) {
+  if (p < c) return carry[p];
+  int q = p - c;
+  return (uint8_t)(step_dword(data, nd, id, q >> 2) >> (8 * (q & 3)));
+}
+// Big-endian message word at stream byte offset p.
+__device__ __forceinline__ uint32_t step_word(const uint8_t *carry, int c, const uint32_t *data,
+                                              int nd, uint32_t id, int p) {
+  if (p >= c) {
+    int q = p - c;
+    if ((q & 3) == 0) return __byte_perm(step_dword(data, nd, id, q >> 2), 0, 0x0123);
+    if ((q & 3) == 2)
+      return __byte_perm(step_dword(data, nd, id, q >> 2), step_dword(data, nd, id, (q >> 2) + 1),
+                         0x2345);
+  }
+  uint32_t w = 0;
+  for (int b = 0; b < 4; ++b) w = (w << 8) | step_byte(carry, c, data, nd, id, p + b);
+  return w;
+}
+
+size_t sha_wk_words(int V, int n_seq) {
+  size_t nb_max = ((size_t)63 + 4 * (size_t)V + 4) / 64;
+  return nb_max * 64 * (size_t)n_seq;
+}
+
+// Expand W+K for every full block of this step.  Layout [block][16 quads][seq]
+// so the compression warp's 32 lanes read 512 contiguous bytes per quad.
+__global__ void k_sha_prep(const ShaState *st, int n_seq, const float *logits, int V,
+                           size_t row_stride, const uint32_t *next_ids, uint32_t *wk, int nb_max) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int s = (int)(idx % n_seq), j = (int)(idx / n_seq);
+  if (j >= nb_max) return;
+  const int c = (int)st[s].carry_n;
+  const int total = c + 4 * V + 4;
+  if (j >= total / 64) return;
+  const uint32_t *data = reinterpret_cast<const uint32_t *>(logits + (size_t)s * row_stride);
+  const uint32_t id = next_ids[s];
+  uint32_t m[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m[i] = step_word(st[s].carry, c, data, V, id, 64 * j + 4 * i);
+  uint32_t w[64];
+  sha_expand_wk(m, w);
+  uint4 *out = reinterpret_cast<uint4 *>(wk);
+#pragma unroll
+  for (int qd = 0; qd < 16; ++qd)
+    out[((size_t)j * 16 + qd) * n_seq + s] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
+}
+
+// The chain: one thread per sequence compresses the step's blocks in order,
+// keeps the tail as the new carry and emits the per-step digest (a
+// finalised copy of the running state).
+__global__ void __launch_bounds__(32)
+k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+               const uint32_t *next_ids, const uint32_t *wk, uint8_t *digest_out, size_t digest_stride) {
+  int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n_seq) return;
+  ShaState S = st[s];
+  const int c = (int)S.carry_n;
+  const int total = c + 4 * V + 4;
+  const int nb = total / 64;
+  const uint4 *in = reinterpret_cast<const uint4 *>(wk);
+  uint32_t h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = S.h[i];
+  uint4 cur[16];
+  if (nb > 0) {
+#pragma unroll
+    for (int qd = 0; qd < 16; ++qd) cur[qd] = in[(size_t)qd * n_seq + s];
+  }
+  for (int j = 0; j < nb; ++j) {
+    uint4 nxt[16];
+    if (j + 1 < nb) {
+#pragma unroll
+      for (int qd = 0; qd < 16; ++qd) nxt[qd] = in[((size_t)(j + 1) * 16 + qd) * n_seq + s];
+    }
+    uint32_t w[64];
+#pragma unroll
+    for (int qd = 0; qd < 16; ++qd) {
+      w[4 * qd] = cur[qd].x; w[4 * qd + 1] = cur[qd].y; w[4 * qd + 2] = cur[qd].z; w[4 * qd + 3] = cur[qd].w;
+    }
+    sha_compress_wk(h, w);
+    if (j + 1 < nb) {
+#pragma unroll
+      for (int qd = 0; qd < 16; ++qd) cur[qd] = nxt[qd];
+    }
+  }
+  // New carry = stream bytes [64*nb, total).
+  const uint32_t *data = reinterpret_cast<const uint32_t *>(logits + (size_t)s * row_stride);
+  const uint32_t id = next_ids[s];
+  uint8_t nc[64];
+  const int cn = total - 64 * nb;
+  for (int b = 0; b < cn; ++b) nc[b] = step_byte(S.carry, c, data, V, id, 64 * nb + b);
+  for (int b = 0; b < cn; ++b) S.carry[b] = nc[b];
+  S.carry_n = (uint32_t)cn;
+  S.len += (uint64_t)4 * V + 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) S.h[i] = h[i];
+  st[s] = S;
+  if (digest_out) {
+    uint8_t d[32];
+    sha_final_copy(S.h, S.len, S.carry, S.carry_n, d);
+    for (int i = 0; i < 32; ++i) digest_out[(size_t)s * digest_stride + i] = d[i];
+  }
+}
+
+void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                     const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,
+                     size_t digest_stride, cudaStream_t s) {
+  if (n_seq <= 0) return;
+  int nb_max = (int)((63 + 4 * (size_t)V + 4) / 64);
+  size_t threads = (size_t)nb_max * n_seq;
+  k_sha_prep<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(st, n_seq, logits, V, row_stride,
+                                                              next_ids, wk_scratch, nb_max);
+  k_sha_compress<<<(n_seq + 31) / 32, 32, 0, s>>>(st, n_seq, logits, V, row_stride, next_ids,
+                                                  wk_scratch, step_digest_out, digest_stride);
+}
+
+__global__ void k_sha_finalize(const ShaState *st, int n_seq, uint8_t *out) {
+  int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n_seq) return;
+  uint8_t d[32];
+  sha_final_copy(st[s].h, st[s].len, st[s].carry, st[s].carry_n, d);
+  for (int i = 0; i < 32; ++i) out[(size_t)s * 32 + i] = d[i];
+}
+void launch_sha_finalize(const ShaState *st, int n_seq, uint8_t *out, cudaStream_t s) {
+  if (n_seq <= 0) return;
+  k_sha_finalize<<<(n_seq + 63) / 64, 64, 0, s>>>(st, n_seq, out);
+}
+
+__global__ void k_sha_ids(const uint32_t *prompt_flat, const uint32_t *prompt_off,
+                          const uint32_t *prompt_len, const uint32_t *gen_tokens, int gen, int n_seq,
+                          uint8_t *out) {
+  int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n_seq) return;
+  uint32_t h[8];
+  sha_init(h);
+  uint8_t buf[64];
+  uint32_t bn = 0;
+  uint64_t len = 0;
+  auto put = [&](uint32_t v) {
+    for (int b = 0; b < 4; ++b) sha_absorb_byte(h, buf, bn, (uint8_t)(v >> (8 * b)));
+    len += 4;
+  };
+  for (uint32_t i = 0; i < prompt_len[s]; ++i) put(prompt_flat[prompt_off[s] + i]);
+  for (int t = 0; t < gen; ++t) put(gen_tokens[(size_t)s * gen + t]);
+  uint8_t d[32];
+  sha_final_copy(h, len, buf, bn, d);
+  for (int i = 0; i < 32; ++i) out[(size_t)s * 32 + i] = d[i];
+}
+void launch_sha_ids(const uint32_t *prompt_flat, const uint32_t *prompt_off, const uint32_t *prompt_len,
+                    const uint32_t *gen_tokens, int gen, int n_seq, uint8_t *out, cudaStream_t s) {
+  if (n_seq <= 0) return;
+  k_sha_ids<<<(n_seq + 63) / 64, 64, 0, s>>>(prompt_flat, prompt_off, prompt_len, gen_tokens, gen,
+                                             n_seq, out);
+}
+
+}  // namespace cis2b

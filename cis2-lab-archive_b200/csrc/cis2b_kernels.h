@@ -1,0 +1,78 @@
+// cis2b_kernels.h -- host-side launchers for the sm_100a kernels of the
+// CIS-2 decode path (implemented in cis2b_kernels.cu).  Internal interface
+// between the runtime (cis2b_runtime.cu) and the kernels; not exported.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace cis2b {
+
+struct ShaState;  // cis2b_sha256.cuh
+
+// Where one activation row of a batch lives: sequence index and position.
+struct RowMap {
+  const int32_t *seq;  // [rows]
+  const int32_t *pos;  // [rows]
+};
+
+// Pinned RoPE / inv_freq tables (built once per model).
+void launch_inv_freq(float rope_theta_f32, int head_dim, float *inv_freq, cudaStream_t s);
+void launch_rope_table(const float *inv_freq, int half, int max_pos, float *cos_t, float *sin_t,
+                       cudaStream_t s);
+
+void launch_embed(const uint16_t *E, int H, const uint32_t *tokens, int rows, float *h,
+                  cudaStream_t s);
+void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
+                    float *out, int ldo, cudaStream_t s);
+
+// Y[m][n] (+)= sum_k W[n][k] X[m][k] in the pinned order.  W bf16 [N][K] row
+// major (K % 8 == 0), X fp32 [M][ldx].  If resid != nullptr, Y = resid + dot.
+// If y_slot != nullptr, Y is offset by (*y_slot) * y_slot_stride floats.
+void launch_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
+                 const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
+                 cudaStream_t s);
+
+// q/k norm (optional), RoPE of q and k, and the KV-cache append.
+// qkv rows: [q (n_heads*hd) | k (n_kv*hd) | v (n_kv*hd)].  Caches are laid
+// out [seq][max_pos][kv_dim] for ONE layer (the caller offsets by layer).
+void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
+                     const uint16_t *q_norm, const uint16_t *k_norm, float eps, bool tree,
+                     const float *cos_t, const float *sin_t, float *kcache, float *vcache,
+                     int max_pos, cudaStream_t s);
+void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
+                      const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
+                      int ld_att, int max_len, cudaStream_t s);
+void launch_silu_mul(const float *gu, int I, int rows, float *hid, cudaStream_t s);
+void launch_add_bias(float *x, int ld, int rows, const uint16_t *b, int n, cudaStream_t s);
+
+// Token selection.  logits rows at logits + slot*slot_stride (slot from device).
+void launch_argmax(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
+                   uint32_t *next, cudaStream_t s);
+void launch_sample(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
+                   float temperature, float top_p, uint64_t seed, const int32_t *position,
+                   float *scratch, uint32_t *next, cudaStream_t s);
+// Record the chosen ids (tokens_out[r][step], ids_hist[step][r]), advance positions, ring slot, step.
+void launch_step_advance(const uint32_t *next, int rows, const int32_t *step, int gen,
+                         uint32_t *tokens_out, uint32_t *ids_hist, int32_t *pos, int32_t *sample_pos,
+                         int32_t *slot, int ring, int32_t *step_ctr, cudaStream_t s);
+// dst[dst_idx[r]][:H] = src[src_idx[r]][:H], r < n
+void launch_gather_rows(const float *src, int ld, const int32_t *src_idx, const int32_t *dst_idx,
+                        int n, int H, float *dst, cudaStream_t s);
+
+// Witness.
+void launch_sha_absorb_bytes(ShaState *st, const uint8_t *bytes, const uint32_t *offsets, int n_seq,
+                             cudaStream_t s);
+size_t sha_wk_words(int V, int n_seq);
+void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                     const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,
+                     size_t digest_stride, cudaStream_t s);
+void launch_sha_finalize(const ShaState *st, int n_seq, uint8_t *out, cudaStream_t s);
+// Argmax digest: SHA-256 over prompt ids then generated ids (u32 LE).
+void launch_sha_ids(const uint32_t *prompt_flat, const uint32_t *prompt_off, const uint32_t *prompt_len,
+                    const uint32_t *gen_tokens, int gen, int n_seq, uint8_t *out, cudaStream_t s);
+
+// Element-wise pinned function map (test entry point).
+void launch_pinned_map(int fn, const float *x, float *y, size_t n, cudaStream_t s);
+
+}  // namespace cis2b

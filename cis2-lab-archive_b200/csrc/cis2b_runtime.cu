@@ -1,0 +1,845 @@
+// cis2b_runtime.cu -- host runtime behind the C ABI (include/cis2b.h).
+//
+// Load: artifact hashes, config (code/cis2-fp/gpu/cis2_host.cpp:87-117 and
+// qwen3-port.diff:109-110), bf16 weights uploaded as-is into one device
+// arena (the exact widen happens inside the kernels), pinned inv_freq and
+// RoPE tables built on the device.
+//
+// Generate: all sequences of a call run as one batch.  Prompt positions go
+// through the model position-batched (each row's arithmetic is identical to
+// a per-token run, code/cis2-fp/verify3/model.h:128-139); then one decode
+// step per token: select (argmax or E23 sampler) -> witness absorb on a
+// second, high-priority stream -> forward of the chosen tokens.  The
+// witness of step t only needs step t's logits, so it lags the forward and
+// overlaps it; logits live in a ring sized to the step count where memory
+// allows, otherwise the forward waits for the witness to free a slot.
+#include "../../include/cis2b.h"
+#include "cis2b_host.h"
+#include "cis2b_kernels.h"
+#include "cis2b_pinned.cuh"
+#include "cis2b_sha256.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+using namespace cis2b;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+
+#define CU(x)                                                                               \
+  do {                                                                                      \
+    cudaError_t e_ = (x);                                                                   \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(CIS2B_ERR_CUDA, std::string(#x) + " -> " + cudaGetErrorString(e_));        \
+  } while (0)
+
+// Kernel launches report errors asynchronously; check after each batch.
+#define CU_LAUNCHED()                                                                       \
+  do {                                                                                      \
+    cudaError_t e_ = cudaGetLastError();                                                    \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(CIS2B_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+struct DevBuf {
+  void *p = nullptr;
+  size_t bytes = 0;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  cudaError_t ensure(size_t want) {
+    if (want <= bytes && p) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&p, want ? want : 16);
+    if (e == cudaSuccess) bytes = want;
+    return e;
+  }
+  template <class T> T *as() const { return reinterpret_cast<T *>(p); }
+};
+
+struct LayerW {
+  const uint16_t *in_norm, *post_norm, *wqkv, *wo, *wgu, *wdown;
+  const uint16_t *q_norm, *k_norm, *q_bias, *k_bias, *v_bias;
+};
+
+constexpr int PREFILL_CHUNK = 8192;            // rows per prefill pass
+constexpr size_t RING_BUDGET = 8ull << 30;     // bytes of logits kept for the witness
+
+}  // namespace
+
+struct cis2b_model {
+  int dev = 0;
+  cis2b_info info{};
+  bool tree = false;
+  int H = 0, I = 0, L = 0, NH = 0, NKV = 0, HD = 0, V = 0, QD = 0, KVD = 0, max_pos = 0;
+  float eps = 0.f;
+  std::vector<LayerW> layers;
+  const uint16_t *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
+  DevBuf arena;  // all weights
+  DevBuf inv_freq, cos_t, sin_t;
+  cudaStream_t s_main = nullptr, s_sha = nullptr;
+  // workspace
+  DevBuf h, ln, qkv, att, gu, hid, hlast, lnlast, kc, vc, ring, scratch;
+  DevBuf rows_seq, rows_pos, rows_tok, gsrc, gdst;
+  DevBuf d_next, d_pos, d_spos, d_seq, d_ctl, d_tokens, d_ids_hist;
+  DevBuf sha_state, sha_wk, step_dig, d_witness, d_argmax;
+  DevBuf hdr_bytes, hdr_off, p_flat, p_off, p_len;
+  std::vector<cudaEvent_t> ev_sha;
+  cudaEvent_t ev_sel = nullptr, ev0 = nullptr, ev_pref = nullptr, ev_dec = nullptr, ev_end = nullptr;
+  cis2b_timing timing{};
+  int64_t launches = 0;
+};
+
+namespace {
+
+const char *kSlotNames[] = {"input_layernorm.weight", "post_attention_layernorm.weight"};
+
+struct TensorRef {
+  size_t begin = 0, end = 0;
+  std::vector<size_t> shape;
+  std::string dtype;
+};
+
+// ------------------------------------------------------------------ loading
+int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
+  if (!dir_c) return fail(CIS2B_ERR_ARG, "weights_dir is NULL");
+  cis2b_opts o{};
+  if (opts) o = *opts;
+  for (int i = 0; i < 5; ++i)
+    if (o.reserved[i] != 0) return fail(CIS2B_ERR_ARG, "cis2b_opts.reserved must be zero");
+  if (o.reduction != CIS2B_REDUCTION_SEQUENTIAL && o.reduction != CIS2B_REDUCTION_TREE)
+    return fail(CIS2B_ERR_ARG, "unknown reduction mode");
+  if (o.max_positions < 0) return fail(CIS2B_ERR_ARG, "max_positions < 0");
+  m->dev = o.device;
+  m->tree = o.reduction == CIS2B_REDUCTION_TREE;
+  m->max_pos = o.max_positions ? o.max_positions : 4096;
+
+  // Everything up to the upload is host work, so artifact and config errors
+  // are reported the same way with or without a device.
+  const std::string dir(dir_c);
+  std::string wbytes, tok, cfgtxt;
+  if (!read_file(dir + "/model.safetensors", wbytes))
+    return fail(CIS2B_ERR_IO, "cannot read " + dir + "/model.safetensors");
+  if (!read_file(dir + "/tokenizer.json", tok)) return fail(CIS2B_ERR_IO, "cannot read " + dir + "/tokenizer.json");
+  if (!read_file(dir + "/config.json", cfgtxt)) return fail(CIS2B_ERR_IO, "cannot read " + dir + "/config.json");
+  {
+    Sha256 a, b, c;
+    a.update(wbytes.data(), wbytes.size());
+    a.final(m->info.weights_sha256);
+    b.update(tok.data(), tok.size());
+    b.final(m->info.tokenizer_sha256);
+    c.update(cfgtxt.data(), cfgtxt.size());
+    c.final(m->info.config_sha256);
+  }
+
+  // ---- config (cis2_host.cpp:97-117, qwen3-port.diff:109-110)
+  Json cfg;
+  std::string jerr;
+  if (!JsonParser(cfgtxt.data(), cfgtxt.data() + cfgtxt.size()).parse(cfg, jerr) || cfg.kind != Json::OBJ)
+    return fail(CIS2B_ERR_IO, "config.json: " + (jerr.empty() ? std::string("not an object") : jerr));
+  auto need = [&](const char *k, double &v) -> bool {
+    const Json *j = cfg.get(k);
+    if (!j || j->kind != Json::NUM) return false;
+    v = j->num;
+    return true;
+  };
+  double hid, inter, nl, nh, nkv, voc, eps, theta;
+  if (!need("hidden_size", hid) || !need("intermediate_size", inter) || !need("num_hidden_layers", nl) ||
+      !need("num_attention_heads", nh) || !need("num_key_value_heads", nkv) || !need("vocab_size", voc) ||
+      !need("rms_norm_eps", eps) || !need("rope_theta", theta))
+    return fail(CIS2B_ERR_CONFIG, "config.json lacks a required numeric key");
+  m->H = (int)hid; m->I = (int)inter; m->L = (int)nl; m->NH = (int)nh; m->NKV = (int)nkv; m->V = (int)voc;
+  m->eps = (float)eps;
+  if (m->NH <= 0 || m->NKV <= 0 || m->H <= 0 || m->I <= 0 || m->L <= 0 || m->V <= 0)
+    return fail(CIS2B_ERR_CONFIG, "non-positive model dimension");
+  m->HD = m->H / m->NH;
+  if (const Json *j = cfg.get("head_dim"); j && j->kind == Json::NUM) m->HD = (int)j->num;
+  bool tied = true;
+  if (const Json *j = cfg.get("tie_word_embeddings")) tied = (j->kind == Json::BOOL) ? j->b : true;
+  if (const Json *j = cfg.get("rope_scaling"); j && j->kind != Json::NUL)
+    return fail(CIS2B_ERR_CONFIG, "rope_scaling is not part of the CIS-2 arithmetic");
+  m->QD = m->NH * m->HD;
+  m->KVD = m->NKV * m->HD;
+  if (m->NH % m->NKV) return fail(CIS2B_ERR_CONFIG, "num_attention_heads % num_key_value_heads != 0");
+  if (m->HD <= 0 || m->HD % 2) return fail(CIS2B_ERR_CONFIG, "head_dim must be even and positive");
+  if (m->H % 8 || m->QD % 8 || m->I % 8)
+    return fail(CIS2B_ERR_CONFIG, "hidden, q_dim and intermediate sizes must be multiples of 8");
+  m->info.hidden = m->H; m->info.intermediate = m->I; m->info.n_layers = m->L;
+  m->info.n_heads = m->NH; m->info.n_kv_heads = m->NKV; m->info.head_dim = m->HD;
+  m->info.vocab = m->V; m->info.tied = tied ? 1 : 0; m->info.rms_norm_eps = m->eps;
+  m->info.rope_theta = theta; m->info.reduction = o.reduction; m->info.max_positions = m->max_pos;
+
+  // ---- safetensors index (cis2_model.h:296-326)
+  if (wbytes.size() < 8) return fail(CIS2B_ERR_IO, "safetensors too short");
+  uint64_t hlen = 0;
+  for (int i = 0; i < 8; ++i) hlen |= (uint64_t)(uint8_t)wbytes[i] << (8 * i);
+  if (8 + hlen > wbytes.size()) return fail(CIS2B_ERR_IO, "safetensors header length out of range");
+  Json hdr;
+  if (!JsonParser(wbytes.data() + 8, wbytes.data() + 8 + hlen).parse(hdr, jerr) || hdr.kind != Json::OBJ)
+    return fail(CIS2B_ERR_IO, "safetensors header: " + jerr);
+  const size_t data0 = 8 + hlen, data_len = wbytes.size() - data0;
+  auto find = [&](const std::string &name, TensorRef &t) -> bool {
+    const Json *j = hdr.get(name.c_str());
+    if (!j) return false;
+    const Json *dt = j->get("dtype"), *sh = j->get("shape"), *of = j->get("data_offsets");
+    if (!dt || !sh || !of || of->arr.size() != 2) return false;
+    t.dtype = dt->str;
+    t.shape.clear();
+    for (auto &x : sh->arr) t.shape.push_back((size_t)x.num);
+    t.begin = (size_t)of->arr[0].num;
+    t.end = (size_t)of->arr[1].num;
+    return true;
+  };
+  struct Piece { size_t dst_off; const uint8_t *src; size_t bytes; };
+  std::vector<Piece> pieces;
+  size_t arena_bytes = 0;
+  auto reserve = [&](size_t bytes) {
+    size_t off = arena_bytes;
+    arena_bytes += (bytes + 255) & ~(size_t)255;
+    return off;
+  };
+  std::string err;
+  // Adds tensor `name` of `shape` at byte offset `dst` within a reserved region.
+  auto take = [&](const std::string &name, std::vector<size_t> shape, size_t dst, bool optional,
+                  bool &present) -> bool {
+    TensorRef t;
+    present = find(name, t);
+    if (!present) {
+      if (!optional) err = "tensor " + name + " missing";
+      return optional;
+    }
+    if (t.dtype != "BF16") { err = "tensor " + name + " dtype " + t.dtype + ", expected BF16"; return false; }
+    if (t.shape != shape) { err = "tensor " + name + " shape mismatch"; return false; }
+    size_t n = 1;
+    for (size_t d : shape) n *= d;
+    if (t.end < t.begin || t.end > data_len || t.end - t.begin != 2 * n) {
+      err = "tensor " + name + " byte range invalid";
+      return false;
+    }
+    pieces.push_back({dst, (const uint8_t *)wbytes.data() + data0 + t.begin, 2 * n});
+    return true;
+  };
+  const size_t H = m->H, I = m->I, QD = m->QD, KVD = m->KVD, V = m->V, HD = m->HD;
+  bool pr;
+  size_t off_embed = reserve(2 * V * H);
+  if (!take("model.embed_tokens.weight", {V, H}, off_embed, false, pr)) return fail(CIS2B_ERR_IO, err);
+  size_t off_norm = reserve(2 * H);
+  if (!take("model.norm.weight", {H}, off_norm, false, pr)) return fail(CIS2B_ERR_IO, err);
+  size_t off_lm = 0;
+  if (!tied) {
+    off_lm = reserve(2 * V * H);
+    if (!take("lm_head.weight", {V, H}, off_lm, false, pr)) return fail(CIS2B_ERR_IO, err);
+  }
+  struct LOff { size_t in, post, qkv, o, gu, down, qn, kn, qb, kb, vb; bool hqn, hkn, hqb, hkb, hvb; };
+  std::vector<LOff> lo((size_t)m->L);
+  for (int l = 0; l < m->L; ++l) {
+    char pfx[64];
+    snprintf(pfx, sizeof pfx, "model.layers.%d.", l);
+    std::string p(pfx);
+    LOff &x = lo[(size_t)l];
+    x.in = reserve(2 * H);
+    x.post = reserve(2 * H);
+    x.qkv = reserve(2 * (QD + 2 * KVD) * H);
+    x.o = reserve(2 * H * QD);
+    x.gu = reserve(2 * 2 * I * H);
+    x.down = reserve(2 * H * I);
+    x.qn = reserve(2 * HD);
+    x.kn = reserve(2 * HD);
+    x.qb = reserve(2 * QD);
+    x.kb = reserve(2 * KVD);
+    x.vb = reserve(2 * KVD);
+    if (!take(p + kSlotNames[0], {H}, x.in, false, pr) || !take(p + kSlotNames[1], {H}, x.post, false, pr) ||
+        !take(p + "self_attn.q_proj.weight", {QD, H}, x.qkv, false, pr) ||
+        !take(p + "self_attn.k_proj.weight", {KVD, H}, x.qkv + 2 * QD * H, false, pr) ||
+        !take(p + "self_attn.v_proj.weight", {KVD, H}, x.qkv + 2 * (QD + KVD) * H, false, pr) ||
+        !take(p + "self_attn.o_proj.weight", {H, QD}, x.o, false, pr) ||
+        !take(p + "mlp.gate_proj.weight", {I, H}, x.gu, false, pr) ||
+        !take(p + "mlp.up_proj.weight", {I, H}, x.gu + 2 * I * H, false, pr) ||
+        !take(p + "mlp.down_proj.weight", {H, I}, x.down, false, pr) ||
+        !take(p + "self_attn.q_norm.weight", {HD}, x.qn, true, x.hqn) ||
+        !take(p + "self_attn.k_norm.weight", {HD}, x.kn, true, x.hkn) ||
+        !take(p + "self_attn.q_proj.bias", {QD}, x.qb, true, x.hqb) ||
+        !take(p + "self_attn.k_proj.bias", {KVD}, x.kb, true, x.hkb) ||
+        !take(p + "self_attn.v_proj.bias", {KVD}, x.vb, true, x.hvb))
+      return fail(CIS2B_ERR_IO, err);
+  }
+  CU(cudaSetDevice(m->dev));
+  CU(cudaStreamCreateWithFlags(&m->s_main, cudaStreamNonBlocking));
+  int lo_pri = 0, hi_pri = 0;
+  CU(cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri));
+  CU(cudaStreamCreateWithPriority(&m->s_sha, cudaStreamNonBlocking, hi_pri));
+  if (m->arena.ensure(arena_bytes) != cudaSuccess)
+    return fail(CIS2B_ERR_NOMEM, "device allocation of the weight arena failed");
+  uint8_t *base = m->arena.as<uint8_t>();
+  for (const Piece &pc : pieces) CU(cudaMemcpy(base + pc.dst_off, pc.src, pc.bytes, cudaMemcpyHostToDevice));
+  auto at = [&](size_t off) { return reinterpret_cast<const uint16_t *>(base + off); };
+  m->embed = at(off_embed);
+  m->final_norm = at(off_norm);
+  m->lm_head = tied ? m->embed : at(off_lm);
+  m->layers.resize((size_t)m->L);
+  for (int l = 0; l < m->L; ++l) {
+    const LOff &x = lo[(size_t)l];
+    LayerW &w = m->layers[(size_t)l];
+    w.in_norm = at(x.in); w.post_norm = at(x.post); w.wqkv = at(x.qkv); w.wo = at(x.o);
+    w.wgu = at(x.gu); w.wdown = at(x.down);
+    w.q_norm = x.hqn ? at(x.qn) : nullptr; w.k_norm = x.hkn ? at(x.kn) : nullptr;
+    w.q_bias = x.hqb ? at(x.qb) : nullptr; w.k_bias = x.hkb ? at(x.kb) : nullptr;
+    w.v_bias = x.hvb ? at(x.vb) : nullptr;
+  }
+  wbytes.clear();
+  wbytes.shrink_to_fit();
+
+  // ---- pinned tables on the device (cis2_model.h:456-476, 547-568)
+  const int half = m->HD / 2;
+  if (m->inv_freq.ensure(sizeof(float) * half) != cudaSuccess ||
+      m->cos_t.ensure(sizeof(float) * half * (size_t)m->max_pos) != cudaSuccess ||
+      m->sin_t.ensure(sizeof(float) * half * (size_t)m->max_pos) != cudaSuccess)
+    return fail(CIS2B_ERR_NOMEM, "device allocation of the RoPE tables failed");
+  launch_inv_freq((float)theta, m->HD, m->inv_freq.as<float>(), m->s_main);
+  launch_rope_table(m->inv_freq.as<float>(), half, m->max_pos, m->cos_t.as<float>(), m->sin_t.as<float>(),
+                    m->s_main);
+  CU_LAUNCHED();
+  std::vector<float> invf((size_t)half);
+  CU(cudaMemcpyAsync(invf.data(), m->inv_freq.p, sizeof(float) * half, cudaMemcpyDeviceToHost, m->s_main));
+  CU(cudaStreamSynchronize(m->s_main));
+  {
+    Sha256 s;
+    for (float f : invf) { uint32_t u; memcpy(&u, &f, 4); s.u32le(u); }
+    s.final(m->info.inv_freq_table_digest);
+  }
+  {
+    // §6.6 table digest: the coefficient bit patterns in declared order
+    // (cis2_model.h:414-450), the same constants the kernels use.
+    Sha256 s;
+    const uint32_t a[] = {EXP_LOG2E, EXP_C1, EXP_C2, EXP_P0, EXP_P1, EXP_P2, EXP_P3, EXP_P4, EXP_P5};
+    for (uint32_t u : a) s.u32le(u);
+    uint8_t le[8];
+    for (int i = 0; i < 8; ++i) le[i] = (uint8_t)(PI_2_F64 >> (8 * i));
+    s.update(le, 8);
+    const uint32_t b[] = {SIN_C0, SIN_C1, SIN_C2, COS_C0, COS_C1, COS_C2, LOG_SQRTHF, LOG_Q1, LOG_Q2,
+                          LOG_P0, LOG_P1, LOG_P2, LOG_P3, LOG_P4, LOG_P5, LOG_P6, LOG_P7, LOG_P8};
+    for (uint32_t u : b) s.u32le(u);
+    s.final(m->info.table_digest);
+  }
+  CU(cudaEventCreate(&m->ev_sel, cudaEventDisableTiming));
+  CU(cudaEventCreate(&m->ev0));
+  CU(cudaEventCreate(&m->ev_pref));
+  CU(cudaEventCreate(&m->ev_dec));
+  CU(cudaEventCreate(&m->ev_end));
+  return CIS2B_OK;
+}
+
+// ------------------------------------------------------------------ forward
+// Runs `rows` activation rows (token ids, sequence index and position per
+// row, all on the device) through every layer.  Leaves the final hidden
+// state in m->h.  kv caches are [layer][seq][maxP][kvd].
+int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *seq,
+                 const int32_t *pos, int n_seq_cache, int maxP) {
+  cudaStream_t s = m->s_main;
+  const int H = m->H, I = m->I, QD = m->QD, KVD = m->KVD, NQKV = QD + 2 * KVD;
+  float *h = m->h.as<float>(), *ln = m->ln.as<float>(), *qkv = m->qkv.as<float>();
+  float *att = m->att.as<float>(), *gu = m->gu.as<float>(), *hid = m->hid.as<float>();
+  const size_t layer_kv = (size_t)n_seq_cache * maxP * KVD;
+  RowMap rm{seq, pos};
+  launch_embed(m->embed, H, tok, rows, h, s);
+  m->launches += 1;
+  for (int l = 0; l < m->L; ++l) {
+    const LayerW &w = m->layers[(size_t)l];
+    float *kc = m->kc.as<float>() + (size_t)l * layer_kv;
+    float *vc = m->vc.as<float>() + (size_t)l * layer_kv;
+    launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, H, s);
+    launch_gemm(ln, H, w.wqkv, H, NQKV, rows, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s);
+    m->launches += 2;
+    if (w.q_bias) { launch_add_bias(qkv, NQKV, rows, w.q_bias, QD, s); m->launches++; }
+    if (w.k_bias) { launch_add_bias(qkv + QD, NQKV, rows, w.k_bias, KVD, s); m->launches++; }
+    if (w.v_bias) { launch_add_bias(qkv + QD + KVD, NQKV, rows, w.v_bias, KVD, s); m->launches++; }
+    launch_qkv_post(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, w.q_norm, w.k_norm, m->eps, m->tree,
+                    m->cos_t.as<float>(), m->sin_t.as<float>(), kc, vc, maxP, s);
+    launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, QD, maxP, s);
+    launch_gemm(att, QD, w.wo, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s);
+    launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, H, s);
+    launch_gemm(ln, H, w.wgu, H, 2 * I, rows, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s);
+    launch_silu_mul(gu, I, rows, hid, s);
+    launch_gemm(hid, I, w.wdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s);
+    m->launches += 7;
+  }
+  CU_LAUNCHED();
+  return CIS2B_OK;
+}
+
+// Final norm + lm_head of `rows` hidden rows -> Y (rows x V).
+int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_t *y_slot,
+              size_t slot_stride) {
+  cudaStream_t s = m->s_main;
+  launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(), m->H, s);
+  launch_gemm(m->lnlast.as<float>(), m->H, m->lm_head, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
+              y_slot, slot_stride, s);
+  m->launches += 2;
+  CU_LAUNCHED();
+  return CIS2B_OK;
+}
+
+int ensure_act(cis2b_model *m, int rows) {
+  const size_t r = (size_t)std::max(rows, 1);
+  const size_t H = m->H, I = m->I, QD = m->QD, KVD = m->KVD;
+  if (m->h.ensure(4 * r * H) || m->ln.ensure(4 * r * H) || m->qkv.ensure(4 * r * (QD + 2 * KVD)) ||
+      m->att.ensure(4 * r * QD) || m->gu.ensure(4 * r * 2 * I) || m->hid.ensure(4 * r * I))
+    return fail(CIS2B_ERR_NOMEM, "device allocation of activations failed");
+  return CIS2B_OK;
+}
+
+// Position-batched pass over prompt rows.  rows_* are host arrays (row order
+// must list each sequence's positions ascending).  For out_rows[i] >= 0,
+// the final hidden state of row out_src[i] lands in hlast row out_dst[i].
+int prefill(cis2b_model *m, const std::vector<uint32_t> &tok, const std::vector<int32_t> &seq,
+            const std::vector<int32_t> &pos, const std::vector<int32_t> &out_src,
+            const std::vector<int32_t> &out_dst, int n_seq_cache, int maxP) {
+  const int total = (int)tok.size();
+  const int chunk = std::min(total, PREFILL_CHUNK);
+  int rc = ensure_act(m, chunk);
+  if (rc) return rc;
+  if (m->rows_tok.ensure(4 * (size_t)total) || m->rows_seq.ensure(4 * (size_t)total) ||
+      m->rows_pos.ensure(4 * (size_t)total) || m->gsrc.ensure(4 * out_src.size() + 4) ||
+      m->gdst.ensure(4 * out_dst.size() + 4))
+    return fail(CIS2B_ERR_NOMEM, "device allocation of row maps failed");
+  cudaStream_t s = m->s_main;
+  CU(cudaMemcpyAsync(m->rows_tok.p, tok.data(), 4 * (size_t)total, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->rows_seq.p, seq.data(), 4 * (size_t)total, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->rows_pos.p, pos.data(), 4 * (size_t)total, cudaMemcpyHostToDevice, s));
+  // Per chunk gather lists, uploaded once (host memory must stay valid until
+  // the copies run, so stage everything before the first launch).
+  std::vector<int32_t> gs, gd;
+  std::vector<std::pair<int, int>> ranges;  // [first, count) into gs/gd per chunk
+  for (int c0 = 0; c0 < total; c0 += chunk) {
+    int first = (int)gs.size();
+    for (size_t i = 0; i < out_src.size(); ++i)
+      if (out_src[i] >= c0 && out_src[i] < c0 + chunk) {
+        gs.push_back(out_src[i] - c0);
+        gd.push_back(out_dst[i]);
+      }
+    ranges.push_back({first, (int)gs.size() - first});
+  }
+  if (!gs.empty()) {
+    CU(cudaMemcpyAsync(m->gsrc.p, gs.data(), 4 * gs.size(), cudaMemcpyHostToDevice, s));
+    CU(cudaMemcpyAsync(m->gdst.p, gd.data(), 4 * gd.size(), cudaMemcpyHostToDevice, s));
+  }
+  int ci = 0;
+  for (int c0 = 0; c0 < total; c0 += chunk, ++ci) {
+    const int n = std::min(chunk, total - c0);
+    rc = forward_rows(m, n, m->rows_tok.as<uint32_t>() + c0, m->rows_seq.as<int32_t>() + c0,
+                      m->rows_pos.as<int32_t>() + c0, n_seq_cache, maxP);
+    if (rc) return rc;
+    const auto &rg = ranges[(size_t)ci];
+    if (rg.second) {
+      launch_gather_rows(m->h.as<float>(), m->H, m->gsrc.as<int32_t>() + rg.first,
+                         m->gdst.as<int32_t>() + rg.first, rg.second, m->H, m->hlast.as<float>(), s);
+      m->launches++;
+    }
+  }
+  // The host vectors above are read by the async copies; make sure they ran.
+  CU(cudaStreamSynchronize(s));
+  CU_LAUNCHED();
+  return CIS2B_OK;
+}
+
+int alloc_cache(cis2b_model *m, int n_seq, int maxP) {
+  size_t kv = (size_t)m->L * n_seq * maxP * m->KVD * sizeof(float);
+  if (m->kc.ensure(kv) || m->vc.ensure(kv))
+    return fail(CIS2B_ERR_NOMEM, "device allocation of the KV cache failed (" + std::to_string(kv >> 20) + " MiB each)");
+  return CIS2B_OK;
+}
+
+int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *prompt_lens,
+                  uint32_t n_seq, uint32_t gen, const cis2b_sample *sample, uint32_t *out_tokens,
+                  uint8_t *out_steps, uint8_t *out_witness, uint8_t *out_argmax) {
+  if (!m) return fail(CIS2B_ERR_ARG, "model is NULL");
+  if (n_seq == 0) return CIS2B_OK;
+  if (!prompt_ids || !prompt_lens || !out_witness) return fail(CIS2B_ERR_ARG, "NULL input/output buffer");
+  if (sample && !(sample->temperature > 0.0f)) return fail(CIS2B_ERR_ARG, "temperature must be > 0");
+  if (sample && !(sample->top_p > 0.0f && sample->top_p <= 1.0f)) return fail(CIS2B_ERR_ARG, "top_p must be in (0, 1]");
+  CU(cudaSetDevice(m->dev));
+  const int B = (int)n_seq, G = (int)gen;
+  uint32_t maxP0 = 0;
+  size_t total_prompt = 0;
+  for (int b = 0; b < B; ++b) {
+    if (prompt_lens[b] == 0) return fail(CIS2B_ERR_ARG, "empty prompt (the reference needs >= 1 id)");
+    maxP0 = std::max(maxP0, prompt_lens[b]);
+    total_prompt += prompt_lens[b];
+  }
+  for (size_t i = 0; i < total_prompt; ++i)
+    if (prompt_ids[i] >= (uint32_t)m->V) return fail(CIS2B_ERR_ARG, "prompt id out of vocabulary range");
+  const int maxP = (int)maxP0 + G;
+  if (maxP > m->max_pos)
+    return fail(CIS2B_ERR_ARG, "prompt + gen_toks exceeds max_positions (" + std::to_string(m->max_pos) + ")");
+  const size_t V = m->V;
+  int ring = std::max(1, G);
+  size_t per_slot = (size_t)B * V * sizeof(float);
+  if ((size_t)ring * per_slot > RING_BUDGET) ring = (int)std::max<size_t>(2, RING_BUDGET / per_slot);
+  ring = std::min(ring, std::max(1, G));
+  int rc = alloc_cache(m, B, maxP);
+  if (rc) return rc;
+  if (m->ring.ensure((size_t)ring * per_slot) || m->hlast.ensure(4 * (size_t)B * m->H) ||
+      m->lnlast.ensure(4 * (size_t)B * m->H) || m->d_next.ensure(4 * (size_t)B) ||
+      m->d_pos.ensure(4 * (size_t)B) || m->d_spos.ensure(4 * (size_t)B) || m->d_seq.ensure(4 * (size_t)B) ||
+      m->d_ctl.ensure(64) || m->d_tokens.ensure(4 * (size_t)B * std::max(G, 1)) ||
+      m->d_ids_hist.ensure(4 * (size_t)B * std::max(G, 1)) ||
+      m->sha_state.ensure(sizeof(ShaState) * (size_t)B) ||
+      m->sha_wk.ensure(4 * sha_wk_words(m->V, B)) || m->step_dig.ensure(32 * (size_t)B * std::max(G, 1)) ||
+      m->d_witness.ensure(32 * (size_t)B) || m->d_argmax.ensure(32 * (size_t)B) ||
+      (sample && m->scratch.ensure(4 * (size_t)B * 5 * V)))
+    return fail(CIS2B_ERR_NOMEM, "device allocation of decode buffers failed");
+  if ((int)m->ev_sha.size() < ring) {
+    for (int i = (int)m->ev_sha.size(); i < ring; ++i) {
+      cudaEvent_t e;
+      CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      m->ev_sha.push_back(e);
+    }
+  }
+  cudaStream_t s = m->s_main, ss = m->s_sha;
+  m->launches = 0;
+
+  // ---- host-side staging (all before the first launch)
+  std::vector<uint32_t> rtok(total_prompt);
+  std::vector<int32_t> rseq(total_prompt), rpos(total_prompt), osrc(B), odst(B), iota(B), pos0(B), spos0(B);
+  std::vector<uint32_t> poff(B), plen(B);
+  {
+    size_t r = 0;
+    for (int b = 0; b < B; ++b) {
+      poff[b] = (uint32_t)r;
+      plen[b] = prompt_lens[b];
+      for (uint32_t p = 0; p < prompt_lens[b]; ++p, ++r) {
+        rtok[r] = prompt_ids[r];
+        rseq[r] = b;
+        rpos[r] = (int32_t)p;
+      }
+      osrc[b] = (int32_t)(r - 1);
+      odst[b] = b;
+      iota[b] = b;
+      pos0[b] = (int32_t)prompt_lens[b] - 1;
+      spos0[b] = (int32_t)prompt_lens[b];
+    }
+  }
+  // witness header bytes (cis2_host.cpp:180-186; e23 patch :617-624)
+  std::vector<uint8_t> hb;
+  std::vector<uint32_t> hoff(B + 1);
+  for (int b = 0; b < B; ++b) {
+    hoff[b] = (uint32_t)hb.size();
+    if (sample) {
+      const char tag[] = "CIS2_SAMPLE_V1";
+      hb.insert(hb.end(), tag, tag + 14);
+      for (int i = 0; i < 8; ++i) hb.push_back((uint8_t)(sample->seed >> (8 * i)));
+      uint32_t tb, pb;
+      memcpy(&tb, &sample->temperature, 4);
+      memcpy(&pb, &sample->top_p, 4);
+      for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(tb >> (8 * i)));
+      for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(pb >> (8 * i)));
+    }
+    hb.insert(hb.end(), m->info.weights_sha256, m->info.weights_sha256 + 32);
+    hb.insert(hb.end(), m->info.tokenizer_sha256, m->info.tokenizer_sha256 + 32);
+    hb.insert(hb.end(), m->info.config_sha256, m->info.config_sha256 + 32);
+    hb.insert(hb.end(), m->info.table_digest, m->info.table_digest + 32);
+    hb.insert(hb.end(), m->info.inv_freq_table_digest, m->info.inv_freq_table_digest + 32);
+    for (uint32_t p = 0; p < prompt_lens[b]; ++p) {
+      uint32_t v = prompt_ids[poff[b] + p];
+      for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(v >> (8 * i)));
+    }
+  }
+  hoff[B] = (uint32_t)hb.size();
+  std::vector<ShaState> st0((size_t)B);
+  for (auto &x : st0) {
+    memset(&x, 0, sizeof x);
+    const uint32_t iv[8] = {0x6a09e667u, 0xbb67ae85u, 0x3c6ef372u, 0xa54ff53au,
+                            0x510e527fu, 0x9b05688cu, 0x1f83d9abu, 0x5be0cd19u};
+    memcpy(x.h, iv, sizeof iv);
+  }
+  if (m->hdr_bytes.ensure(hb.size()) || m->hdr_off.ensure(4 * (size_t)(B + 1)) ||
+      m->p_flat.ensure(4 * total_prompt) || m->p_off.ensure(4 * (size_t)B) || m->p_len.ensure(4 * (size_t)B))
+    return fail(CIS2B_ERR_NOMEM, "device allocation of header buffers failed");
+
+  CU(cudaEventRecord(m->ev0, s));
+  CU(cudaMemcpyAsync(m->hdr_bytes.p, hb.data(), hb.size(), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->hdr_off.p, hoff.data(), 4 * hoff.size(), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->sha_state.p, st0.data(), sizeof(ShaState) * st0.size(), cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->p_flat.p, rtok.data(), 4 * total_prompt, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->p_off.p, poff.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->p_len.p, plen.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->d_seq.p, iota.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->d_pos.p, pos0.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->d_spos.p, spos0.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
+  CU(cudaMemsetAsync(m->d_ctl.p, 0, 64, s));  // [0] step counter, [1] ring slot
+  // Header absorb on the witness stream, ordered after the copies.
+  CU(cudaEventRecord(m->ev_sel, s));
+  CU(cudaStreamWaitEvent(ss, m->ev_sel, 0));
+  launch_sha_absorb_bytes(m->sha_state.as<ShaState>(), m->hdr_bytes.as<uint8_t>(), m->hdr_off.as<uint32_t>(),
+                          B, ss);
+  m->launches++;
+
+  // ---- prefill: every prompt position of every sequence
+  rc = prefill(m, rtok, rseq, rpos, osrc, odst, B, maxP);
+  if (rc) return rc;
+  float *ring_base = m->ring.as<float>();
+  rc = head_rows(m, m->hlast.as<float>(), B, ring_base, nullptr, 0);  // step-0 logits -> slot 0
+  if (rc) return rc;
+  CU(cudaEventRecord(m->ev_pref, s));
+
+  int32_t *d_step = m->d_ctl.as<int32_t>(), *d_slot = m->d_ctl.as<int32_t>() + 1;
+  uint32_t *d_next = m->d_next.as<uint32_t>();
+  for (int t = 0; t < G; ++t) {
+    if (sample)
+      launch_sample(ring_base, m->V, B, d_slot, (size_t)B * V, sample->temperature, sample->top_p,
+                    sample->seed, m->d_spos.as<int32_t>(), m->scratch.as<float>(), d_next, s);
+    else
+      launch_argmax(ring_base, m->V, B, d_slot, (size_t)B * V, d_next, s);
+    launch_step_advance(d_next, B, d_step, G, m->d_tokens.as<uint32_t>(), m->d_ids_hist.as<uint32_t>(),
+                        m->d_pos.as<int32_t>(), m->d_spos.as<int32_t>(), d_slot, ring, d_step, s);
+    m->launches += 2;
+    CU(cudaEventRecord(m->ev_sel, s));
+    CU(cudaStreamWaitEvent(ss, m->ev_sel, 0));
+    launch_sha_step(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
+                    m->d_ids_hist.as<uint32_t>() + (size_t)t * B, m->sha_wk.as<uint32_t>(),
+                    m->step_dig.as<uint8_t>() + (size_t)t * 32, (size_t)G * 32, ss);
+    m->launches += 2;
+    CU(cudaEventRecord(m->ev_sha[(size_t)(t % ring)], ss));
+    if (t + 1 < G) {
+      if (t + 1 >= ring) CU(cudaStreamWaitEvent(s, m->ev_sha[(size_t)((t + 1) % ring)], 0));
+      rc = forward_rows(m, B, d_next, m->d_seq.as<int32_t>(), m->d_pos.as<int32_t>(), B, maxP);
+      if (rc) return rc;
+      rc = head_rows(m, m->h.as<float>(), B, ring_base, d_slot, (size_t)B * V);
+      if (rc) return rc;
+    }
+  }
+  CU(cudaEventRecord(m->ev_dec, s));
+  // Join the witness stream; the final digest and the argmax digest run on
+  // the main stream after its last step.
+  CU(cudaEventRecord(m->ev_sel, ss));
+  CU(cudaStreamWaitEvent(s, m->ev_sel, 0));
+  launch_sha_finalize(m->sha_state.as<ShaState>(), B, m->d_witness.as<uint8_t>(), s);
+  launch_sha_ids(m->p_flat.as<uint32_t>(), m->p_off.as<uint32_t>(), m->p_len.as<uint32_t>(),
+                 m->d_tokens.as<uint32_t>(), G, B, m->d_argmax.as<uint8_t>(), s);
+  m->launches += 2;
+  CU(cudaEventRecord(m->ev_end, s));
+  CU_LAUNCHED();
+  if (out_tokens && G) CU(cudaMemcpyAsync(out_tokens, m->d_tokens.p, 4 * (size_t)B * G, cudaMemcpyDeviceToHost, s));
+  if (out_steps && G) CU(cudaMemcpyAsync(out_steps, m->step_dig.p, 32 * (size_t)B * G, cudaMemcpyDeviceToHost, s));
+  CU(cudaMemcpyAsync(out_witness, m->d_witness.p, 32 * (size_t)B, cudaMemcpyDeviceToHost, s));
+  if (out_argmax) CU(cudaMemcpyAsync(out_argmax, m->d_argmax.p, 32 * (size_t)B, cudaMemcpyDeviceToHost, s));
+  CU(cudaStreamSynchronize(s));
+  CU(cudaStreamSynchronize(ss));
+  float t_tot = 0, t_pre = 0, t_dec = 0, t_tail = 0;
+  CU(cudaEventElapsedTime(&t_tot, m->ev0, m->ev_end));
+  CU(cudaEventElapsedTime(&t_pre, m->ev0, m->ev_pref));
+  CU(cudaEventElapsedTime(&t_dec, m->ev_pref, m->ev_dec));
+  CU(cudaEventElapsedTime(&t_tail, m->ev_dec, m->ev_end));
+  m->timing.total_ms = t_tot;
+  m->timing.prefill_ms = t_pre;
+  m->timing.decode_ms = t_dec;
+  m->timing.witness_tail_ms = t_tail;
+  m->timing.kernel_launches = m->launches;
+  return CIS2B_OK;
+}
+
+int logits_impl(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_rows, float *out) {
+  if (!m || !ids || !out) return fail(CIS2B_ERR_ARG, "NULL argument");
+  if (n_prompt == 0 || n_rows == 0) return fail(CIS2B_ERR_ARG, "n_prompt and n_rows must be >= 1");
+  CU(cudaSetDevice(m->dev));
+  const int total = (int)(n_prompt + n_rows - 1);
+  if (total > m->max_pos) return fail(CIS2B_ERR_ARG, "sequence exceeds max_positions");
+  for (int i = 0; i < total; ++i)
+    if (ids[i] >= (uint32_t)m->V) return fail(CIS2B_ERR_ARG, "id out of vocabulary range");
+  int rc = alloc_cache(m, 1, total);
+  if (rc) return rc;
+  std::vector<uint32_t> tok(ids, ids + total);
+  std::vector<int32_t> seq((size_t)total, 0), pos((size_t)total), osrc(n_rows), odst(n_rows);
+  for (int i = 0; i < total; ++i) pos[(size_t)i] = i;
+  for (uint32_t r = 0; r < n_rows; ++r) { osrc[r] = (int32_t)(n_prompt - 1 + r); odst[r] = (int32_t)r; }
+  if (m->hlast.ensure(4 * (size_t)n_rows * m->H) || m->lnlast.ensure(4 * (size_t)n_rows * m->H) ||
+      m->ring.ensure(4 * (size_t)n_rows * m->V) || ensure_act(m, 1))
+    return fail(CIS2B_ERR_NOMEM, "device allocation failed");
+  rc = prefill(m, tok, seq, pos, osrc, odst, 1, total);
+  if (rc) return rc;
+  rc = head_rows(m, m->hlast.as<float>(), (int)n_rows, m->ring.as<float>(), nullptr, 0);
+  if (rc) return rc;
+  CU(cudaMemcpyAsync(out, m->ring.p, 4 * (size_t)n_rows * m->V, cudaMemcpyDeviceToHost, m->s_main));
+  CU(cudaStreamSynchronize(m->s_main));
+  return CIS2B_OK;
+}
+
+template <class T>
+struct Scoped {
+  T *p = nullptr;
+  ~Scoped() { if (p) cudaFree(p); }
+};
+
+}  // namespace
+
+// ================================================================== C ABI
+extern "C" {
+
+const char *cis2b_last_error(void) { return g_err.c_str(); }
+
+int cis2b_load(const char *weights_dir, const cis2b_opts *opts, cis2b_model **out) {
+  if (!out) return fail(CIS2B_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  cis2b_model *m = new (std::nothrow) cis2b_model();
+  if (!m) return fail(CIS2B_ERR_NOMEM, "host allocation failed");
+  int rc = load_impl(weights_dir, opts, m);
+  if (rc) {
+    cis2b_free(m);
+    return rc;
+  }
+  *out = m;
+  g_err.clear();
+  return CIS2B_OK;
+}
+
+int cis2b_info_get(const cis2b_model *m, cis2b_info *out) {
+  if (!m || !out) return fail(CIS2B_ERR_ARG, "NULL argument");
+  *out = m->info;
+  return CIS2B_OK;
+}
+
+int cis2b_generate(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *prompt_lens, uint32_t n_seq,
+                   uint32_t gen_toks, const cis2b_sample *sample, uint32_t *out_tokens,
+                   uint8_t *out_step_digests, uint8_t *out_witness, uint8_t *out_argmax) {
+  int rc = generate_impl(m, prompt_ids, prompt_lens, n_seq, gen_toks, sample, out_tokens, out_step_digests,
+                         out_witness, out_argmax);
+  if (rc == CIS2B_OK) g_err.clear();
+  return rc;
+}
+
+int cis2b_last_timing(const cis2b_model *m, cis2b_timing *out) {
+  if (!m || !out) return fail(CIS2B_ERR_ARG, "NULL argument");
+  *out = m->timing;
+  return CIS2B_OK;
+}
+
+int cis2b_logits(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_rows, float *out_logits) {
+  int rc = logits_impl(m, ids, n_prompt, n_rows, out_logits);
+  if (rc == CIS2B_OK) g_err.clear();
+  return rc;
+}
+
+void cis2b_free(cis2b_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->dev);
+  if (m->s_main) cudaStreamSynchronize(m->s_main);
+  if (m->s_sha) cudaStreamSynchronize(m->s_sha);
+  for (cudaEvent_t e : m->ev_sha) cudaEventDestroy(e);
+  cudaEvent_t evs[] = {m->ev_sel, m->ev0, m->ev_pref, m->ev_dec, m->ev_end};
+  for (cudaEvent_t e : evs)
+    if (e) cudaEventDestroy(e);
+  if (m->s_main) cudaStreamDestroy(m->s_main);
+  if (m->s_sha) cudaStreamDestroy(m->s_sha);
+  delete m;
+}
+
+// ---------------------------------------------------------------- op entry points
+
+int cis2b_op_pinned_map(int32_t device, int32_t fn, const float *x, float *y, size_t n) {
+  if (!x || !y) return fail(CIS2B_ERR_ARG, "NULL buffer");
+  if (fn < 0 || fn > 5) return fail(CIS2B_ERR_ARG, "unknown function id");
+  CU(cudaSetDevice(device));
+  Scoped<float> dx, dy;
+  CU(cudaMalloc(&dx.p, 4 * n + 4));
+  CU(cudaMalloc(&dy.p, 4 * n + 4));
+  CU(cudaMemcpy(dx.p, x, 4 * n, cudaMemcpyHostToDevice));
+  launch_pinned_map(fn, dx.p, dy.p, n, 0);
+  CU_LAUNCHED();
+  CU(cudaMemcpy(y, dy.p, 4 * n, cudaMemcpyDeviceToHost));
+  return CIS2B_OK;
+}
+
+int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t rows, int32_t n_out, int32_t k,
+                    int32_t reduction, float *Y) {
+  if (!W || !X || !Y) return fail(CIS2B_ERR_ARG, "NULL buffer");
+  if (rows <= 0 || n_out <= 0 || k <= 0 || k % 8) return fail(CIS2B_ERR_ARG, "bad shape (k must be a multiple of 8)");
+  CU(cudaSetDevice(device));
+  Scoped<uint16_t> dw;
+  Scoped<float> dx, dy;
+  CU(cudaMalloc(&dw.p, 2 * (size_t)n_out * k));
+  CU(cudaMalloc(&dx.p, 4 * (size_t)rows * k));
+  CU(cudaMalloc(&dy.p, 4 * (size_t)rows * n_out));
+  CU(cudaMemcpy(dw.p, W, 2 * (size_t)n_out * k, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(dx.p, X, 4 * (size_t)rows * k, cudaMemcpyHostToDevice));
+  launch_gemm(dx.p, k, dw.p, k, n_out, rows, dy.p, n_out, nullptr, 0, reduction == CIS2B_REDUCTION_TREE,
+              nullptr, 0, 0);
+  CU_LAUNCHED();
+  CU(cudaMemcpy(Y, dy.p, 4 * (size_t)rows * n_out, cudaMemcpyDeviceToHost));
+  return CIS2B_OK;
+}
+
+int cis2b_op_sha256_stream(int32_t device, const uint8_t *prefix, size_t prefix_len, const uint32_t *words,
+                           uint32_t chunk_words, uint32_t n_chunks, uint8_t *out_digests) {
+  if ((!prefix && prefix_len) || (!words && n_chunks) || !out_digests) return fail(CIS2B_ERR_ARG, "NULL buffer");
+  if (chunk_words < 2 && n_chunks) return fail(CIS2B_ERR_ARG, "chunk_words must be >= 2");
+  CU(cudaSetDevice(device));
+  Scoped<ShaState> st;
+  Scoped<uint8_t> pre, dig;
+  Scoped<uint32_t> off, w, wk;
+  ShaState s0;
+  memset(&s0, 0, sizeof s0);
+  const uint32_t iv[8] = {0x6a09e667u, 0xbb67ae85u, 0x3c6ef372u, 0xa54ff53au,
+                          0x510e527fu, 0x9b05688cu, 0x1f83d9abu, 0x5be0cd19u};
+  memcpy(s0.h, iv, sizeof iv);
+  CU(cudaMalloc(&st.p, sizeof(ShaState)));
+  CU(cudaMemcpy(st.p, &s0, sizeof s0, cudaMemcpyHostToDevice));
+  CU(cudaMalloc(&pre.p, prefix_len + 1));
+  CU(cudaMalloc(&off.p, 8));
+  uint32_t offs[2] = {0, (uint32_t)prefix_len};
+  if (prefix_len) CU(cudaMemcpy(pre.p, prefix, prefix_len, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(off.p, offs, 8, cudaMemcpyHostToDevice));
+  launch_sha_absorb_bytes(st.p, pre.p, off.p, 1, 0);
+  const int V = (int)chunk_words - 1;
+  CU(cudaMalloc(&w.p, 4 * (size_t)chunk_words * n_chunks + 4));
+  CU(cudaMalloc(&wk.p, 4 * sha_wk_words(V, 1)));
+  CU(cudaMalloc(&dig.p, 32 * (size_t)n_chunks + 32));
+  if (n_chunks) CU(cudaMemcpy(w.p, words, 4 * (size_t)chunk_words * n_chunks, cudaMemcpyHostToDevice));
+  for (uint32_t c = 0; c < n_chunks; ++c) {
+    const uint32_t *base = w.p + (size_t)c * chunk_words;
+    launch_sha_step(st.p, 1, reinterpret_cast<const float *>(base), V, (size_t)V, base + V, wk.p,
+                    dig.p + 32 * (size_t)c, 32, 0);
+  }
+  CU_LAUNCHED();
+  if (n_chunks) CU(cudaMemcpy(out_digests, dig.p, 32 * (size_t)n_chunks, cudaMemcpyDeviceToHost));
+  else {
+    launch_sha_finalize(st.p, 1, dig.p, 0);
+    CU(cudaMemcpy(out_digests, dig.p, 32, cudaMemcpyDeviceToHost));
+  }
+  return CIS2B_OK;
+}
+
+int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temperature, float top_p, uint64_t seed,
+                    uint64_t position, uint32_t *out_index) {
+  if (!logits || !out_index || n <= 0) return fail(CIS2B_ERR_ARG, "bad argument");
+  if (!(temperature > 0.0f) || !(top_p > 0.0f && top_p <= 1.0f)) return fail(CIS2B_ERR_ARG, "bad sampler parameters");
+  CU(cudaSetDevice(device));
+  Scoped<float> dl, scr;
+  Scoped<uint32_t> nx;
+  Scoped<int32_t> dp;
+  CU(cudaMalloc(&dl.p, 4 * (size_t)n));
+  CU(cudaMalloc(&scr.p, 4 * 5 * (size_t)n));
+  CU(cudaMalloc(&nx.p, 4));
+  CU(cudaMalloc(&dp.p, 4));
+  int32_t pos32 = (int32_t)position;
+  CU(cudaMemcpy(dl.p, logits, 4 * (size_t)n, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(dp.p, &pos32, 4, cudaMemcpyHostToDevice));
+  launch_sample(dl.p, n, 1, nullptr, 0, temperature, top_p, seed, dp.p, scr.p, nx.p, 0);
+  CU_LAUNCHED();
+  CU(cudaMemcpy(out_index, nx.p, 4, cudaMemcpyDeviceToHost));
+  return CIS2B_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+/* include/cis2b.h -- C ABI of the B200 (sm_100a) CIS-2 deterministic decoder.
+ *
+ * Drop-in boundary for the reference's model-load / generate / witness
+ * surface.  Plain C types only.  Every function returns CIS2B_OK (0) or an
+ * error code and never exits the process; the message of the last failure
+ * on the calling thread is available from cis2b_last_error().
+ *
+ * Reference interfaces each entry point replaces (paths inside
+ * Aefinity-AI/cis2-lab-archive):
+ *   cis2b_load      cis2_model_load()            code/cis2-fp/verify3/model.h:56
+ *                   + the load half of main()    code/cis2-fp/gpu/cis2_host.cpp:87-163
+ *                                                (config, artifact sha256, table digest,
+ *                                                 inv_freq table, bf16 weights)
+ *   cis2b_generate  cis2_run_decode()            code/cis2-fp/verify3/model.h:71-76
+ *                   + the decode half of main()  code/cis2-fp/gpu/cis2_host.cpp:165-218
+ *                   + run_one_prompt (sampled)   code/patches/cis2-fp__cm_e23-pinned-sampling.patch:581-780
+ *                   batched over sequences as in code/patches/cis2-fp__cm_gpu3-batched-full.patch:687-763
+ *   cis2b_free      cis2_model_free()            code/cis2-fp/verify3/model.h:57
+ *   cis2b_info_get  the printed header lines     code/cis2-fp/gpu/cis2_host.cpp:222-227
+ *   cis2b_logits    teacher-forced logits        code/cis2-fp/verify3/model.h:138-158
+ *                   (cis2_verify_receipt_prefill's all_logits)
+ *
+ * Threading: a model handle belongs to one device and must not be used by
+ * two threads at once (the reference's verify3 state is global and not
+ * thread-safe at all, model.c:49).  Different handles are independent.
+ */
+#ifndef CIS2B_H
+#define CIS2B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CIS2B_OK 0
+#define CIS2B_ERR_ARG 1      /* invalid argument or size */
+#define CIS2B_ERR_IO 2       /* artifact missing / unreadable / malformed */
+#define CIS2B_ERR_CONFIG 3   /* architecture this decoder refuses */
+#define CIS2B_ERR_CUDA 4     /* CUDA runtime or kernel failure */
+#define CIS2B_ERR_NOMEM 5    /* host or device allocation failed */
+
+#define CIS2B_REDUCTION_SEQUENTIAL 0 /* CIS-2 v0.3b default: strict left-to-right folds */
+#define CIS2B_REDUCTION_TREE 1       /* v0.4 candidate: 32-leaf pairwise blocks */
+
+typedef struct cis2b_model cis2b_model;
+
+typedef struct {
+  int32_t device;        /* CUDA device ordinal */
+  int32_t reduction;     /* CIS2B_REDUCTION_* */
+  int32_t max_positions; /* prompt + generated positions per sequence; 0 = 4096 */
+  int32_t reserved[5];   /* must be zero */
+} cis2b_opts;
+
+/* E23 pinned sampler parameters (sampled mode).  Pass NULL for greedy. */
+typedef struct {
+  uint64_t seed;
+  float temperature; /* > 0 */
+  float top_p;       /* (0, 1] */
+} cis2b_sample;
+
+typedef struct {
+  int32_t hidden, intermediate, n_layers, n_heads, n_kv_heads, head_dim, vocab, tied;
+  float rms_norm_eps;  /* narrowed once from the f64 config value */
+  double rope_theta;
+  int32_t reduction;
+  int32_t max_positions;
+  uint8_t weights_sha256[32];
+  uint8_t tokenizer_sha256[32];
+  uint8_t config_sha256[32];
+  uint8_t table_digest[32];
+  uint8_t inv_freq_table_digest[32];
+} cis2b_info;
+
+/* Device-side timing of the last cis2b_generate (CUDA events). */
+typedef struct {
+  double total_ms;    /* first kernel to last witness kernel */
+  double prefill_ms;  /* prompt positions through the model */
+  double decode_ms;   /* token steps (forward + selection), main stream */
+  double witness_tail_ms; /* witness work left after the last decode step */
+  int64_t kernel_launches; /* kernels this library launched for the call */
+} cis2b_timing;
+
+/* Loads weights_dir/{model.safetensors,config.json,tokenizer.json}: hashes
+ * the three artifacts, parses the config (numbers as f64, eps narrowed once),
+ * uploads the bf16 weights to the device and builds the pinned inv_freq and
+ * RoPE tables there. */
+int cis2b_load(const char *weights_dir, const cis2b_opts *opts, cis2b_model **out);
+
+int cis2b_info_get(const cis2b_model *m, cis2b_info *out);
+
+/* Decodes n_seq independent sequences in one batch.
+ *   prompt_ids   concatenated prompts (u32 token ids), prompt_lens[n_seq] >= 1
+ *   gen_toks     tokens to generate per sequence (>= 0)
+ *   sample       NULL = greedy argmax (first maximum wins); else the E23
+ *                sampler with position = prompt_len + step
+ * Outputs (caller-owned host buffers, any may be NULL except out_witness):
+ *   out_tokens        [n_seq][gen_toks]
+ *   out_step_digests  [n_seq][gen_toks][32]  witness state finalised after each step
+ *   out_witness       [n_seq][32]  final witness digest (CIS2_REF / CIS2_SAMPLE digest)
+ *   out_argmax        [n_seq][32]  SHA-256 over prompt ids then generated ids
+ * Each sequence's outputs equal its own batch-1 run. */
+int cis2b_generate(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *prompt_lens,
+                   uint32_t n_seq, uint32_t gen_toks, const cis2b_sample *sample,
+                   uint32_t *out_tokens, uint8_t *out_step_digests, uint8_t *out_witness,
+                   uint8_t *out_argmax);
+
+int cis2b_last_timing(const cis2b_model *m, cis2b_timing *out);
+
+/* Teacher-forced logits of ONE sequence: runs ids[0 .. n_prompt+n_rows-2]
+ * and writes the fp32 logits after positions n_prompt-1 .. n_prompt+n_rows-2
+ * into out_logits[n_rows][vocab]. */
+int cis2b_logits(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_rows,
+                 float *out_logits);
+
+void cis2b_free(cis2b_model *m);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *cis2b_last_error(void);
+
+/* ---- kernel-level entry points (host buffers in and out) ---------------
+ * Used by the parity tests to check single kernels against the CPU oracle. */
+
+/* y[i] = f(x[i]); f: 0 exp, 1 sin, 2 cos, 3 ln, 4 silu, 5 rsqrt (spec §6). */
+int cis2b_op_pinned_map(int32_t device, int32_t fn, const float *x, float *y, size_t n);
+/* Y[r][o] = dot(W[o,:], X[r,:]) in the pinned order; W bf16 [n_out][k], k % 8 == 0. */
+int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t rows, int32_t n_out,
+                    int32_t k, int32_t reduction, float *Y);
+/* Witness stream check: absorbs `prefix` (byte path), then n_chunks chunks of
+ * chunk_words u32 words through the device step path (last word of each
+ * chunk plays the token id); writes the digest after each chunk. */
+int cis2b_op_sha256_stream(int32_t device, const uint8_t *prefix, size_t prefix_len,
+                           const uint32_t *words, uint32_t chunk_words, uint32_t n_chunks,
+                           uint8_t *out_digests);
+/* E23 sampler on one logits row. */
+int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temperature, float top_p,
+                    uint64_t seed, uint64_t position, uint32_t *out_index);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CIS2B_H */

@@ -1,0 +1,109 @@
+"""GPU parity of single kernels, through the C ABI, against the oracle.
+Bit-exact (tolerance zero) everywhere."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def sweep_inputs() -> np.ndarray:
+    """Edge values plus a seeded sweep, following the reference's golden
+    sweep recipe (code/cis2-fp/src/bin/math_dump.rs:67-180): explicit edges,
+    exp clamp boundaries, k*pi/2 and k*pi/4 neighbours, then LCG bit
+    patterns and uniform ranges."""
+    edges = [0x00000000, 0x80000000, 0x00000001, 0x80000001, 0x007FFFFF, 0x807FFFFF, 0x00800000,
+             0x80800000, 0x3F800000, 0xBF800000, 0x3F000000, 0xBF000000, 0x7F7FFFFF, 0xFF7FFFFF,
+             0x7F800000, 0xFF800000, 0x7FC00000, 0x34000000, 0x4B000000, 0x5F000000]
+    v = list(np.array(edges, dtype=np.uint32).view(np.float32))
+    for x in [-88.0, -87.99999, -88.00001, 88.0, 87.99999, 88.00001, 1e-10, -1e-10, 0.6931472,
+              -0.6931472, 0.3465736, 1e10, -1e10]:
+        f = np.float32(x)
+        v += [f, np.nextafter(f, np.float32(np.inf)), np.nextafter(f, np.float32(-np.inf))]
+    for k in range(-64, 65):
+        for base in (np.pi / 2, np.pi / 4):
+            f = np.float32(k * base)
+            v += [f, np.nextafter(f, np.float32(np.inf)), np.nextafter(f, np.float32(-np.inf))]
+    state = np.uint64(0x243F6A8885A308D3)
+    bits = []
+    for _ in range(60000):
+        state = np.uint64((int(state) * 6364136223846793005 + 1442695040888963407) & ((1 << 64) - 1))
+        bits.append(int(state) >> 32)
+    v += list(np.array(bits, dtype=np.uint32).view(np.float32))
+    rng = np.random.default_rng(7)
+    v += list(rng.uniform(-100, 100, 40000).astype(np.float32))
+    v += list(rng.uniform(-3, 3, 40000).astype(np.float32))
+    v += list((rng.uniform(0, 1, 20000) * 2048 * 0.5).astype(np.float32))  # RoPE angles
+    v += list(np.exp(rng.uniform(-80, 80, 20000)).astype(np.float32))      # ln domain
+    return np.array(v, dtype=np.float32)
+
+
+@pytest.mark.parametrize("fn", ["exp", "sin", "cos", "ln", "silu", "rsqrt"])
+def test_pinned_math_bit_exact(fn, pkg, oracle):
+    x = sweep_inputs()
+    got = pkg.pinned_map(fn, x)
+    want = oracle.pinned_map(pkg.PINNED_FUNCS[fn], x)
+    gb, wb = got.view(np.uint32), want.view(np.uint32)
+    bad = np.nonzero(gb != wb)[0]
+    assert bad.size == 0, [(hex(x.view(np.uint32)[i]), hex(gb[i]), hex(wb[i])) for i in bad[:8]]
+
+
+SHAPES = [(1, 576, 576), (3, 192, 576), (4, 100, 96), (7, 1536, 576), (16, 64, 1536), (33, 200, 40),
+          (64, 576, 1536), (64, 960, 576), (5, 4099, 64), (128, 1024, 3072), (65, 300, 8), (2, 49152, 576)]
+
+
+@pytest.mark.parametrize("tree", [False, True])
+@pytest.mark.parametrize("rows,n,k", SHAPES)
+def test_matmul_bit_exact(rows, n, k, tree, pkg, oracle):
+    rng = np.random.default_rng(rows * 1000003 + n * 31 + k)
+    W = (rng.standard_normal((n, k)).astype(np.float32) * np.float32(0.02)).view(np.uint32)
+    W = ((W + 0x7FFF + ((W >> 16) & 1)) >> 16).astype(np.uint16)
+    X = rng.standard_normal((rows, k)).astype(np.float32)
+    X[:, ::7] = 0.0  # signed zeros and cancellations in the chains
+    X[:, 1::11] *= -0.0
+    got = pkg.matmul(W, X, tree=tree)
+    want = oracle.matmul_bf16(W, X, tree=tree)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("prefix_len,chunk", [(0, 17), (160, 49153), (190, 49153), (30, 1024), (2, 2),
+                                              (62, 16), (64, 15), (190, 151937), (14, 100)])
+def test_witness_stream_sha256(prefix_len, chunk, pkg):
+    rng = np.random.default_rng(prefix_len * 7 + chunk)
+    prefix = rng.integers(0, 256, prefix_len, dtype=np.uint8).tobytes()
+    n_chunks = 3
+    words = rng.integers(0, 2**32, chunk * n_chunks, dtype=np.uint64).astype(np.uint32)
+    got = pkg.sha256_stream(prefix, words, chunk)
+    h = hashlib.sha256(prefix)
+    for c in range(n_chunks):
+        h.update(words[c * chunk:(c + 1) * chunk].astype("<u4").tobytes())
+        assert got[c].tobytes() == h.copy().digest(), c
+
+
+def test_witness_stream_prefix_only(pkg):
+    got = pkg.sha256_stream(b"abc", np.zeros(0, np.uint32), 0)
+    assert got[0].tobytes() == hashlib.sha256(b"abc").digest()
+
+
+@pytest.mark.parametrize("n,T,top_p", [(64, 0.8, 0.95), (4096, 0.8, 0.95), (151936, 0.8, 0.95),
+                                       (1000, 1.0, 1e-6), (1000, 0.5, 1.0), (49152, 1.3, 0.5)])
+def test_sampler_matches_oracle(n, T, top_p, pkg, oracle):
+    rng = np.random.default_rng(n)
+    for trial in range(3):
+        logits = (rng.standard_normal(n) * (0.6 + trial)).astype(np.float32)
+        if trial == 2:
+            logits[::5] = logits[0]  # many exact ties -> index tie-break
+        for pos in (0, 63, 300):
+            seed = 1234 + trial
+            want = oracle.lib().cis2o_sample_pinned(logits.ctypes.data, n, T, top_p, seed, pos)
+            assert pkg.sample(logits, T, top_p, seed, pos) == want
+
+
+def test_sampler_unit_cases_gpu(pkg):
+    l2 = np.zeros(32, dtype=np.float32)
+    l2[7] = 50.0
+    assert pkg.sample(l2, 1.0, 1e-6, 999, 3) == 7
+    assert pkg.sample(np.zeros(4, np.float32), 1.0, 1e-6, 0, 0) == 0
