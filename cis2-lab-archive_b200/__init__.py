@@ -59,7 +59,15 @@ class _Info(ctypes.Structure):
 class _Timing(ctypes.Structure):
     _fields_ = [("total_ms", ctypes.c_double), ("prefill_ms", ctypes.c_double),
                 ("decode_ms", ctypes.c_double), ("witness_tail_ms", ctypes.c_double),
-                ("kernel_launches", ctypes.c_int64)]
+                ("kernel_launches", ctypes.c_int64), ("h2d_bytes", ctypes.c_int64),
+                ("d2h_bytes", ctypes.c_int64)]
+
+
+class _KTime(ctypes.Structure):
+    _fields_ = [("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
+
+
+PROF_CLASSES = {"lm_head": 1, "layer_gemm": 2, "attention": 4, "witness": 8}
 
 
 _lib = None
@@ -81,6 +89,8 @@ def lib() -> ctypes.CDLL:
     L.cis2b_generate.argtypes = [P, P, P, U32, U32, ctypes.POINTER(_Sample), P, P, P, P]
     L.cis2b_last_timing.argtypes = [P, ctypes.POINTER(_Timing)]
     L.cis2b_logits.argtypes = [P, P, U32, U32, P]
+    L.cis2b_profile.argtypes = [P, U32]
+    L.cis2b_profile_read.argtypes = [P, U32, ctypes.POINTER(_KTime)]
     L.cis2b_free.argtypes = [P]
     L.cis2b_free.restype = None
     L.cis2b_op_pinned_map.argtypes = [I32, I32, P, P, SZ]
@@ -158,6 +168,18 @@ class Model:
         t = _Timing()
         _check(lib().cis2b_last_timing(self._h, ctypes.byref(t)))
         return {k: getattr(t, k) for k, _ in _Timing._fields_}
+
+    def profile(self, classes) -> None:
+        """Time every launch of the named kernel classes (see PROF_CLASSES)."""
+        mask = 0
+        for c in classes:
+            mask |= PROF_CLASSES[c]
+        _check(lib().cis2b_profile(self._h, mask))
+
+    def profile_read(self, cls: str) -> dict:
+        k = _KTime()
+        _check(lib().cis2b_profile_read(self._h, PROF_CLASSES[cls], ctypes.byref(k)))
+        return {"launches": k.launches, "total_ms": k.total_ms}
 
     def logits(self, ids, n_prompt: int, n_rows: int) -> np.ndarray:
         ids = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))

@@ -951,16 +951,27 @@ k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_s
   }
 }
 
-void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
-                     const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,
-                     size_t digest_stride, cudaStream_t s) {
+void launch_sha_prep(const ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                     const uint32_t *next_ids, uint32_t *wk_scratch, cudaStream_t s) {
   if (n_seq <= 0) return;
   int nb_max = (int)((63 + 4 * (size_t)V + 4) / 64);
   size_t threads = (size_t)nb_max * n_seq;
   k_sha_prep<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(st, n_seq, logits, V, row_stride,
                                                               next_ids, wk_scratch, nb_max);
+}
+void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                         const uint32_t *next_ids, const uint32_t *wk_scratch, uint8_t *step_digest_out,
+                         size_t digest_stride, cudaStream_t s) {
+  if (n_seq <= 0) return;
   k_sha_compress<<<(n_seq + 31) / 32, 32, 0, s>>>(st, n_seq, logits, V, row_stride, next_ids,
                                                   wk_scratch, step_digest_out, digest_stride);
+}
+void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                     const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,
+                     size_t digest_stride, cudaStream_t s) {
+  launch_sha_prep(st, n_seq, logits, V, row_stride, next_ids, wk_scratch, s);
+  launch_sha_compress(st, n_seq, logits, V, row_stride, next_ids, wk_scratch, step_digest_out,
+                      digest_stride, s);
 }
 
 __global__ void k_sha_finalize(const ShaState *st, int n_seq, uint8_t *out) {

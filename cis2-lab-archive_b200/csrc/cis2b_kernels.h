@@ -67,6 +67,13 @@ size_t sha_wk_words(int V, int n_seq);
 void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                      const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,
                      size_t digest_stride, cudaStream_t s);
+// The two halves of launch_sha_step: W+K expansion (many threads), then the
+// per-sequence compression chain.
+void launch_sha_prep(const ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                     const uint32_t *next_ids, uint32_t *wk_scratch, cudaStream_t s);
+void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
+                         const uint32_t *next_ids, const uint32_t *wk_scratch, uint8_t *step_digest_out,
+                         size_t digest_stride, cudaStream_t s);
 void launch_sha_finalize(const ShaState *st, int n_seq, uint8_t *out, cudaStream_t s);
 // Argmax digest: SHA-256 over prompt ids then generated ids (u32 LE).
 void launch_sha_ids(const uint32_t *prompt_flat, const uint32_t *prompt_off, const uint32_t *prompt_len,

@@ -100,10 +100,57 @@ struct cis2b_model {
   std::vector<cudaEvent_t> ev_sha;
   cudaEvent_t ev_sel = nullptr, ev0 = nullptr, ev_pref = nullptr, ev_dec = nullptr, ev_end = nullptr;
   cis2b_timing timing{};
-  int64_t launches = 0;
+  int64_t launches = 0, h2d = 0, d2h = 0;
+  // per-launch event timing of selected kernel classes (cis2b_profile)
+  struct ProfEvent { uint32_t cls; cudaEvent_t a, b; };
+  uint32_t prof_mask = 0;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<ProfEvent> prof_events;
+  cis2b_kernel_time prof[4]{};
 };
 
 namespace {
+
+cudaEvent_t pool_event(cis2b_model *m) {
+  if (m->ev_used == m->ev_pool.size()) {
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    m->ev_pool.push_back(e);
+  }
+  return m->ev_pool[m->ev_used++];
+}
+
+// Brackets the launches made in its scope with an event pair on stream `s`
+// when the class is selected for profiling.
+struct ProfScope {
+  cis2b_model *m;
+  uint32_t cls;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr;
+  ProfScope(cis2b_model *m_, uint32_t cls_, cudaStream_t s_) : m(m_), cls(cls_), s(s_) {
+    if (m->prof_mask & cls) {
+      a = pool_event(m);
+      cudaEventRecord(a, s);
+    }
+  }
+  ~ProfScope() {
+    if (!a) return;
+    cudaEvent_t b = pool_event(m);
+    cudaEventRecord(b, s);
+    m->prof_events.push_back({cls, a, b});
+  }
+};
+
+int class_index(uint32_t bit) {
+  switch (bit) {
+    case CIS2B_PROF_LM_HEAD: return 0;
+    case CIS2B_PROF_LAYER_GEMM: return 1;
+    case CIS2B_PROF_ATTENTION: return 2;
+    case CIS2B_PROF_WITNESS: return 3;
+    default: return -1;
+  }
+}
 
 const char *kSlotNames[] = {"input_layernorm.weight", "post_attention_layernorm.weight"};
 
@@ -361,19 +408,24 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     float *kc = m->kc.as<float>() + (size_t)l * layer_kv;
     float *vc = m->vc.as<float>() + (size_t)l * layer_kv;
     launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, H, s);
-    launch_gemm(ln, H, w.wqkv, H, NQKV, rows, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s);
+    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+      launch_gemm(ln, H, w.wqkv, H, NQKV, rows, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s); }
     m->launches += 2;
     if (w.q_bias) { launch_add_bias(qkv, NQKV, rows, w.q_bias, QD, s); m->launches++; }
     if (w.k_bias) { launch_add_bias(qkv + QD, NQKV, rows, w.k_bias, KVD, s); m->launches++; }
     if (w.v_bias) { launch_add_bias(qkv + QD + KVD, NQKV, rows, w.v_bias, KVD, s); m->launches++; }
     launch_qkv_post(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, w.q_norm, w.k_norm, m->eps, m->tree,
                     m->cos_t.as<float>(), m->sin_t.as<float>(), kc, vc, maxP, s);
-    launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, QD, maxP, s);
-    launch_gemm(att, QD, w.wo, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s);
+    { ProfScope p(m, CIS2B_PROF_ATTENTION, s);
+      launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, QD, maxP, s); }
+    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+      launch_gemm(att, QD, w.wo, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
     launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, H, s);
-    launch_gemm(ln, H, w.wgu, H, 2 * I, rows, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s);
+    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+      launch_gemm(ln, H, w.wgu, H, 2 * I, rows, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s); }
     launch_silu_mul(gu, I, rows, hid, s);
-    launch_gemm(hid, I, w.wdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s);
+    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+      launch_gemm(hid, I, w.wdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
     m->launches += 7;
   }
   CU_LAUNCHED();
@@ -385,8 +437,11 @@ int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_
               size_t slot_stride) {
   cudaStream_t s = m->s_main;
   launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(), m->H, s);
-  launch_gemm(m->lnlast.as<float>(), m->H, m->lm_head, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
-              y_slot, slot_stride, s);
+  {
+    ProfScope p(m, CIS2B_PROF_LM_HEAD, s);
+    launch_gemm(m->lnlast.as<float>(), m->H, m->lm_head, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
+                y_slot, slot_stride, s);
+  }
   m->launches += 2;
   CU_LAUNCHED();
   return CIS2B_OK;
@@ -510,6 +565,8 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   }
   cudaStream_t s = m->s_main, ss = m->s_sha;
   m->launches = 0;
+  m->ev_used = 0;
+  m->prof_events.clear();
 
   // ---- host-side staging (all before the first launch)
   std::vector<uint32_t> rtok(total_prompt);
@@ -608,9 +665,14 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
     m->launches += 2;
     CU(cudaEventRecord(m->ev_sel, s));
     CU(cudaStreamWaitEvent(ss, m->ev_sel, 0));
-    launch_sha_step(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
-                    m->d_ids_hist.as<uint32_t>() + (size_t)t * B, m->sha_wk.as<uint32_t>(),
-                    m->step_dig.as<uint8_t>() + (size_t)t * 32, (size_t)G * 32, ss);
+    launch_sha_prep(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
+                    m->d_ids_hist.as<uint32_t>() + (size_t)t * B, m->sha_wk.as<uint32_t>(), ss);
+    {
+      ProfScope p(m, CIS2B_PROF_WITNESS, ss);
+      launch_sha_compress(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
+                          m->d_ids_hist.as<uint32_t>() + (size_t)t * B, m->sha_wk.as<uint32_t>(),
+                          m->step_dig.as<uint8_t>() + (size_t)t * 32, (size_t)G * 32, ss);
+    }
     m->launches += 2;
     CU(cudaEventRecord(m->ev_sha[(size_t)(t % ring)], ss));
     if (t + 1 < G) {
@@ -648,6 +710,20 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   m->timing.decode_ms = t_dec;
   m->timing.witness_tail_ms = t_tail;
   m->timing.kernel_launches = m->launches;
+  // bytes the call moved across PCIe: header bytes, offsets, states, prompt
+  // ids and row maps in; tokens, digests out.
+  m->timing.h2d_bytes = (int64_t)(hb.size() + 4 * hoff.size() + sizeof(ShaState) * st0.size() +
+                                  4 * total_prompt * 4 + 4 * (size_t)B * 6 + 8 * (size_t)B);
+  m->timing.d2h_bytes = (int64_t)((out_tokens ? 4 * (size_t)B * G : 0) + (out_steps ? 32 * (size_t)B * G : 0) +
+                                  32 * (size_t)B + (out_argmax ? 32 * (size_t)B : 0));
+  for (auto &k : m->prof) k = cis2b_kernel_time{0, 0.0};
+  for (const auto &pe : m->prof_events) {
+    float ms = 0;
+    CU(cudaEventElapsedTime(&ms, pe.a, pe.b));
+    int ci = class_index(pe.cls);
+    m->prof[ci].launches += 1;
+    m->prof[ci].total_ms += ms;
+  }
   return CIS2B_OK;
 }
 
@@ -726,6 +802,21 @@ int cis2b_last_timing(const cis2b_model *m, cis2b_timing *out) {
   return CIS2B_OK;
 }
 
+int cis2b_profile(cis2b_model *m, uint32_t class_mask) {
+  if (!m) return fail(CIS2B_ERR_ARG, "model is NULL");
+  if (class_mask & ~15u) return fail(CIS2B_ERR_ARG, "unknown profile class bit");
+  m->prof_mask = class_mask;
+  return CIS2B_OK;
+}
+
+int cis2b_profile_read(const cis2b_model *m, uint32_t class_bit, cis2b_kernel_time *out) {
+  if (!m || !out) return fail(CIS2B_ERR_ARG, "NULL argument");
+  int ci = class_index(class_bit);
+  if (ci < 0) return fail(CIS2B_ERR_ARG, "class_bit must be exactly one CIS2B_PROF_* bit");
+  *out = m->prof[ci];
+  return CIS2B_OK;
+}
+
 int cis2b_logits(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_rows, float *out_logits) {
   int rc = logits_impl(m, ids, n_prompt, n_rows, out_logits);
   if (rc == CIS2B_OK) g_err.clear();
@@ -738,6 +829,7 @@ void cis2b_free(cis2b_model *m) {
   if (m->s_main) cudaStreamSynchronize(m->s_main);
   if (m->s_sha) cudaStreamSynchronize(m->s_sha);
   for (cudaEvent_t e : m->ev_sha) cudaEventDestroy(e);
+  for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
   cudaEvent_t evs[] = {m->ev_sel, m->ev0, m->ev_pref, m->ev_dec, m->ev_end};
   for (cudaEvent_t e : evs)
     if (e) cudaEventDestroy(e);

@@ -80,7 +80,19 @@ typedef struct {
   double decode_ms;   /* token steps (forward + selection), main stream */
   double witness_tail_ms; /* witness work left after the last decode step */
   int64_t kernel_launches; /* kernels this library launched for the call */
+  int64_t h2d_bytes;       /* host -> device bytes copied by the call */
+  int64_t d2h_bytes;       /* device -> host bytes copied by the call */
 } cis2b_timing;
+
+/* Per-kernel-class CUDA-event timing (for roofline measurement).  Classes: */
+#define CIS2B_PROF_LM_HEAD 1u     /* lm_head GEMM (final norm output x vocab) */
+#define CIS2B_PROF_LAYER_GEMM 2u  /* q/k/v, o, gate/up and down GEMMs */
+#define CIS2B_PROF_ATTENTION 4u   /* scores + softmax + V-mix kernel */
+#define CIS2B_PROF_WITNESS 8u     /* witness SHA-256 compression chain */
+typedef struct {
+  int64_t launches;
+  double total_ms;  /* sum of per-launch event durations on the launching stream */
+} cis2b_kernel_time;
 
 /* Loads weights_dir/{model.safetensors,config.json,tokenizer.json}: hashes
  * the three artifacts, parses the config (numbers as f64, eps narrowed once),
@@ -107,6 +119,12 @@ int cis2b_generate(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *p
                    uint8_t *out_argmax);
 
 int cis2b_last_timing(const cis2b_model *m, cis2b_timing *out);
+
+/* Times every launch of the classes in `class_mask` (CIS2B_PROF_*) with a
+ * CUDA event pair in later cis2b_generate calls; 0 turns it off. */
+int cis2b_profile(cis2b_model *m, uint32_t class_mask);
+/* Totals of the last cis2b_generate for ONE class bit. */
+int cis2b_profile_read(const cis2b_model *m, uint32_t class_bit, cis2b_kernel_time *out);
 
 /* Teacher-forced logits of ONE sequence: runs ids[0 .. n_prompt+n_rows-2]
  * and writes the fp32 logits after positions n_prompt-1 .. n_prompt+n_rows-2
