@@ -896,42 +896,61 @@ __global__ void k_sha_prep(const ShaState *st, int n_seq, const float *logits, i
 
 // The chain: one thread per sequence compresses the step's blocks in order,
 // keeps the tail as the new carry and emits the per-step digest (a
-// finalised copy of the running state).
+// finalised copy of the running state).  The expanded W+K words stream
+// into shared memory through an SHA_STAGES-deep cp.async pipeline, so the
+// compression never waits on L2/HBM latency; each lane copies and reads
+// only its own slots, so no warp-level synchronisation is involved.
+constexpr int SHA_STAGES = 8;
+constexpr size_t SHA_SMEM = (size_t)SHA_STAGES * 16 * 32 * sizeof(uint4);
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(32)
 k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                const uint32_t *next_ids, const uint32_t *wk, uint8_t *digest_out, size_t digest_stride) {
-  int s = blockIdx.x * blockDim.x + threadIdx.x;
+  extern __shared__ uint4 stg[];  // [SHA_STAGES][16][32 lanes]
+  const int lane = threadIdx.x;
+  const int s = blockIdx.x * blockDim.x + lane;
   if (s >= n_seq) return;
   ShaState S = st[s];
   const int c = (int)S.carry_n;
   const int total = c + 4 * V + 4;
   const int nb = total / 64;
   const uint4 *in = reinterpret_cast<const uint4 *>(wk);
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(stg);
   uint32_t h[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) h[i] = S.h[i];
-  uint4 cur[16];
-  if (nb > 0) {
+  auto issue = [&](int j) {
+    if (j < nb) {
+      const int slot = j % SHA_STAGES;
 #pragma unroll
-    for (int qd = 0; qd < 16; ++qd) cur[qd] = in[(size_t)qd * n_seq + s];
-  }
-  for (int j = 0; j < nb; ++j) {
-    uint4 nxt[16];
-    if (j + 1 < nb) {
-#pragma unroll
-      for (int qd = 0; qd < 16; ++qd) nxt[qd] = in[((size_t)(j + 1) * 16 + qd) * n_seq + s];
+      for (int qd = 0; qd < 16; ++qd)
+        cp_async16(sbase + (uint32_t)(((slot * 16 + qd) * 32 + lane) * 16),
+                   in + ((size_t)j * 16 + qd) * n_seq + s);
     }
+    cp_async_commit();  // empty groups keep the per-thread group count uniform
+  };
+#pragma unroll
+  for (int j = 0; j < SHA_STAGES - 1; ++j) issue(j);
+  for (int j = 0; j < nb; ++j) {
+    issue(j + SHA_STAGES - 1);
+    cp_async_wait<SHA_STAGES - 1>();
+    const uint4 *src = stg + (size_t)(j % SHA_STAGES) * 16 * 32 + lane;
     uint32_t w[64];
 #pragma unroll
     for (int qd = 0; qd < 16; ++qd) {
-      w[4 * qd] = cur[qd].x; w[4 * qd + 1] = cur[qd].y; w[4 * qd + 2] = cur[qd].z; w[4 * qd + 3] = cur[qd].w;
+      uint4 v = src[qd * 32];
+      w[4 * qd] = v.x; w[4 * qd + 1] = v.y; w[4 * qd + 2] = v.z; w[4 * qd + 3] = v.w;
     }
     sha_compress_wk(h, w);
-    if (j + 1 < nb) {
-#pragma unroll
-      for (int qd = 0; qd < 16; ++qd) cur[qd] = nxt[qd];
-    }
   }
+  cp_async_wait<0>();
   // New carry = stream bytes [64*nb, total).
   const uint32_t *data = reinterpret_cast<const uint32_t *>(logits + (size_t)s * row_stride);
   const uint32_t id = next_ids[s];
@@ -963,8 +982,13 @@ void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, si
                          const uint32_t *next_ids, const uint32_t *wk_scratch, uint8_t *step_digest_out,
                          size_t digest_stride, cudaStream_t s) {
   if (n_seq <= 0) return;
-  k_sha_compress<<<(n_seq + 31) / 32, 32, 0, s>>>(st, n_seq, logits, V, row_stride, next_ids,
-                                                  wk_scratch, step_digest_out, digest_stride);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_sha_compress, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SHA_SMEM);
+    attr = true;
+  }
+  k_sha_compress<<<(n_seq + 31) / 32, 32, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
+                                                         wk_scratch, step_digest_out, digest_stride);
 }
 void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                      const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,

@@ -654,7 +654,9 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
 
   int32_t *d_step = m->d_ctl.as<int32_t>(), *d_slot = m->d_ctl.as<int32_t>() + 1;
   uint32_t *d_next = m->d_next.as<uint32_t>();
-  for (int t = 0; t < G; ++t) {
+  // Token selection for the step whose logits sit in ring slot *d_slot,
+  // then the bookkeeping that points the next forward at its position.
+  auto select = [&]() {
     if (sample)
       launch_sample(ring_base, m->V, B, d_slot, (size_t)B * V, sample->temperature, sample->top_p,
                     sample->seed, m->d_spos.as<int32_t>(), m->scratch.as<float>(), d_next, s);
@@ -663,6 +665,54 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
     launch_step_advance(d_next, B, d_step, G, m->d_tokens.as<uint32_t>(), m->d_ids_hist.as<uint32_t>(),
                         m->d_pos.as<int32_t>(), m->d_spos.as<int32_t>(), d_slot, ring, d_step, s);
     m->launches += 2;
+  };
+  // One decode step on the main stream: forward of the chosen ids, lm_head
+  // into the next ring slot, selection.  Every argument is a fixed device
+  // pointer (positions, ids, slot and step live in device memory), so the
+  // step is captured once as a CUDA graph and replayed.
+  auto step_body = [&]() -> int {
+    int r = forward_rows(m, B, d_next, m->d_seq.as<int32_t>(), m->d_pos.as<int32_t>(), B, maxP);
+    if (r) return r;
+    r = head_rows(m, m->h.as<float>(), B, ring_base, d_slot, (size_t)B * V);
+    if (r) return r;
+    select();
+    return CIS2B_OK;
+  };
+  const uint32_t in_graph = CIS2B_PROF_LM_HEAD | CIS2B_PROF_LAYER_GEMM | CIS2B_PROF_ATTENTION;
+  const bool use_graph = G >= 3 && !(m->prof_mask & in_graph);
+  cudaGraphExec_t gexec = nullptr;
+  int64_t step_launches = 0;
+  if (use_graph) {
+    cudaGraph_t g = nullptr;
+    const int64_t l0 = m->launches;
+    CU(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    rc = step_body();
+    cudaError_t ce = cudaStreamEndCapture(s, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (ce != cudaSuccess) return fail(CIS2B_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    ce = cudaGraphInstantiate(&gexec, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(CIS2B_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+    step_launches = m->launches - l0;
+    m->launches = l0;
+  }
+  struct GraphGuard {
+    cudaGraphExec_t e;
+    ~GraphGuard() { if (e) cudaGraphExecDestroy(e); }
+  } guard{gexec};
+  for (int t = 0; t < G; ++t) {
+    if (t == 0) {
+      select();
+    } else {
+      if (t >= ring) CU(cudaStreamWaitEvent(s, m->ev_sha[(size_t)(t % ring)], 0));
+      if (use_graph) {
+        CU(cudaGraphLaunch(gexec, s));
+        m->launches += step_launches;
+      } else {
+        rc = step_body();
+        if (rc) return rc;
+      }
+    }
     CU(cudaEventRecord(m->ev_sel, s));
     CU(cudaStreamWaitEvent(ss, m->ev_sel, 0));
     launch_sha_prep(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
@@ -675,14 +725,8 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
     }
     m->launches += 2;
     CU(cudaEventRecord(m->ev_sha[(size_t)(t % ring)], ss));
-    if (t + 1 < G) {
-      if (t + 1 >= ring) CU(cudaStreamWaitEvent(s, m->ev_sha[(size_t)((t + 1) % ring)], 0));
-      rc = forward_rows(m, B, d_next, m->d_seq.as<int32_t>(), m->d_pos.as<int32_t>(), B, maxP);
-      if (rc) return rc;
-      rc = head_rows(m, m->h.as<float>(), B, ring_base, d_slot, (size_t)B * V);
-      if (rc) return rc;
-    }
   }
+  CU_LAUNCHED();
   CU(cudaEventRecord(m->ev_dec, s));
   // Join the witness stream; the final digest and the argmax digest run on
   // the main stream after its last step.
