@@ -372,16 +372,46 @@ static void run_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, i
                                                       y_slot_stride);
 }
 
-// Tile choice: the largest tile that still gives >= 2 CTAs per SM without
-// wasting more than half of a row tile; small problems fall back to one
-// output per thread so that every SM has dot products to walk.
+// Tile choice.  No dot product may be split, so a GEMM of M rows and N
+// outputs has exactly M*N serial chains to spread over 148 SMs x 4
+// schedulers.  Each candidate tile is scored by the issue cycles of the
+// busiest SM: its CTAs' MACs, divided by the fraction of issue slots that are
+// FP32 work (2*TM*TN FP ops against the shared-memory loads per k), over
+// the schedulers its warps can occupy.  Small decode GEMMs get one or two
+// outputs per thread so that all SMs walk chains; large ones get 4x8
+// register tiles.
+struct TileCfg { int bm, bn, tm, tn; };
+static double tile_cost(const TileCfg &c, int M, int N, int K) {
+  const long ctas = (long)((N + c.bn - 1) / c.bn) * ((M + c.bm - 1) / c.bm);
+  const int threads = (c.bm / c.tm) * (c.bn / c.tn);
+  const long per_sm = (ctas + 147) / 148;
+  const double fp = 2.0 * c.tm * c.tn;
+  const double loads = (c.tm + 3) / 4 + (c.tn + 3) / 4;
+  const double eff = fp / (fp + loads);
+  const double warps = (double)per_sm * threads / 32.0;
+  const double sched = warps < 4.0 ? warps : 4.0;
+  const double issue = (double)per_sm * c.bm * c.bn * K * 2.0 / eff / (32.0 * sched);
+  const double chain = 4.0 * K * (c.tm * c.tn > 4 ? 1.0 : 1.0);  // dependent-add floor per thread
+  return issue > chain ? issue : chain;
+}
+
 void launch_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
                  const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
-  const long target = 2 * 148;
-  auto ctas = [&](int bm, int bn) { return (long)((N + bn - 1) / bn) * ((M + bm - 1) / bm); };
-  auto fits = [&](int bm) { return M >= bm / 2 || bm == 1; };
+  static const TileCfg cands[] = {{64, 128, 4, 8}, {32, 64, 2, 4}, {16, 64, 1, 4}, {64, 4, 2, 1},
+                                  {32, 8, 2, 1},   {16, 16, 2, 1}, {8, 32, 2, 1},  {4, 64, 1, 1},
+                                  {1, 256, 1, 1}};
+  int best = -1;
+  double best_cost = 0;
+  for (int i = 0; i < (int)(sizeof(cands) / sizeof(cands[0])); ++i) {
+    const TileCfg &c = cands[i];
+    if (tree && c.tm * c.tn > 8) continue;       // tree mode keeps 5 pending levels per output
+    if (c.bm > 1 && M < c.bm / 2) continue;      // at most half a row tile wasted
+    if (c.bm == 1 && M > 3) continue;
+    double cost = tile_cost(c, M, N, K);
+    if (best < 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
+  }
 #define CIS2B_GEMM(BM_, BN_, TM_, TN_)                                                         \
   do {                                                                                         \
     if (tree)                                                                                  \
@@ -392,13 +422,37 @@ void launch_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M
                                           y_slot_stride, s);                                  \
     return;                                                                                    \
   } while (0)
-  if (!tree && fits(64) && ctas(64, 128) >= target) CIS2B_GEMM(64, 128, 4, 8);
-  if (fits(32) && ctas(32, 64) >= target) CIS2B_GEMM(32, 64, 2, 4);
-  if (fits(16) && ctas(16, 64) >= target) CIS2B_GEMM(16, 64, 1, 4);
-  if (fits(8) && ctas(8, 64) >= target) CIS2B_GEMM(8, 64, 1, 2);
-  if (M >= 4) CIS2B_GEMM(4, 64, 1, 1);
+  switch (best) {
+    case 0: if (!tree) CIS2B_GEMM(64, 128, 4, 8); break;
+    case 1: CIS2B_GEMM(32, 64, 2, 4);
+    case 2: CIS2B_GEMM(16, 64, 1, 4);
+    case 3: CIS2B_GEMM(64, 4, 2, 1);
+    case 4: CIS2B_GEMM(32, 8, 2, 1);
+    case 5: CIS2B_GEMM(16, 16, 2, 1);
+    case 6: CIS2B_GEMM(8, 32, 2, 1);
+    case 7: CIS2B_GEMM(4, 64, 1, 1);
+    default: break;
+  }
   CIS2B_GEMM(1, 256, 1, 1);
 #undef CIS2B_GEMM
+}
+
+// Chosen tile for a shape (for tests and tuning).
+int gemm_tile_choice(int M, int N, int K, bool tree) {
+  static const TileCfg cands[] = {{64, 128, 4, 8}, {32, 64, 2, 4}, {16, 64, 1, 4}, {64, 4, 2, 1},
+                                  {32, 8, 2, 1},   {16, 16, 2, 1}, {8, 32, 2, 1},  {4, 64, 1, 1},
+                                  {1, 256, 1, 1}};
+  int best = -1;
+  double best_cost = 0;
+  for (int i = 0; i < 9; ++i) {
+    const TileCfg &c = cands[i];
+    if (tree && c.tm * c.tn > 8) continue;
+    if (c.bm > 1 && M < c.bm / 2) continue;
+    if (c.bm == 1 && M > 3) continue;
+    double cost = tile_cost(c, M, N, K);
+    if (best < 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
+  }
+  return best;
 }
 
 // ============================================================ attention
@@ -460,92 +514,147 @@ __device__ __forceinline__ float max_comb(float a, float b) {
   return (b > a) ? b : a;
 }
 
-// One CTA per (row, query head): scores (dot * scale, cis2_model.h:571-585),
-// softmax (max scan, pinned exp, pinned-order denominator, divide;
-// cis2_math.h:442-467), V-mix serial over key positions (cis2_model.h:599-617).
+// One CTA per (row, KV head), covering the G = n_heads / n_kv query heads
+// that share it (GQA), so each key/value row crosses HBM once per row:
+//   scores  q_g . k_j * scale          (cis2_model.h:571-585; scale after the dot)
+//   softmax strict-'>' max, pinned exp, pinned-order denominator, divide
+//                                      (cis2_math.h:442-467)
+//   V-mix   acc = acc + p_j * v_j[d], j ascending, both modes
+//                                      (cis2_model.h:599-617)
+// K and V stream through shared memory in chunks of ATT_JC positions
+// (coalesced loads); one thread owns each (head, position) dot product and
+// each (head, d) V-mix chain.
+constexpr int ATT_JC = 64;
+
+size_t attention_smem_floats(int G, int hd, int max_len) {
+  return (size_t)G * hd + (size_t)G * max_len + (size_t)G * (max_len / 32 + 1) + 64 +
+         (size_t)ATT_JC * (hd + 1);
+}
+
 __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
                             int nh, int nkv, int hd, const float *kc, const float *vc, int max_pos,
                             int tree, float *att, int ld_att, int max_len) {
   extern __shared__ float sm[];
-  const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+  const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+  const int G = nh / nkv, KV = nkv * hd;
   const int seq = rseq[r], pos = rpos[r], len = pos + 1;
-  const int group = nh / nkv, kvh = h / group, KV = nkv * hd;
-  float *q = sm;                 // [hd]
-  float *sc = q + hd;            // [max_len]
-  float *part = sc + max_len;    // [max_len/32 + 1]
-  float *red = part + (max_len / 32 + 1);  // [32]
-  for (int d = tid; d < hd; d += nt) q[d] = qkv[(size_t)r * ld + (size_t)h * hd + d];
-  __syncthreads();
+  const int nb = (len + 31) / 32;
+  float *q = sm;                              // [G][hd]
+  float *sc = q + G * hd;                     // [G][max_len]
+  float *part = sc + (size_t)G * max_len;     // [G][max_len/32 + 1]
+  float *red = part + (size_t)G * (max_len / 32 + 1);  // [64]
+  float *tile = red + 64;                     // [ATT_JC][hd + 1]
+  const int tstride = hd + 1;
+  for (int i = tid; i < G * hd; i += nt) q[i] = qkv[(size_t)r * ld + (size_t)kvh * G * hd + i];
   const float scale = rsqrt_cr(__int2float_rn(hd));
   const float *kbase = kc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
-  for (int j = tid; j < len; j += nt) {
-    const float *kj = kbase + (size_t)j * KV;
-    float d = tree ? dot_tree(q, kj, hd) : dot_seq(q, kj, hd);
-    sc[j] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
-  }
-  __syncthreads();
-  // max
-  float m = bitsf(0x7fc00000u);
-  for (int j = tid; j < len; j += nt) m = max_comb(m, sc[j]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = max_comb(m, __shfl_xor_sync(FULL, m, o));
-  if ((tid & 31) == 0) red[tid >> 5] = m;
-  __syncthreads();
-  if (tid == 0) {
-    float mm = red[0];
-    for (int w = 1; w < nt / 32; ++w) mm = max_comb(mm, red[w]);
-    if (is_nan(sc[0])) mm = sc[0];
-    red[0] = mm;
-  }
-  __syncthreads();
-  const float mx = red[0];
-  for (int j = tid; j < len; j += nt) sc[j] = exp_pinned(fsub(sc[j], mx));
-  __syncthreads();
-  if (!tree) {
-    if (tid == 0) {
-      float acc = 0.0f;
-      for (int j = 0; j < len; ++j) acc = fadd(acc, sc[j]);
-      red[1] = acc;
-    }
-  } else {
-    const int nb = (len + 31) / 32, warp = tid >> 5, lane = tid & 31;
-    for (int b = warp; b < nb; b += nt / 32) {
-      int j = b * 32 + lane;
-      float v = warp_tree32(j < len ? sc[j] : 0.0f);
-      if (lane == 0) part[b] = v;
+  const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
+
+  // ---- scores
+  for (int j0 = 0; j0 < len; j0 += ATT_JC) {
+    const int jc = min(ATT_JC, len - j0);
+    __syncthreads();
+    for (int i = tid; i < jc * hd; i += nt) {
+      int jj = i / hd, dd = i - jj * hd;
+      tile[jj * tstride + dd] = kbase[(size_t)(j0 + jj) * KV + dd];
     }
     __syncthreads();
-    if (tid == 0) {
-      float acc = 0.0f;
-      for (int b = 0; b < nb; ++b) acc = fadd(acc, part[b]);
-      red[1] = acc;
+    for (int pr = tid; pr < G * jc; pr += nt) {
+      const int g = pr / jc, jj = pr - g * jc;
+      const float *qg = q + g * hd, *kj = tile + jj * tstride;
+      float d;
+      if (!tree) {
+        d = 0.0f;
+        for (int i = 0; i < hd; ++i) d = fadd(d, fmul(qg[i], kj[i]));
+      } else {
+        d = dot_tree(qg, kj, hd);
+      }
+      sc[(size_t)g * max_len + j0 + jj] = fmul(d, scale);
     }
   }
   __syncthreads();
-  const float den = red[1];
-  for (int j = tid; j < len; j += nt) sc[j] = fdiv(sc[j], den);
-  __syncthreads();
-  const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
-  for (int d = tid; d < hd; d += nt) {
-    float acc = 0.0f;
-    for (int j = 0; j < len; ++j) acc = fadd(acc, fmul(sc[j], vbase[(size_t)j * KV + d]));
-    att[(size_t)r * ld_att + (size_t)h * hd + d] = acc;
+  // ---- max per head (serial-scan semantics, see max_comb)
+  for (int g = warp; g < G; g += nw) {
+    const float *sg = sc + (size_t)g * max_len;
+    float m = bitsf(0x7fc00000u);
+    for (int j = lane; j < len; j += 32) m = max_comb(m, sg[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max_comb(m, __shfl_xor_sync(FULL, m, o));
+    if (lane == 0) red[g] = is_nan(sg[0]) ? sg[0] : m;
   }
+  __syncthreads();
+  for (int i = tid; i < G * len; i += nt) {
+    const int g = i / len, j = i - g * len;
+    float *p = sc + (size_t)g * max_len + j;
+    *p = exp_pinned(fsub(*p, red[g]));
+  }
+  __syncthreads();
+  // ---- denominators
+  if (tree) {
+    for (int pb = warp; pb < G * nb; pb += nw) {
+      const int g = pb / nb, b = pb - g * nb, j = b * 32 + lane;
+      float v = warp_tree32(j < len ? sc[(size_t)g * max_len + j] : 0.0f);
+      if (lane == 0) part[(size_t)g * (max_len / 32 + 1) + b] = v;
+    }
+    __syncthreads();
+  }
+  for (int g = warp; g < G; g += nw) {
+    if (lane == 0) {
+      float acc = 0.0f;
+      if (!tree) {
+        const float *sg = sc + (size_t)g * max_len;
+        for (int j = 0; j < len; ++j) acc = fadd(acc, sg[j]);
+      } else {
+        const float *pg = part + (size_t)g * (max_len / 32 + 1);
+        for (int b = 0; b < nb; ++b) acc = fadd(acc, pg[b]);
+      }
+      red[32 + g] = acc;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * len; i += nt) {
+    const int g = i / len, j = i - g * len;
+    float *p = sc + (size_t)g * max_len + j;
+    *p = fdiv(*p, red[32 + g]);
+  }
+  // ---- V-mix
+  const int gd = tid;                  // (g, d) chain owned by this thread
+  const int g = gd / hd, d = gd - (gd / hd) * hd;
+  const bool owns = gd < G * hd;
+  float acc = 0.0f;
+  for (int j0 = 0; j0 < len; j0 += ATT_JC) {
+    const int jc = min(ATT_JC, len - j0);
+    __syncthreads();
+    for (int i = tid; i < jc * hd; i += nt) {
+      int jj = i / hd, dd = i - jj * hd;
+      tile[jj * hd + dd] = vbase[(size_t)(j0 + jj) * KV + dd];
+    }
+    __syncthreads();
+    if (owns) {
+      const float *pg = sc + (size_t)g * max_len + j0;
+      for (int jj = 0; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * hd + d]));
+    }
+  }
+  if (owns) att[(size_t)r * ld_att + ((size_t)kvh * G + g) * hd + d] = acc;
 }
 
 void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
                       const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
                       int ld_att, int max_len, cudaStream_t s) {
   if (rows <= 0) return;
-  size_t smem = (size_t)(hd + max_len + max_len / 32 + 1 + 32) * sizeof(float);
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
+  const int G = n_heads / n_kv;
+  int nt = ((G * hd + 31) / 32) * 32;
+  if (nt < 128) nt = 128;
+  size_t smem = attention_smem_floats(G, hd, max_len) * sizeof(float);
+  static size_t attr = 48 * 1024;
+  if (smem > attr) {
     cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr = smem;
   }
-  dim3 grid(rows, n_heads);
-  k_attention<<<grid, 128, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache,
-                                      max_pos, tree ? 1 : 0, att, ld_att, max_len);
+  dim3 grid(rows, n_kv);
+  k_attention<<<grid, nt, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache, max_pos,
+                                     tree ? 1 : 0, att, ld_att, max_len);
 }
 
 // ============================================================ token selection
@@ -900,8 +1009,17 @@ __global__ void k_sha_prep(const ShaState *st, int n_seq, const float *logits, i
 // into shared memory through an SHA_STAGES-deep cp.async pipeline, so the
 // compression never waits on L2/HBM latency; each lane copies and reads
 // only its own slots, so no warp-level synchronisation is involved.
-constexpr int SHA_STAGES = 8;
-constexpr size_t SHA_SMEM = (size_t)SHA_STAGES * 16 * 32 * sizeof(uint4);
+//
+// The chain is issue-bound (~14 integer instructions per round, one warp),
+// so a chain warp must not share its scheduler with forward-pass warps: a
+// CTA holds up to 4 chain warps (one per SM sub-partition) and asks for the
+// whole shared memory of the SM, which keeps every other kernel's CTAs off
+// that SM while the witness runs.
+constexpr int SHA_WARPS = 4;
+constexpr int SHA_STAGES = 7;
+constexpr size_t SHA_STAGE_BYTES = (size_t)16 * 32 * sizeof(uint4);          // one block, 32 chains
+constexpr size_t SHA_SMEM = (size_t)227 * 1024;                              // SM's maximum per CTA
+static_assert(SHA_WARPS * SHA_STAGES * SHA_STAGE_BYTES <= SHA_SMEM, "witness pipeline exceeds smem");
 
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
@@ -910,12 +1028,13 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(32 * SHA_WARPS)
 k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                const uint32_t *next_ids, const uint32_t *wk, uint8_t *digest_out, size_t digest_stride) {
-  extern __shared__ uint4 stg[];  // [SHA_STAGES][16][32 lanes]
-  const int lane = threadIdx.x;
-  const int s = blockIdx.x * blockDim.x + lane;
+  extern __shared__ uint4 smem_all[];  // [warp][SHA_STAGES][16][32 lanes]
+  const int lane = threadIdx.x & 31;
+  uint4 *stg = smem_all + (size_t)(threadIdx.x >> 5) * SHA_STAGES * 16 * 32;
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= n_seq) return;
   ShaState S = st[s];
   const int c = (int)S.carry_n;
@@ -987,8 +1106,11 @@ void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, si
     cudaFuncSetAttribute(k_sha_compress, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SHA_SMEM);
     attr = true;
   }
-  k_sha_compress<<<(n_seq + 31) / 32, 32, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
-                                                         wk_scratch, step_digest_out, digest_stride);
+  const int warps = (n_seq + 31) / 32;
+  const int per_cta = warps < SHA_WARPS ? warps : SHA_WARPS;
+  const int ctas = (warps + per_cta - 1) / per_cta;
+  k_sha_compress<<<ctas, 32 * per_cta, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
+                                                      wk_scratch, step_digest_out, digest_stride);
 }
 void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                      const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,

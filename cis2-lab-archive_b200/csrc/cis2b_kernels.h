@@ -43,6 +43,10 @@ void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n
 void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
                       const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
                       int ld_att, int max_len, cudaStream_t s);
+// Shared memory (floats) the attention kernel needs; G = n_heads / n_kv.
+size_t attention_smem_floats(int G, int hd, int max_len);
+// Index of the GEMM tile the dispatcher picks for (M, N, K).
+int gemm_tile_choice(int M, int N, int K, bool tree);
 void launch_silu_mul(const float *gu, int I, int rows, float *hid, cudaStream_t s);
 void launch_add_bias(float *x, int ld, int rows, const uint16_t *b, int n, cudaStream_t s);
 
