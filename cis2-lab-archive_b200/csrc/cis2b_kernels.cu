@@ -57,19 +57,35 @@ __device__ __forceinline__ float dot_tree(const float *a, const float *b, int n)
   return acc;
 }
 
+// Strict left-to-right sum of a[0..n) from +0 by ONE thread.  Operands
+// are fetched 16 at a time ahead of the dependent adds, so the chain runs
+// at add latency rather than load latency.
+__device__ __forceinline__ float serial_sum(const float *a, int n) {
+  float acc = 0.0f;
+  int i = 0;
+  for (; i + 16 <= n; i += 16) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = a[i + u];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) acc = fadd(acc, v[u]);
+  }
+  for (; i < n; ++i) acc = fadd(acc, a[i]);
+  return acc;
+}
+
 // RMSNorm of one row by one warp (cis2_model.h:511-523):
 // sq = x*x; ss = fold(sq); mean = ss/n; inv = 1/sqrt(mean+eps); out = (x*inv)*w.
-// `sq` is warp-private scratch of n floats.  out may alias x.
+// `sq` is warp-private scratch of n floats.  out (element stride os) may alias x.
 __device__ __forceinline__ void warp_rmsnorm(const float *x, const uint16_t *w, float eps, int n,
-                                             bool tree, float *sq, float *out) {
+                                             bool tree, float *sq, float *out, int os = 1) {
   const int lane = threadIdx.x & 31;
   float ss;
   if (!tree) {
     for (int i = lane; i < n; i += 32) sq[i] = fmul(x[i], x[i]);
     __syncwarp();
     float acc = 0.0f;
-    if (lane == 0)
-      for (int i = 0; i < n; ++i) acc = fadd(acc, sq[i]);
+    if (lane == 0) acc = serial_sum(sq, n);
     ss = __shfl_sync(FULL, acc, 0);
   } else {
     float acc = 0.0f;
@@ -82,7 +98,7 @@ __device__ __forceinline__ void warp_rmsnorm(const float *x, const uint16_t *w, 
   float mean = fdiv(ss, __int2float_rn(n));
   float inv = rsqrt_cr(fadd(mean, eps));
   __syncwarp();
-  for (int i = lane; i < n; i += 32) out[i] = fmul(fmul(x[i], inv), widen_bf16(w[i]));
+  for (int i = lane; i < n; i += 32) out[(size_t)i * os] = fmul(fmul(x[i], inv), widen_bf16(w[i]));
   __syncwarp();
 }
 
@@ -131,33 +147,33 @@ void launch_embed(const uint16_t *E, int H, const uint32_t *tokens, int rows, fl
 }
 
 __global__ void k_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows,
-                          int tree, float *out, int ldo) {
+                          int tree, float *out, int ors, int ocs) {
   extern __shared__ float sm[];
   int warp = threadIdx.x >> 5;
   int r = blockIdx.x * (blockDim.x >> 5) + warp;
   if (r >= rows) return;
   warp_rmsnorm(x + (size_t)r * ldx, w, eps, n, tree != 0, sm + (size_t)warp * n,
-               out + (size_t)r * ldo);
+               out + (size_t)r * ors, ocs);
 }
 void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
-                    float *out, int ldo, cudaStream_t s) {
+                    float *out, int ors, int ocs, cudaStream_t s) {
   if (rows <= 0) return;
   const int wpb = 4;
   k_rmsnorm<<<(rows + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * n * sizeof(float), s>>>(
-      x, ldx, w, eps, n, rows, tree ? 1 : 0, out, ldo);
+      x, ldx, w, eps, n, rows, tree ? 1 : 0, out, ors, ocs);
 }
 
-__global__ void k_silu_mul(const float *gu, int I, int rows, float *hid) {
+__global__ void k_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs) {
   size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (size_t)rows * I) return;
   size_t r = idx / I, i = idx % I;
   const float *row = gu + r * 2 * (size_t)I;
-  hid[idx] = fmul(silu_pinned(row[i]), row[I + i]);  // silu(g)*up (cis2_model.h:619-623)
+  hid[r * hrs + i * hcs] = fmul(silu_pinned(row[i]), row[I + i]);  // silu(g)*up (cis2_model.h:619-623)
 }
-void launch_silu_mul(const float *gu, int I, int rows, float *hid, cudaStream_t s) {
+void launch_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs, cudaStream_t s) {
   size_t n = (size_t)rows * I;
   if (!n) return;
-  k_silu_mul<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(gu, I, rows, hid);
+  k_silu_mul<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(gu, I, rows, hid, hrs, hcs);
 }
 
 __global__ void k_add_bias(float *x, int ld, int rows, const uint16_t *b, int n) {
@@ -194,89 +210,63 @@ void launch_pinned_map(int fn, const float *x, float *y, size_t n, cudaStream_t 
 
 // ============================================================ GEMM
 //
-// Y[m][n] = dot(W[n][:], X[m][:]).  One thread owns a TM x TN tile of
-// outputs and walks k = 0..K-1 in order for all of them: the register
-// tiling reuses smem loads across outputs without ever splitting a dot
-// product.  W arrives as bf16 and is widened exactly (bits << 16) while it
-// is staged into shared memory, so HBM carries half the reference's fp32
-// bytes.  Padding past K contributes +0 products, which leave a sequential
-// accumulator unchanged (it starts at +0 and can never be -0) and are the
-// spec's own zero leaves in tree mode.
-template <int BM, int BN, int TM, int TN, bool TREE>
-__global__ void __launch_bounds__((BM / TM) * (BN / TN))
-k_gemm(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ W, int K, int N, int M,
-       float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
-       size_t y_slot_stride) {
-  constexpr int NT = (BM / TM) * (BN / TN);
-  constexpr int BK = 32;
-  constexpr int WS = BN + 4;  // smem row strides (floats), keep 16-byte alignment
-  constexpr int XS = BM + 4;
-  constexpr int WCH = (BN * 4 + NT - 1) / NT;  // 16-byte W chunks per thread
-  constexpr int XCH = (BM * 8 + NT - 1) / NT;  // 16-byte X chunks per thread
-  extern __shared__ __align__(16) float smem[];
-  float *Ws = smem;                 // [2][BK][WS]
-  float *Xs = smem + 2 * BK * WS;   // [2][BK][XS]
+// Y[m][n] = dot(W[n][:], X[m][:]) for M activation rows and N outputs.
+// One thread owns a TM x TN tile of outputs and walks k = 0..K-1 in order
+// for all of them: register tiling shares shared-memory loads between
+// outputs without ever splitting a dot product.
+//
+// Operand layouts (chosen so every tile is a run of 16-byte chunks that
+// cp.async can move without a register round trip):
+//   X^T  [K][ldm] fp32   activations k-major (the producing kernels write it)
+//   Wp   [N8][K][8] bf16 weights in 8-row k-major panels, re-laid once at
+//                        load from the checkpoint's [N][K] (same bf16 bits)
+// STAGES k-tiles of 32 are in flight; the widen bits<<16 happens as a
+// thread reads its weights.  Padding past K or N is zero-filled by cp.async:
+// a +0 product leaves a sequential accumulator unchanged (it starts at +0
+// and can never become -0) and is the spec's own zero leaf in tree mode.
+constexpr int GEMM_KT = 32;
+constexpr int GEMM_STAGES = 4;
 
+__device__ __forceinline__ void cp_async16_zfill(uint32_t saddr, const void *g, bool valid) {
+  const int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "r"(sz) : "memory");
+}
+
+template <int BM, int BP, int TM, int TN, bool TREE>
+__global__ void __launch_bounds__((BM / TM) * (8 * BP / TN))
+k_gemm_t(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp, int K, int N, int M,
+         float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
+         size_t y_slot_stride) {
+  constexpr int BN = 8 * BP;
+  constexpr int NT = (BM / TM) * (BN / TN);
+  constexpr int XF = GEMM_KT * BM;            // floats per X stage
+  constexpr int WH = GEMM_KT * BN;            // bf16 per W stage
+  constexpr int XCH = GEMM_KT * BM / 4;       // 16-byte chunks per X stage
+  constexpr int WCH = GEMM_KT * BP;           // 16-byte chunks per W stage
+  extern __shared__ __align__(16) float smem[];
+  float *Xs = smem;                                                  // [S][KT][BM]
+  uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + GEMM_STAGES * XF);  // [S][KT][BP][8]
   const int tid = threadIdx.x;
   const int tn = tid % (BN / TN), tm = tid / (BN / TN);
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int n8_0 = blockIdx.x * BP, m0 = blockIdx.y * BM;
+  const int N8 = (N + 7) / 8;
+  const uint32_t xs_base = (uint32_t)__cvta_generic_to_shared(Xs);
+  const uint32_t ws_base = (uint32_t)__cvta_generic_to_shared(Ws);
 
-  uint4 wreg[WCH];
-  float4 xreg[XCH];
-  auto gload = [&](int k0) {
-#pragma unroll
-    for (int c = 0; c < WCH; ++c) {
-      int id = tid + c * NT;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (id < BN * 4) {
-        int r = id >> 2, k = k0 + (id & 3) * 8, n = n0 + r;
-        if (n < N && k < K) v = __ldg(reinterpret_cast<const uint4 *>(W + (size_t)n * K + k));
-      }
-      wreg[c] = v;
+  auto issue = [&](int kt) {
+    const int slot = kt % GEMM_STAGES, k0 = kt * GEMM_KT;
+    for (int c = tid; c < XCH; c += NT) {
+      const int k = c / (BM / 4), q = c % (BM / 4);
+      const bool ok = (k0 + k < K) && (m0 + 4 * q < ldm);
+      const float *src = ok ? XT + (size_t)(k0 + k) * ldm + m0 + 4 * q : XT;
+      cp_async16_zfill(xs_base + (uint32_t)((slot * XF + k * BM + 4 * q) * 4), src, ok);
     }
-#pragma unroll
-    for (int c = 0; c < XCH; ++c) {
-      int id = tid + c * NT;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (id < BM * 8) {
-        int r = id >> 3, k = k0 + (id & 7) * 4, m = m0 + r;
-        if (m < M && k < K) v = *reinterpret_cast<const float4 *>(X + (size_t)m * ldx + k);
-      }
-      xreg[c] = v;
+    for (int c = tid; c < WCH; c += NT) {
+      const int k = c / BP, p = c % BP;
+      const bool ok = (k0 + k < K) && (n8_0 + p < N8);
+      const uint16_t *src = ok ? Wp + ((size_t)(n8_0 + p) * K + k0 + k) * 8 : Wp;
+      cp_async16_zfill(ws_base + (uint32_t)((slot * WH + (k * BP + p) * 8) * 2), src, ok);
     }
-  };
-  auto sstore = [&](int buf) {
-    float *ws = Ws + buf * BK * WS;
-    float *xs = Xs + buf * BK * XS;
-#pragma unroll
-    for (int c = 0; c < WCH; ++c) {
-      int id = tid + c * NT;
-      if (id < BN * 4) {
-        int r = id >> 2, q = (id & 3) * 8;
-        uint32_t u[4] = {wreg[c].x, wreg[c].y, wreg[c].z, wreg[c].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          ws[(q + 2 * e) * WS + r] = __uint_as_float(u[e] << 16);
-          ws[(q + 2 * e + 1) * WS + r] = __uint_as_float(u[e] & 0xffff0000u);
-        }
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < XCH; ++c) {
-      int id = tid + c * NT;
-      if (id < BM * 8) {
-        int r = id >> 3, q = (id & 7) * 4;
-        xs[(q + 0) * XS + r] = xreg[c].x;
-        xs[(q + 1) * XS + r] = xreg[c].y;
-        xs[(q + 2) * XS + r] = xreg[c].z;
-        xs[(q + 3) * XS + r] = xreg[c].w;
-      }
-    }
-  };
-  // Column owned by output j of this thread.
-  auto ncol = [&](int j) -> int {
-    if (TN == 8) return (j < 4) ? tn * 4 + j : BN / 2 + tn * 4 + (j - 4);
-    return tn * TN + j;
   };
 
   float acc[TM][TN];
@@ -285,23 +275,30 @@ k_gemm(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ W, int
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
 
-  gload(0);
-  sstore(0);
-  __syncthreads();
-  const int nk = (K + BK - 1) / BK;
+  const int nk = (K + GEMM_KT - 1) / GEMM_KT;
+#pragma unroll
+  for (int s = 0; s < GEMM_STAGES - 1; ++s) {
+    if (s < nk) issue(s);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  const int nl0 = tn * TN;                     // first output column of this thread (within BN)
+  const int wp = nl0 / 8, wj = nl0 % 8;        // panel and lane within the panel
   for (int kt = 0; kt < nk; ++kt) {
-    const int buf = kt & 1;
-    if (kt + 1 < nk) gload((kt + 1) * BK);
-    const float *ws = Ws + buf * BK * WS;
-    const float *xs = Xs + buf * BK * XS;
+    asm volatile("cp.async.wait_group %0;" ::"n"(GEMM_STAGES - 2) : "memory");
+    __syncthreads();
+    if (kt + GEMM_STAGES - 1 < nk) issue(kt + GEMM_STAGES - 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const int slot = kt % GEMM_STAGES;
+    const float *xs = Xs + slot * XF + tm * TM;
+    const uint16_t *ws = Ws + slot * WH + wp * 8 + wj;
     if (!TREE) {
-#pragma unroll 4
-      for (int kk = 0; kk < BK; ++kk) {
-        float w[TN], x[TM];
+#pragma unroll 8
+      for (int kk = 0; kk < GEMM_KT; ++kk) {
+        float x[TM], w[TN];
 #pragma unroll
-        for (int j = 0; j < TN; ++j) w[j] = ws[kk * WS + ncol(j)];
+        for (int i = 0; i < TM; ++i) x[i] = xs[kk * BM + i];
 #pragma unroll
-        for (int i = 0; i < TM; ++i) x[i] = xs[kk * XS + tm * TM + i];
+        for (int j = 0; j < TN; ++j) w[j] = widen_bf16(ws[kk * BN + j]);
 #pragma unroll
         for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -309,16 +306,16 @@ k_gemm(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ W, int
       }
     } else {
       // Streaming pairwise tree over the 32 leaves of this k tile: level L
-      // keeps the pending left operand; leaf kk closes as many levels as kk
+      // holds the pending left operand; leaf kk closes as many levels as kk
       // has trailing one bits.  Same adds, same operands as tree32.
       float lv[5][TM][TN];
 #pragma unroll
-      for (int kk = 0; kk < BK; ++kk) {
-        float w[TN], x[TM];
+      for (int kk = 0; kk < GEMM_KT; ++kk) {
+        float x[TM], w[TN];
 #pragma unroll
-        for (int j = 0; j < TN; ++j) w[j] = ws[kk * WS + ncol(j)];
+        for (int i = 0; i < TM; ++i) x[i] = xs[kk * BM + i];
 #pragma unroll
-        for (int i = 0; i < TM; ++i) x[i] = xs[kk * XS + tm * TM + i];
+        for (int j = 0; j < TN; ++j) w[j] = widen_bf16(ws[kk * BN + j]);
 #pragma unroll
         for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -335,18 +332,17 @@ k_gemm(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ W, int
           }
       }
     }
-    if (kt + 1 < nk) sstore(buf ^ 1);
-    __syncthreads();
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 
   float *Yb = Y + (y_slot ? (size_t)(*y_slot) * y_slot_stride : 0);
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
-    int m = m0 + tm * TM + i;
+    const int m = m0 + tm * TM + i;
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < TN; ++j) {
-      int n = n0 + ncol(j);
+      const int n = n8_0 * 8 + nl0 + j;
       if (n >= N) continue;
       float v = acc[i][j];
       if (R) v = fadd(R[(size_t)m * ldr + n], v);  // residual h + o (cis2_model.h:540-542)
@@ -355,105 +351,100 @@ k_gemm(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ W, int
   }
 }
 
-template <int BM, int BN, int TM, int TN, bool TREE>
-static void run_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
-                     const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride,
-                     cudaStream_t s) {
-  constexpr int NT = (BM / TM) * (BN / TN);
-  size_t smem = (size_t)2 * 32 * ((BN + 4) + (BM + 4)) * sizeof(float);
+template <int BM, int BP, int TM, int TN, bool TREE>
+static void run_gemm_t(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
+                       const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s) {
+  constexpr int NT = (BM / TM) * (8 * BP / TN);
+  const size_t smem = (size_t)GEMM_STAGES * (GEMM_KT * BM * 4 + GEMM_KT * 8 * BP * 2);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm<BM, BN, TM, TN, TREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_gemm_t<BM, BP, TM, TN, TREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
     attr_set = true;
   }
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  k_gemm<BM, BN, TM, TN, TREE><<<grid, NT, smem, s>>>(X, ldx, W, K, N, M, Y, ldy, R, ldr, y_slot,
-                                                      y_slot_stride);
+  dim3 grid((N + 8 * BP - 1) / (8 * BP), (M + BM - 1) / BM);
+  k_gemm_t<BM, BP, TM, TN, TREE><<<grid, NT, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot,
+                                                          y_slot_stride);
 }
 
 // Tile choice.  No dot product may be split, so a GEMM of M rows and N
 // outputs has exactly M*N serial chains to spread over 148 SMs x 4
-// schedulers.  Each candidate tile is scored by the issue cycles of the
-// busiest SM: its CTAs' MACs, divided by the fraction of issue slots that are
-// FP32 work (2*TM*TN FP ops against the shared-memory loads per k), over
-// the schedulers its warps can occupy.  Small decode GEMMs get one or two
-// outputs per thread so that all SMs walk chains; large ones get 4x8
-// register tiles.
-struct TileCfg { int bm, bn, tm, tn; };
+// schedulers.  Each candidate is scored by the issue cycles of the busiest
+// SM (its CTAs' multiply-adds over the fraction of issue slots that are
+// FP32 work, spread over the schedulers its warps occupy), floored by the
+// dependent-add latency of one chain.
+struct TileCfg { int bm, bp, tm, tn; };
+static const TileCfg kTiles[] = {{64, 4, 4, 4}, {64, 2, 4, 2}, {32, 1, 2, 1}, {16, 2, 2, 1}, {4, 4, 1, 1}};
+constexpr int kNumTiles = 5;
+
 static double tile_cost(const TileCfg &c, int M, int N, int K) {
-  const long ctas = (long)((N + c.bn - 1) / c.bn) * ((M + c.bm - 1) / c.bm);
-  const int threads = (c.bm / c.tm) * (c.bn / c.tn);
+  const int bn = 8 * c.bp;
+  const long ctas = (long)((N + bn - 1) / bn) * ((M + c.bm - 1) / c.bm);
+  const int threads = (c.bm / c.tm) * (bn / c.tn);
   const long per_sm = (ctas + 147) / 148;
   const double fp = 2.0 * c.tm * c.tn;
-  const double loads = (c.tm + 3) / 4 + (c.tn + 3) / 4;
-  const double eff = fp / (fp + loads);
+  const double other = (c.tm + 3) / 4 + 1 + c.tn;   // x loads, w load, widens
+  const double eff = fp / (fp + other);
   const double warps = (double)per_sm * threads / 32.0;
   const double sched = warps < 4.0 ? warps : 4.0;
-  const double issue = (double)per_sm * c.bm * c.bn * K * 2.0 / eff / (32.0 * sched);
-  const double chain = 4.0 * K * (c.tm * c.tn > 4 ? 1.0 : 1.0);  // dependent-add floor per thread
+  const double issue = (double)per_sm * c.bm * bn * K * 2.0 / eff / (32.0 * sched);
+  const double chain = 4.0 * K;
   return issue > chain ? issue : chain;
 }
 
-void launch_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
-                 const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
-                 cudaStream_t s) {
-  if (M <= 0 || N <= 0) return;
-  static const TileCfg cands[] = {{64, 128, 4, 8}, {32, 64, 2, 4}, {16, 64, 1, 4}, {64, 4, 2, 1},
-                                  {32, 8, 2, 1},   {16, 16, 2, 1}, {8, 32, 2, 1},  {4, 64, 1, 1},
-                                  {1, 256, 1, 1}};
-  int best = -1;
-  double best_cost = 0;
-  for (int i = 0; i < (int)(sizeof(cands) / sizeof(cands[0])); ++i) {
-    const TileCfg &c = cands[i];
-    if (tree && c.tm * c.tn > 8) continue;       // tree mode keeps 5 pending levels per output
-    if (c.bm > 1 && M < c.bm / 2) continue;      // at most half a row tile wasted
-    if (c.bm == 1 && M > 3) continue;
-    double cost = tile_cost(c, M, N, K);
-    if (best < 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
-  }
-#define CIS2B_GEMM(BM_, BN_, TM_, TN_)                                                         \
-  do {                                                                                         \
-    if (tree)                                                                                  \
-      run_gemm<BM_, BN_, TM_, TN_, true>(X, ldx, W, K, N, M, Y, ldy, resid, ldr, y_slot,        \
-                                         y_slot_stride, s);                                   \
-    else                                                                                       \
-      run_gemm<BM_, BN_, TM_, TN_, false>(X, ldx, W, K, N, M, Y, ldy, resid, ldr, y_slot,       \
-                                          y_slot_stride, s);                                  \
-    return;                                                                                    \
-  } while (0)
-  switch (best) {
-    case 0: if (!tree) CIS2B_GEMM(64, 128, 4, 8); break;
-    case 1: CIS2B_GEMM(32, 64, 2, 4);
-    case 2: CIS2B_GEMM(16, 64, 1, 4);
-    case 3: CIS2B_GEMM(64, 4, 2, 1);
-    case 4: CIS2B_GEMM(32, 8, 2, 1);
-    case 5: CIS2B_GEMM(16, 16, 2, 1);
-    case 6: CIS2B_GEMM(8, 32, 2, 1);
-    case 7: CIS2B_GEMM(4, 64, 1, 1);
-    default: break;
-  }
-  CIS2B_GEMM(1, 256, 1, 1);
-#undef CIS2B_GEMM
-}
-
-// Chosen tile for a shape (for tests and tuning).
 int gemm_tile_choice(int M, int N, int K, bool tree) {
-  static const TileCfg cands[] = {{64, 128, 4, 8}, {32, 64, 2, 4}, {16, 64, 1, 4}, {64, 4, 2, 1},
-                                  {32, 8, 2, 1},   {16, 16, 2, 1}, {8, 32, 2, 1},  {4, 64, 1, 1},
-                                  {1, 256, 1, 1}};
   int best = -1;
   double best_cost = 0;
-  for (int i = 0; i < 9; ++i) {
-    const TileCfg &c = cands[i];
-    if (tree && c.tm * c.tn > 8) continue;
-    if (c.bm > 1 && M < c.bm / 2) continue;
-    if (c.bm == 1 && M > 3) continue;
-    double cost = tile_cost(c, M, N, K);
+  for (int i = 0; i < kNumTiles; ++i) {
+    const TileCfg &c = kTiles[i];
+    if (tree && c.tm * c.tn > 8) continue;       // tree mode keeps 5 pending levels per output
+    if (c.bm > 4 && M < c.bm / 2) continue;      // at most half a row tile wasted
+    const double cost = tile_cost(c, M, N, K);
     if (best < 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
   }
   return best;
 }
+
+void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
+                 const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
+                 cudaStream_t s) {
+  if (M <= 0 || N <= 0) return;
+#define CIS2B_GEMM(BM_, BP_, TM_, TN_)                                                           \
+  do {                                                                                           \
+    if (tree)                                                                                    \
+      run_gemm_t<BM_, BP_, TM_, TN_, true>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot,      \
+                                           y_slot_stride, s);                                   \
+    else                                                                                         \
+      run_gemm_t<BM_, BP_, TM_, TN_, false>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot,     \
+                                            y_slot_stride, s);                                  \
+    return;                                                                                      \
+  } while (0)
+  switch (gemm_tile_choice(M, N, K, tree)) {
+    case 0: if (!tree) CIS2B_GEMM(64, 4, 4, 4); break;
+    case 1: CIS2B_GEMM(64, 2, 4, 2);
+    case 2: CIS2B_GEMM(32, 1, 2, 1);
+    case 3: CIS2B_GEMM(16, 2, 2, 1);
+    default: break;
+  }
+  CIS2B_GEMM(4, 4, 1, 1);
+#undef CIS2B_GEMM
+}
+
+// Wp[n8][k][j] = W[8*n8 + j][k] (zero rows past N): the panel layout above.
+__global__ void k_panelize(const uint16_t *W, int N, int K, uint16_t *Wp) {
+  const size_t N8 = (size_t)(N + 7) / 8;
+  const size_t total = N8 * (size_t)K * 8;
+  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const size_t j = idx % 8, k = (idx / 8) % K, n8 = idx / (8 * (size_t)K);
+    const size_t n = n8 * 8 + j;
+    Wp[idx] = n < (size_t)N ? W[n * K + k] : (uint16_t)0;
+  }
+}
+void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s) {
+  k_panelize<<<1184, 256, 0, s>>>(W, N, K, Wp);
+}
+size_t panel_elems(int N, int K) { return (size_t)((N + 7) / 8) * 8 * (size_t)K; }
 
 // ============================================================ attention
 
@@ -533,7 +524,7 @@ size_t attention_smem_floats(int G, int hd, int max_len) {
 
 __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
                             int nh, int nkv, int hd, const float *kc, const float *vc, int max_pos,
-                            int tree, float *att, int ld_att, int max_len) {
+                            int tree, float *att, int ars, int acs, int max_len) {
   extern __shared__ float sm[];
   const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
@@ -566,7 +557,15 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
       float d;
       if (!tree) {
         d = 0.0f;
-        for (int i = 0; i < hd; ++i) d = fadd(d, fmul(qg[i], kj[i]));
+        int i = 0;
+        for (; i + 16 <= hd; i += 16) {
+          float a[16], b[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) { a[u] = qg[i + u]; b[u] = kj[i + u]; }
+#pragma unroll
+          for (int u = 0; u < 16; ++u) d = fadd(d, fmul(a[u], b[u]));
+        }
+        for (; i < hd; ++i) d = fadd(d, fmul(qg[i], kj[i]));
       } else {
         d = dot_tree(qg, kj, hd);
       }
@@ -602,13 +601,8 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
   for (int g = warp; g < G; g += nw) {
     if (lane == 0) {
       float acc = 0.0f;
-      if (!tree) {
-        const float *sg = sc + (size_t)g * max_len;
-        for (int j = 0; j < len; ++j) acc = fadd(acc, sg[j]);
-      } else {
-        const float *pg = part + (size_t)g * (max_len / 32 + 1);
-        for (int b = 0; b < nb; ++b) acc = fadd(acc, pg[b]);
-      }
+      if (!tree) acc = serial_sum(sc + (size_t)g * max_len, len);
+      else acc = serial_sum(part + (size_t)g * (max_len / 32 + 1), nb);
       red[32 + g] = acc;
     }
   }
@@ -633,15 +627,23 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
     __syncthreads();
     if (owns) {
       const float *pg = sc + (size_t)g * max_len + j0;
-      for (int jj = 0; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * hd + d]));
+      int jj = 0;
+      for (; jj + 16 <= jc; jj += 16) {
+        float a[16], b[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) { a[u] = pg[jj + u]; b[u] = tile[(jj + u) * hd + d]; }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc = fadd(acc, fmul(a[u], b[u]));
+      }
+      for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * hd + d]));
     }
   }
-  if (owns) att[(size_t)r * ld_att + ((size_t)kvh * G + g) * hd + d] = acc;
+  if (owns) att[(size_t)r * ars + ((size_t)kvh * G + g) * hd * acs + (size_t)d * acs] = acc;
 }
 
 void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
                       const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
-                      int ld_att, int max_len, cudaStream_t s) {
+                      int ars, int acs, int max_len, cudaStream_t s) {
   if (rows <= 0) return;
   const int G = n_heads / n_kv;
   int nt = ((G * hd + 31) / 32) * 32;
@@ -654,7 +656,7 @@ void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads
   }
   dim3 grid(rows, n_kv);
   k_attention<<<grid, nt, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache, max_pos,
-                                     tree ? 1 : 0, att, ld_att, max_len);
+                                     tree ? 1 : 0, att, ars, acs, max_len);
 }
 
 // ============================================================ token selection

@@ -23,15 +23,20 @@ void launch_rope_table(const float *inv_freq, int half, int max_pos, float *cos_
 
 void launch_embed(const uint16_t *E, int H, const uint32_t *tokens, int rows, float *h,
                   cudaStream_t s);
+// out[r * ors + i * ocs]: (ors, ocs) = (n, 1) row-major or (1, ldm) k-major.
 void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
-                    float *out, int ldo, cudaStream_t s);
+                    float *out, int ors, int ocs, cudaStream_t s);
 
-// Y[m][n] (+)= sum_k W[n][k] X[m][k] in the pinned order.  W bf16 [N][K] row
-// major (K % 8 == 0), X fp32 [M][ldx].  If resid != nullptr, Y = resid + dot.
-// If y_slot != nullptr, Y is offset by (*y_slot) * y_slot_stride floats.
-void launch_gemm(const float *X, int ldx, const uint16_t *W, int K, int N, int M, float *Y, int ldy,
+// Y[m][n] (+)= sum_k W[n][k] X[m][k] in the pinned order.  XT is X k-major
+// [K][ldm] (ldm % 4 == 0, ldm >= M); Wp holds W bf16 in 8-row k-major
+// panels (launch_panelize).  If resid != nullptr, Y = resid + dot.  If
+// y_slot != nullptr, Y is offset by (*y_slot) * y_slot_stride floats.
+void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                  const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s);
+// Wp[n8][k][j] = W[8*n8 + j][k], zero rows past N; Wp holds panel_elems(N, K) bf16.
+void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s);
+size_t panel_elems(int N, int K);
 
 // q/k norm (optional), RoPE of q and k, and the KV-cache append.
 // qkv rows: [q (n_heads*hd) | k (n_kv*hd) | v (n_kv*hd)].  Caches are laid
@@ -42,12 +47,12 @@ void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n
                      int max_pos, cudaStream_t s);
 void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
                       const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
-                      int ld_att, int max_len, cudaStream_t s);
+                      int ars, int acs, int max_len, cudaStream_t s);
 // Shared memory (floats) the attention kernel needs; G = n_heads / n_kv.
 size_t attention_smem_floats(int G, int hd, int max_len);
 // Index of the GEMM tile the dispatcher picks for (M, N, K).
 int gemm_tile_choice(int M, int N, int K, bool tree);
-void launch_silu_mul(const float *gu, int I, int rows, float *hid, cudaStream_t s);
+void launch_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs, cudaStream_t s);
 void launch_add_bias(float *x, int ld, int rows, const uint16_t *b, int n, cudaStream_t s);
 
 // Token selection.  logits rows at logits + slot*slot_stride (slot from device).

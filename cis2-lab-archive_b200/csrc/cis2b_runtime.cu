@@ -71,9 +71,12 @@ struct DevBuf {
 };
 
 struct LayerW {
-  const uint16_t *in_norm, *post_norm, *wqkv, *wo, *wgu, *wdown;
+  const uint16_t *in_norm, *post_norm, *wqkv, *wo, *wgu, *wdown;  // row-major [N][K] as on disk
   const uint16_t *q_norm, *k_norm, *q_bias, *k_bias, *v_bias;
+  const uint16_t *pqkv, *po, *pgu, *pdown;  // the same weights in GEMM panel layout
 };
+
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 constexpr int PREFILL_CHUNK = 8192;            // rows per prefill pass
 constexpr size_t RING_BUDGET = 8ull << 30;     // bytes of logits kept for the witness
@@ -88,11 +91,14 @@ struct cis2b_model {
   float eps = 0.f;
   std::vector<LayerW> layers;
   const uint16_t *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
-  DevBuf arena;  // all weights
+  DevBuf arena;   // all weights as on disk (embedding rows, norms, biases are read from here)
+  DevBuf panels;  // GEMM weights re-laid in 8-row k-major panels
+  const uint16_t *lm_head_p = nullptr;
   DevBuf inv_freq, cos_t, sin_t;
   cudaStream_t s_main = nullptr, s_sha = nullptr;
   // workspace
   DevBuf h, ln, qkv, att, gu, hid, hlast, lnlast, kc, vc, ring, scratch;
+  int act_ldm = 0;  // column count of the k-major activation buffers
   DevBuf rows_seq, rows_pos, rows_tok, gsrc, gdst;
   DevBuf d_next, d_pos, d_spos, d_seq, d_ctl, d_tokens, d_ids_hist;
   DevBuf sha_state, sha_wk, step_dig, d_witness, d_argmax;
@@ -349,6 +355,44 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   wbytes.clear();
   wbytes.shrink_to_fit();
 
+  // ---- GEMM weights in panel layout (same bf16 bits, k-major 8-row panels)
+  {
+    const int NQKV = m->QD + 2 * m->KVD;
+    size_t total = 0;
+    auto preserve = [&](int N, int K) {
+      size_t off = total;
+      total += (panel_elems(N, K) * 2 + 255) & ~(size_t)255;
+      return off;
+    };
+    std::vector<size_t> offs;
+    for (int l = 0; l < m->L; ++l) {
+      offs.push_back(preserve(NQKV, m->H));
+      offs.push_back(preserve(m->H, m->QD));
+      offs.push_back(preserve(2 * m->I, m->H));
+      offs.push_back(preserve(m->H, m->I));
+    }
+    size_t off_lmp = preserve(m->V, m->H);
+    if (m->panels.ensure(total) != cudaSuccess)
+      return fail(CIS2B_ERR_NOMEM, "device allocation of the weight panels failed");
+    uint8_t *pb = m->panels.as<uint8_t>();
+    auto pat = [&](size_t off) { return reinterpret_cast<uint16_t *>(pb + off); };
+    for (int l = 0; l < m->L; ++l) {
+      LayerW &w = m->layers[(size_t)l];
+      w.pqkv = pat(offs[4 * l]);
+      w.po = pat(offs[4 * l + 1]);
+      w.pgu = pat(offs[4 * l + 2]);
+      w.pdown = pat(offs[4 * l + 3]);
+      launch_panelize(w.wqkv, NQKV, m->H, const_cast<uint16_t *>(w.pqkv), m->s_main);
+      launch_panelize(w.wo, m->H, m->QD, const_cast<uint16_t *>(w.po), m->s_main);
+      launch_panelize(w.wgu, 2 * m->I, m->H, const_cast<uint16_t *>(w.pgu), m->s_main);
+      launch_panelize(w.wdown, m->H, m->I, const_cast<uint16_t *>(w.pdown), m->s_main);
+    }
+    m->lm_head_p = pat(off_lmp);
+    launch_panelize(m->lm_head, m->V, m->H, const_cast<uint16_t *>(m->lm_head_p), m->s_main);
+    CU_LAUNCHED();
+    CU(cudaStreamSynchronize(m->s_main));
+  }
+
   // ---- pinned tables on the device (cis2_model.h:456-476, 547-568)
   const int half = m->HD / 2;
   if (m->inv_freq.ensure(sizeof(float) * half) != cudaSuccess ||
@@ -400,6 +444,7 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
   float *h = m->h.as<float>(), *ln = m->ln.as<float>(), *qkv = m->qkv.as<float>();
   float *att = m->att.as<float>(), *gu = m->gu.as<float>(), *hid = m->hid.as<float>();
   const size_t layer_kv = (size_t)n_seq_cache * maxP * KVD;
+  const int ldm = m->act_ldm;  // ln, att, hid are k-major [K][ldm] GEMM operands
   RowMap rm{seq, pos};
   launch_embed(m->embed, H, tok, rows, h, s);
   m->launches += 1;
@@ -407,9 +452,9 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     const LayerW &w = m->layers[(size_t)l];
     float *kc = m->kc.as<float>() + (size_t)l * layer_kv;
     float *vc = m->vc.as<float>() + (size_t)l * layer_kv;
-    launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, H, s);
+    launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, 1, ldm, s);
     { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(ln, H, w.wqkv, H, NQKV, rows, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s); }
+      launch_gemm(ln, ldm, w.pqkv, H, NQKV, rows, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s); }
     m->launches += 2;
     if (w.q_bias) { launch_add_bias(qkv, NQKV, rows, w.q_bias, QD, s); m->launches++; }
     if (w.k_bias) { launch_add_bias(qkv + QD, NQKV, rows, w.k_bias, KVD, s); m->launches++; }
@@ -417,15 +462,16 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     launch_qkv_post(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, w.q_norm, w.k_norm, m->eps, m->tree,
                     m->cos_t.as<float>(), m->sin_t.as<float>(), kc, vc, maxP, s);
     { ProfScope p(m, CIS2B_PROF_ATTENTION, s);
-      launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, QD, maxP, s); }
+      launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, 1, ldm, maxP,
+                       s); }
     { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(att, QD, w.wo, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
-    launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, H, s);
+      launch_gemm(att, ldm, w.po, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
+    launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, 1, ldm, s);
     { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(ln, H, w.wgu, H, 2 * I, rows, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s); }
-    launch_silu_mul(gu, I, rows, hid, s);
+      launch_gemm(ln, ldm, w.pgu, H, 2 * I, rows, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s); }
+    launch_silu_mul(gu, I, rows, hid, 1, ldm, s);
     { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(hid, I, w.wdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
+      launch_gemm(hid, ldm, w.pdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
     m->launches += 7;
   }
   CU_LAUNCHED();
@@ -436,10 +482,11 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
 int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_t *y_slot,
               size_t slot_stride) {
   cudaStream_t s = m->s_main;
-  launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(), m->H, s);
+  const int ldb = round_up(rows, 64);  // lnlast is k-major [H][ldb]
+  launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(), 1, ldb, s);
   {
     ProfScope p(m, CIS2B_PROF_LM_HEAD, s);
-    launch_gemm(m->lnlast.as<float>(), m->H, m->lm_head, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
+    launch_gemm(m->lnlast.as<float>(), ldb, m->lm_head_p, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
                 y_slot, slot_stride, s);
   }
   m->launches += 2;
@@ -447,12 +494,16 @@ int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_
   return CIS2B_OK;
 }
 
+// Activation buffers for up to `rows` rows.  The GEMM operands (ln, att,
+// hid) are k-major with act_ldm = rows rounded up to 64 columns.
 int ensure_act(cis2b_model *m, int rows) {
   const size_t r = (size_t)std::max(rows, 1);
+  const size_t ldm = (size_t)round_up((int)r, 64);
   const size_t H = m->H, I = m->I, QD = m->QD, KVD = m->KVD;
-  if (m->h.ensure(4 * r * H) || m->ln.ensure(4 * r * H) || m->qkv.ensure(4 * r * (QD + 2 * KVD)) ||
-      m->att.ensure(4 * r * QD) || m->gu.ensure(4 * r * 2 * I) || m->hid.ensure(4 * r * I))
+  if (m->h.ensure(4 * r * H) || m->ln.ensure(4 * ldm * H) || m->qkv.ensure(4 * r * (QD + 2 * KVD)) ||
+      m->att.ensure(4 * ldm * QD) || m->gu.ensure(4 * r * 2 * I) || m->hid.ensure(4 * ldm * I))
     return fail(CIS2B_ERR_NOMEM, "device allocation of activations failed");
+  m->act_ldm = (int)ldm;
   return CIS2B_OK;
 }
 
@@ -464,7 +515,7 @@ int prefill(cis2b_model *m, const std::vector<uint32_t> &tok, const std::vector<
             const std::vector<int32_t> &out_dst, int n_seq_cache, int maxP) {
   const int total = (int)tok.size();
   const int chunk = std::min(total, PREFILL_CHUNK);
-  int rc = ensure_act(m, chunk);
+  int rc = ensure_act(m, std::max(chunk, n_seq_cache));
   if (rc) return rc;
   if (m->rows_tok.ensure(4 * (size_t)total) || m->rows_seq.ensure(4 * (size_t)total) ||
       m->rows_pos.ensure(4 * (size_t)total) || m->gsrc.ensure(4 * out_src.size() + 4) ||
@@ -547,7 +598,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   int rc = alloc_cache(m, B, maxP);
   if (rc) return rc;
   if (m->ring.ensure((size_t)ring * per_slot) || m->hlast.ensure(4 * (size_t)B * m->H) ||
-      m->lnlast.ensure(4 * (size_t)B * m->H) || m->d_next.ensure(4 * (size_t)B) ||
+      m->lnlast.ensure(4 * (size_t)round_up(B, 64) * m->H) || m->d_next.ensure(4 * (size_t)B) ||
       m->d_pos.ensure(4 * (size_t)B) || m->d_spos.ensure(4 * (size_t)B) || m->d_seq.ensure(4 * (size_t)B) ||
       m->d_ctl.ensure(64) || m->d_tokens.ensure(4 * (size_t)B * std::max(G, 1)) ||
       m->d_ids_hist.ensure(4 * (size_t)B * std::max(G, 1)) ||
@@ -785,7 +836,7 @@ int logits_impl(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t
   std::vector<int32_t> seq((size_t)total, 0), pos((size_t)total), osrc(n_rows), odst(n_rows);
   for (int i = 0; i < total; ++i) pos[(size_t)i] = i;
   for (uint32_t r = 0; r < n_rows; ++r) { osrc[r] = (int32_t)(n_prompt - 1 + r); odst[r] = (int32_t)r; }
-  if (m->hlast.ensure(4 * (size_t)n_rows * m->H) || m->lnlast.ensure(4 * (size_t)n_rows * m->H) ||
+  if (m->hlast.ensure(4 * (size_t)n_rows * m->H) || m->lnlast.ensure(4 * (size_t)round_up((int)n_rows, 64) * m->H) ||
       m->ring.ensure(4 * (size_t)n_rows * m->V) || ensure_act(m, 1))
     return fail(CIS2B_ERR_NOMEM, "device allocation failed");
   rc = prefill(m, tok, seq, pos, osrc, odst, 1, total);
@@ -903,14 +954,21 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
   if (!W || !X || !Y) return fail(CIS2B_ERR_ARG, "NULL buffer");
   if (rows <= 0 || n_out <= 0 || k <= 0 || k % 8) return fail(CIS2B_ERR_ARG, "bad shape (k must be a multiple of 8)");
   CU(cudaSetDevice(device));
-  Scoped<uint16_t> dw;
+  // Same operand layouts as the decoder: W in 8-row panels, X k-major.
+  const int ldm = round_up(rows, 4);
+  std::vector<float> xt((size_t)k * ldm, 0.0f);
+  for (int r = 0; r < rows; ++r)
+    for (int i = 0; i < k; ++i) xt[(size_t)i * ldm + r] = X[(size_t)r * k + i];
+  Scoped<uint16_t> dw, dp;
   Scoped<float> dx, dy;
   CU(cudaMalloc(&dw.p, 2 * (size_t)n_out * k));
-  CU(cudaMalloc(&dx.p, 4 * (size_t)rows * k));
+  CU(cudaMalloc(&dp.p, 2 * panel_elems(n_out, k)));
+  CU(cudaMalloc(&dx.p, 4 * xt.size()));
   CU(cudaMalloc(&dy.p, 4 * (size_t)rows * n_out));
   CU(cudaMemcpy(dw.p, W, 2 * (size_t)n_out * k, cudaMemcpyHostToDevice));
-  CU(cudaMemcpy(dx.p, X, 4 * (size_t)rows * k, cudaMemcpyHostToDevice));
-  launch_gemm(dx.p, k, dw.p, k, n_out, rows, dy.p, n_out, nullptr, 0, reduction == CIS2B_REDUCTION_TREE,
+  CU(cudaMemcpy(dx.p, xt.data(), 4 * xt.size(), cudaMemcpyHostToDevice));
+  launch_panelize(dw.p, n_out, k, dp.p, 0);
+  launch_gemm(dx.p, ldm, dp.p, k, n_out, rows, dy.p, n_out, nullptr, 0, reduction == CIS2B_REDUCTION_TREE,
               nullptr, 0, 0);
   CU_LAUNCHED();
   CU(cudaMemcpy(Y, dy.p, 4 * (size_t)rows * n_out, cudaMemcpyDeviceToHost));

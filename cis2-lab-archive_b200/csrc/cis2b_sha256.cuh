@@ -60,15 +60,23 @@ __device__ __forceinline__ void sha_expand_wk(const uint32_t m[16], uint32_t wk[
   }
 }
 
-// One round with the pre-added W+K word.
+// One round with the pre-added W+K word, arranged so that both recurrences
+// are three dependent instructions deep:
+//   e' = (d + h + WK) + S1(e) + Ch(e,f,g)      -- d, h are 3 rounds old
+//   a' = (h + WK) + S1(e) + Ch(e,f,g) + S0(a) + Maj(a,b,c)
+// (FIPS 180-4 §6.2.2 step 3, regrouped; integer addition is associative
+// mod 2^32, so the result is the same word.)
 #define CIS2B_SHA_ROUND(a, b, c, d, e, f, g, h, wkv)                                 \
   do {                                                                               \
-    uint32_t t1 = (h) + (rotr((e), 6) ^ rotr((e), 11) ^ rotr((e), 25)) +             \
-                  (((e) & (f)) ^ (~(e) & (g))) + (wkv);                              \
-    uint32_t t2 = (rotr((a), 2) ^ rotr((a), 13) ^ rotr((a), 22)) +                   \
-                  (((a) & (b)) ^ ((a) & (c)) ^ ((b) & (c)));                         \
-    (d) += t1;                                                                       \
-    (h) = t1 + t2;                                                                   \
+    const uint32_t hk_ = (h) + (wkv);                                                \
+    const uint32_t x_ = hk_ + (d);                                                   \
+    const uint32_t s1_ = rotr((e), 6) ^ rotr((e), 11) ^ rotr((e), 25);               \
+    const uint32_t ch_ = ((e) & (f)) ^ (~(e) & (g));                                 \
+    const uint32_t s0_ = rotr((a), 2) ^ rotr((a), 13) ^ rotr((a), 22);               \
+    const uint32_t mj_ = ((a) & (b)) ^ ((a) & (c)) ^ ((b) & (c));                    \
+    const uint32_t t1_ = hk_ + s1_ + ch_;                                            \
+    (d) = x_ + s1_ + ch_;                                                            \
+    (h) = t1_ + s0_ + mj_;                                                           \
   } while (0)
 
 // Compress one block given its 64 W+K words (fully unrolled, register-renamed).
