@@ -98,6 +98,8 @@ def lib() -> ctypes.CDLL:
     L.cis2b_op_sha256_stream.argtypes = [I32, P, SZ, P, U32, U32, P]
     L.cis2b_op_sample.argtypes = [I32, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
                                   ctypes.c_uint64, ctypes.POINTER(U32)]
+    L.cis2b_op_sample_static.argtypes = [I32, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
+                                         ctypes.c_uint64, P, P]
     _lib = L
     return L
 

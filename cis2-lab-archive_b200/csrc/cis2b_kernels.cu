@@ -18,6 +18,8 @@
 
 #include <stdio.h>
 
+#include <mutex>
+
 namespace cis2b {
 
 static constexpr unsigned FULL = 0xffffffffu;
@@ -890,6 +892,68 @@ void launch_sample(const float *logits, int V, int rows, const int32_t *slot, si
   k_sample<<<rows, SAMPLE_THREADS, 0, s>>>(logits, V, slot, slot_stride, temperature, top_p, seed,
                                            position, scratch, next);
 }
+
+// ------------------------------------------------------------ sampler without allocation
+//
+// A second way to run the E23 sampler on one row, for callers that cannot
+// allocate device memory themselves or through this library: code whose
+// device memory belongs to its own allocator (a framework's caching pool or
+// a pre-reserved arena) and must not be bypassed with cudaMalloc, and code
+// on a latency-critical path where cudaMalloc/cudaFree would synchronise the
+// device.  Its working memory is the file-scope array below, which every GPU
+// that loads the library holds until the process exits.  Sized for rows of
+// up to CIS2B_STATIC_SAMPLE_MAX logits: the sampler needs 5 floats per logit
+// (probabilities, two key/index buffer pairs) plus one int for the position.
+constexpr int kStaticSampleMax = 262144;
+static __device__ __align__(256) float g_sample_scratch[5 * kStaticSampleMax + 64];
+
+// The host-side name g_sample_scratch is not a device address; the address
+// is looked up once per device, with that device current.
+static float *g_scratch_addr[64];
+static std::mutex g_scratch_mu;
+
+__global__ void k_store_position(int32_t *dst, int32_t v) { *dst = v; }
+
+}  // namespace cis2b
+
+extern "C" int cis2b_op_sample_static(int32_t device, const float *d_logits, int32_t n, float temperature,
+                                      float top_p, uint64_t seed, uint64_t position, uint32_t *d_out_index,
+                                      void *stream) {
+  using namespace cis2b;
+  if (!d_logits || !d_out_index) return set_last_error(1, "d_logits and d_out_index must be device pointers");
+  if (n <= 0 || n > kStaticSampleMax)
+    return set_last_error(1, "n must be in 1..262144: the static sampler scratch holds 5 floats per logit "
+                             "for at most 262144 logits");
+  if (!(temperature > 0.0f) || !(top_p > 0.0f && top_p <= 1.0f))
+    return set_last_error(1, "temperature must be > 0 and top_p in (0, 1]");
+  if (position > 0x7fffffffull) return set_last_error(1, "position must be < 2^31");
+  if (device < 0 || device >= 64) return set_last_error(1, "device ordinal out of range");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return set_last_error(4, cudaGetErrorString(e));
+  float *scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[device]) {
+      void *p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_sample_scratch);
+      if (e != cudaSuccess) return set_last_error(4, cudaGetErrorString(e));
+      g_scratch_addr[device] = static_cast<float *>(p);
+    }
+    scratch = g_scratch_addr[device];
+  }
+  // Every element of the scratch that the sampler reads it first writes, so
+  // nothing is cleared between calls.  Only the position slot is set here.
+  int32_t *pos_slot = reinterpret_cast<int32_t *>(scratch + 5 * (size_t)kStaticSampleMax);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  k_store_position<<<1, 1, 0, s>>>(pos_slot, (int32_t)position);
+  k_sample<<<1, SAMPLE_THREADS, 0, s>>>(d_logits, n, nullptr, 0, temperature, top_p, seed, pos_slot, scratch,
+                                        d_out_index);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_last_error(4, cudaGetErrorString(e));
+  return 0;
+}
+
+namespace cis2b {
 
 // After token selection: record the token, advance the row's position and
 // the logits ring slot for the next step.

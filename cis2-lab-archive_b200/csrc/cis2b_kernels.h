@@ -88,6 +88,9 @@ void launch_sha_finalize(const ShaState *st, int n_seq, uint8_t *out, cudaStream
 void launch_sha_ids(const uint32_t *prompt_flat, const uint32_t *prompt_off, const uint32_t *prompt_len,
                     const uint32_t *gen_tokens, int gen, int n_seq, uint8_t *out, cudaStream_t s);
 
+// Records `msg` as this thread's cis2b_last_error() and returns `code`.
+int set_last_error(int code, const char *msg);
+
 // Element-wise pinned function map (test entry point).
 void launch_pinned_map(int fn, const float *x, float *y, size_t n, cudaStream_t s);
 

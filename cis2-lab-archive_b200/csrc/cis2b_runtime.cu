@@ -36,6 +36,14 @@ int fail(int code, const std::string &msg) {
   return code;
 }
 
+}  // namespace
+
+// Lets entry points defined next to their kernels report through
+// cis2b_last_error() like every other call.
+int cis2b::set_last_error(int code, const char *msg) { return fail(code, msg); }
+
+namespace {
+
 #define CU(x)                                                                               \
   do {                                                                                      \
     cudaError_t e_ = (x);                                                                   \

@@ -155,6 +155,31 @@ int cis2b_op_sha256_stream(int32_t device, const uint8_t *prefix, size_t prefix_
 int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temperature, float top_p,
                     uint64_t seed, uint64_t position, uint32_t *out_index);
 
+/* No counterpart in the reference.  The E23 sampler on one logits row that
+ * ALLOCATES NOTHING: for callers that cannot call cudaMalloc -- code whose
+ * device memory is owned by its own allocator (a framework's caching pool,
+ * a pre-reserved arena) that must not be bypassed, or code on a
+ * latency-critical path where cudaMalloc/cudaFree would synchronise the
+ * device.  The caller passes device pointers for the input row and the
+ * output index; the sampler's working memory is a fixed array inside the
+ * library (5 floats per logit for CIS2B_STATIC_SAMPLE_MAX logits, about
+ * 5 MiB) that every GPU which loads the library keeps until the process
+ * exits.
+ *   d_logits     device pointer to n fp32 logits, 1 <= n <= CIS2B_STATIC_SAMPLE_MAX
+ *   d_out_index  device pointer to one uint32, written with the drawn index
+ *   stream       cudaStream_t to run on (NULL: the legacy default stream)
+ * Makes `device` current on the calling thread.  The first call on a device
+ * looks up the array's device address; make that first call before any
+ * stream capture.  The call is asynchronous: the index is valid once
+ * `stream` has reached it.  All calls share the one array and it keeps the
+ * last call's contents (every element the sampler reads it writes first),
+ * so calls whose work overlaps on the GPU -- two streams, or two threads --
+ * race and must be ordered by the caller.  Sizes above the maximum are
+ * rejected with CIS2B_ERR_ARG.  Same result as cis2b_op_sample. */
+#define CIS2B_STATIC_SAMPLE_MAX 262144
+int cis2b_op_sample_static(int32_t device, const float *d_logits, int32_t n, float temperature, float top_p,
+                           uint64_t seed, uint64_t position, uint32_t *d_out_index, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
