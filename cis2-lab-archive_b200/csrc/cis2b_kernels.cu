@@ -35,6 +35,14 @@ __device__ __forceinline__ float warp_tree32(float v) {
   return v;
 }
 
+// Asynchronous 16-byte global -> shared copies (sm_80+ cp.async).
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // Thread-local pinned dot of two smem/global vectors.
 __device__ __forceinline__ float dot_seq(const float *a, const float *b, int n) {
   float acc = 0.0f;
@@ -60,17 +68,17 @@ __device__ __forceinline__ float dot_tree(const float *a, const float *b, int n)
 }
 
 // Strict left-to-right sum of a[0..n) from +0 by ONE thread.  Operands
-// are fetched 16 at a time ahead of the dependent adds, so the chain runs
-// at add latency rather than load latency.
+// are fetched 32 at a time ahead of the dependent adds, so the chain runs
+// near add latency (4 cycles) rather than load latency (~34 for shared).
 __device__ __forceinline__ float serial_sum(const float *a, int n) {
   float acc = 0.0f;
   int i = 0;
-  for (; i + 16 <= n; i += 16) {
-    float v[16];
+  for (; i + 32 <= n; i += 32) {
+    float v[32];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = a[i + u];
+    for (int u = 0; u < 32; ++u) v[u] = a[i + u];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) acc = fadd(acc, v[u]);
+    for (int u = 0; u < 32; ++u) acc = fadd(acc, v[u]);
   }
   for (; i < n; ++i) acc = fadd(acc, a[i]);
   return acc;
@@ -78,10 +86,16 @@ __device__ __forceinline__ float serial_sum(const float *a, int n) {
 
 // RMSNorm of one row by one warp (cis2_model.h:511-523):
 // sq = x*x; ss = fold(sq); mean = ss/n; inv = 1/sqrt(mean+eps); out = (x*inv)*w.
-// `sq` is warp-private scratch of n floats.  out (element stride os) may alias x.
+// `sq` is warp-private shared scratch of 2n floats (squares, then a copy of
+// x, so the row is read from global memory once).  out (element stride os)
+// may alias x.
 __device__ __forceinline__ void warp_rmsnorm(const float *x, const uint16_t *w, float eps, int n,
                                              bool tree, float *sq, float *out, int os = 1) {
   const int lane = threadIdx.x & 31;
+  float *xc = sq + n;
+  for (int i = lane; i < n; i += 32) xc[i] = x[i];
+  __syncwarp();
+  x = xc;
   float ss;
   if (!tree) {
     for (int i = lane; i < n; i += 32) sq[i] = fmul(x[i], x[i]);
@@ -154,14 +168,14 @@ __global__ void k_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps,
   int warp = threadIdx.x >> 5;
   int r = blockIdx.x * (blockDim.x >> 5) + warp;
   if (r >= rows) return;
-  warp_rmsnorm(x + (size_t)r * ldx, w, eps, n, tree != 0, sm + (size_t)warp * n,
+  warp_rmsnorm(x + (size_t)r * ldx, w, eps, n, tree != 0, sm + (size_t)warp * 2 * n,
                out + (size_t)r * ors, ocs);
 }
 void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
                     float *out, int ors, int ocs, cudaStream_t s) {
   if (rows <= 0) return;
   const int wpb = 4;
-  k_rmsnorm<<<(rows + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * n * sizeof(float), s>>>(
+  k_rmsnorm<<<(rows + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * 2 * n * sizeof(float), s>>>(
       x, ldx, w, eps, n, rows, tree ? 1 : 0, out, ors, ocs);
 }
 
@@ -294,17 +308,33 @@ k_gemm_t(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp,
     const float *xs = Xs + slot * XF + tm * TM;
     const uint16_t *ws = Ws + slot * WH + wp * 8 + wj;
     if (!TREE) {
-#pragma unroll 8
-      for (int kk = 0; kk < GEMM_KT; ++kk) {
-        float x[TM], w[TN];
+      // Operands of GRP k-steps are fetched into registers one group ahead
+      // of the multiply-adds that use them, so the ~34-cycle shared-memory
+      // latency overlaps the dependent-add chain instead of adding to it.
+      constexpr int GRP = (TM + TN <= 4) ? 8 : 4;
+      constexpr int NG = GEMM_KT / GRP;
+      float xr[2][GRP][TM], wr[2][GRP][TN];
+      auto fetch = [&](int buf, int g) {
 #pragma unroll
-        for (int i = 0; i < TM; ++i) x[i] = xs[kk * BM + i];
+        for (int u = 0; u < GRP; ++u) {
+          const int kk = g * GRP + u;
 #pragma unroll
-        for (int j = 0; j < TN; ++j) w[j] = widen_bf16(ws[kk * BN + j]);
+          for (int i = 0; i < TM; ++i) xr[buf][u][i] = xs[kk * BM + i];
 #pragma unroll
-        for (int i = 0; i < TM; ++i)
+          for (int j = 0; j < TN; ++j) wr[buf][u][j] = widen_bf16(ws[kk * BN + j]);
+        }
+      };
+      fetch(0, 0);
 #pragma unroll
-          for (int j = 0; j < TN; ++j) acc[i][j] = fadd(acc[i][j], fmul(w[j], x[i]));
+      for (int g = 0; g < NG; ++g) {
+        if (g + 1 < NG) fetch((g + 1) & 1, g + 1);
+#pragma unroll
+        for (int u = 0; u < GRP; ++u)
+#pragma unroll
+          for (int i = 0; i < TM; ++i)
+#pragma unroll
+            for (int j = 0; j < TN; ++j)
+              acc[i][j] = fadd(acc[i][j], fmul(wr[g & 1][u][j], xr[g & 1][u][i]));
       }
     } else {
       // Streaming pairwise tree over the 32 leaves of this k tile: level L
@@ -376,8 +406,9 @@ static void run_gemm_t(const float *XT, int ldm, const uint16_t *Wp, int K, int 
 // FP32 work, spread over the schedulers its warps occupy), floored by the
 // dependent-add latency of one chain.
 struct TileCfg { int bm, bp, tm, tn; };
-static const TileCfg kTiles[] = {{64, 4, 4, 4}, {64, 2, 4, 2}, {32, 1, 2, 1}, {16, 2, 2, 1}, {4, 4, 1, 1}};
-constexpr int kNumTiles = 5;
+static const TileCfg kTiles[] = {{64, 4, 4, 4}, {64, 2, 4, 2}, {32, 1, 2, 1}, {16, 2, 2, 1}, {4, 4, 1, 1},
+                                 {32, 2, 2, 2}, {32, 4, 2, 4}};
+constexpr int kNumTiles = 7;
 
 static double tile_cost(const TileCfg &c, int M, int N, int K) {
   const int bn = 8 * c.bp;
@@ -426,6 +457,8 @@ void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int
     case 1: CIS2B_GEMM(64, 2, 4, 2);
     case 2: CIS2B_GEMM(32, 1, 2, 1);
     case 3: CIS2B_GEMM(16, 2, 2, 1);
+    case 5: CIS2B_GEMM(32, 2, 2, 2);
+    case 6: CIS2B_GEMM(32, 4, 2, 4);
     default: break;
   }
   CIS2B_GEMM(4, 4, 1, 1);
@@ -465,7 +498,7 @@ __global__ void k_qkv_post(float *qkv, int ld, const int32_t *rseq, const int32_
   const int half = hd / 2, QD = nh * hd, KV = nkv * hd;
   const float *ct = cos_t + (size_t)pos * half;
   const float *st = sin_t + (size_t)pos * half;
-  float *sq = sm + (size_t)warp * hd;
+  float *sq = sm + (size_t)warp * 2 * hd;
   for (int h = warp; h < nh + nkv; h += nw) {
     const bool is_k = h >= nh;
     float *x = is_k ? row + QD + (size_t)(h - nh) * hd : row + (size_t)h * hd;
@@ -494,7 +527,7 @@ void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n
                      int max_pos, cudaStream_t s) {
   if (rows <= 0) return;
   const int threads = 128;
-  k_qkv_post<<<rows, threads, (size_t)(threads / 32) * hd * sizeof(float), s>>>(
+  k_qkv_post<<<rows, threads, (size_t)(threads / 32) * 2 * hd * sizeof(float), s>>>(
       qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, q_norm, k_norm, eps, tree ? 1 : 0, cos_t, sin_t,
       kcache, vcache, max_pos);
 }
@@ -520,14 +553,17 @@ __device__ __forceinline__ float max_comb(float a, float b) {
 constexpr int ATT_JC = 64;
 
 size_t attention_smem_floats(int G, int hd, int max_len) {
-  return (size_t)G * hd + (size_t)G * max_len + (size_t)G * (max_len / 32 + 1) + 64 +
-         (size_t)ATT_JC * (hd + 1);
+  size_t f = (size_t)G * hd + (size_t)G * max_len + (size_t)G * (max_len / 32 + 1) + 64;
+  f = (f + 3) & ~(size_t)3;                              // tiles start 16-byte aligned
+  return f + (size_t)2 * ATT_JC * (hd + 4);
 }
 
-__global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
-                            int nh, int nkv, int hd, const float *kc, const float *vc, int max_pos,
-                            int tree, float *att, int ars, int acs, int max_len) {
-  extern __shared__ float sm[];
+__global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
+                            int nh, int nkv, int hd, float *kc, float *vc, int max_pos,
+                            int tree, float *att, int ars, int acs, int max_len, int fuse_post,
+                            const uint16_t *qn, const uint16_t *kn, float eps, const float *cos_t,
+                            const float *sin_t) {
+  extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
   const int G = nh / nkv, KV = nkv * hd;
@@ -537,25 +573,68 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
   float *sc = q + G * hd;                     // [G][max_len]
   float *part = sc + (size_t)G * max_len;     // [G][max_len/32 + 1]
   float *red = part + (size_t)G * (max_len / 32 + 1);  // [64]
-  float *tile = red + 64;                     // [ATT_JC][hd + 1]
-  const int tstride = hd + 1;
+  size_t toff = (size_t)(red + 64 - sm);
+  toff = (toff + 3) & ~(size_t)3;
+  float *tiles = sm + toff;                   // [2][ATT_JC][hd + 4], K then V chunks
+  const int ts = hd + 4;
+  if (fuse_post) {
+    // Decode rows only (each CTA's row is its sequence's newest position):
+    // the work of k_qkv_post for this KV head's q heads, k head and v head,
+    // done here so the new key/value reach the cache without another launch.
+    float *row = qkv + (size_t)r * ld;
+    const int QD = nh * hd, half = hd / 2;
+    const float *ct = cos_t + (size_t)pos * half, *st = sin_t + (size_t)pos * half;
+    for (int hh = warp; hh <= G; hh += nw) {
+      const bool is_k = hh == G;
+      float *x = is_k ? row + QD + (size_t)kvh * hd : row + ((size_t)kvh * G + hh) * hd;
+      const uint16_t *nwt = is_k ? kn : qn;
+      if (nwt) warp_rmsnorm(x, nwt, eps, hd, tree != 0, tiles + (size_t)warp * 2 * hd, x);
+      for (int i = lane; i < half; i += 32) {
+        float x1 = x[i], x2 = x[i + half], c = ct[i], sn = st[i];
+        float o1 = fadd(fmul(x1, c), fmul(fneg(x2), sn));
+        float o2 = fadd(fmul(x2, c), fmul(x1, sn));
+        x[i] = o1;
+        x[i + half] = o2;
+      }
+      __syncwarp();
+      if (is_k) {
+        float *dst = kc + ((size_t)seq * max_pos + pos) * KV + (size_t)kvh * hd;
+        for (int i = lane; i < hd; i += 32) dst[i] = x[i];
+      }
+    }
+    const float *vsrc = row + QD + KV + (size_t)kvh * hd;
+    float *vdst = vc + ((size_t)seq * max_pos + pos) * KV + (size_t)kvh * hd;
+    for (int i = tid; i < hd; i += nt) vdst[i] = vsrc[i];
+    __syncthreads();
+  }
   for (int i = tid; i < G * hd; i += nt) q[i] = qkv[(size_t)r * ld + (size_t)kvh * G * hd + i];
   const float scale = rsqrt_cr(__int2float_rn(hd));
   const float *kbase = kc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
   const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
-
-  // ---- scores
-  for (int j0 = 0; j0 < len; j0 += ATT_JC) {
-    const int jc = min(ATT_JC, len - j0);
-    __syncthreads();
-    for (int i = tid; i < jc * hd; i += nt) {
-      int jj = i / hd, dd = i - jj * hd;
-      tile[jj * tstride + dd] = kbase[(size_t)(j0 + jj) * KV + dd];
+  const int nch = (len + ATT_JC - 1) / ATT_JC;
+  const uint32_t tbase = (uint32_t)__cvta_generic_to_shared(tiles);
+  // K or V rows [j0, j0+ATT_JC) of this KV head -> tile buffer `buf`, async.
+  auto stage = [&](const float *base, int c, int buf) {
+    const int j0 = c * ATT_JC, jc = min(ATT_JC, len - j0), nq = hd / 4;
+    for (int i = tid; i < jc * nq; i += nt) {
+      const int jj = i / nq, q4 = i - jj * nq;
+      cp_async16(tbase + (uint32_t)(((buf * ATT_JC + jj) * ts + 4 * q4) * 4), base + (size_t)(j0 + jj) * KV + 4 * q4);
     }
+    cp_async_commit();
+  };
+
+  // ---- scores, K streamed through two tile buffers
+  stage(kbase, 0, 0);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) stage(kbase, c + 1, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
+    const int j0 = c * ATT_JC, jc = min(ATT_JC, len - j0);
+    const float *tile = tiles + (size_t)(c & 1) * ATT_JC * ts;
     for (int pr = tid; pr < G * jc; pr += nt) {
       const int g = pr / jc, jj = pr - g * jc;
-      const float *qg = q + g * hd, *kj = tile + jj * tstride;
+      const float *qg = q + g * hd, *kj = tile + jj * ts;
       float d;
       if (!tree) {
         d = 0.0f;
@@ -571,10 +650,12 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
       } else {
         d = dot_tree(qg, kj, hd);
       }
-      sc[(size_t)g * max_len + j0 + jj] = fmul(d, scale);
+      sc[(size_t)g * max_len + j0 + jj] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
     }
+    __syncthreads();
   }
-  __syncthreads();
+  // V chunk 0 loads while the softmax runs.
+  stage(vbase, 0, 0);
   // ---- max per head (serial-scan semantics, see max_comb)
   for (int g = warp; g < G; g += nw) {
     const float *sg = sc + (size_t)g * max_len;
@@ -602,7 +683,7 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
   }
   for (int g = warp; g < G; g += nw) {
     if (lane == 0) {
-      float acc = 0.0f;
+      float acc;
       if (!tree) acc = serial_sum(sc + (size_t)g * max_len, len);
       else acc = serial_sum(part + (size_t)g * (max_len / 32 + 1), nb);
       red[32 + g] = acc;
@@ -614,38 +695,41 @@ __global__ void k_attention(const float *qkv, int ld, const int32_t *rseq, const
     float *p = sc + (size_t)g * max_len + j;
     *p = fdiv(*p, red[32 + g]);
   }
-  // ---- V-mix
+  // ---- V-mix, V streamed through the two tile buffers
   const int gd = tid;                  // (g, d) chain owned by this thread
   const int g = gd / hd, d = gd - (gd / hd) * hd;
   const bool owns = gd < G * hd;
   float acc = 0.0f;
-  for (int j0 = 0; j0 < len; j0 += ATT_JC) {
-    const int jc = min(ATT_JC, len - j0);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) stage(vbase, c + 1, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
-    for (int i = tid; i < jc * hd; i += nt) {
-      int jj = i / hd, dd = i - jj * hd;
-      tile[jj * hd + dd] = vbase[(size_t)(j0 + jj) * KV + dd];
-    }
-    __syncthreads();
+    const int j0 = c * ATT_JC, jc = min(ATT_JC, len - j0);
+    const float *tile = tiles + (size_t)(c & 1) * ATT_JC * ts;
     if (owns) {
       const float *pg = sc + (size_t)g * max_len + j0;
       int jj = 0;
       for (; jj + 16 <= jc; jj += 16) {
         float a[16], b[16];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) { a[u] = pg[jj + u]; b[u] = tile[(jj + u) * hd + d]; }
+        for (int u = 0; u < 16; ++u) { a[u] = pg[jj + u]; b[u] = tile[(jj + u) * ts + d]; }
 #pragma unroll
         for (int u = 0; u < 16; ++u) acc = fadd(acc, fmul(a[u], b[u]));
       }
-      for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * hd + d]));
+      for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * ts + d]));
     }
+    __syncthreads();
   }
+  cp_async_wait<0>();
   if (owns) att[(size_t)r * ars + ((size_t)kvh * G + g) * hd * acs + (size_t)d * acs] = acc;
 }
 
-void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
-                      const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
-                      int ars, int acs, int max_len, cudaStream_t s) {
+void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
+                      float *kcache, float *vcache, int max_pos, bool tree, float *att,
+                      int ars, int acs, int max_len, bool fuse_post, const uint16_t *q_norm,
+                      const uint16_t *k_norm, float eps, const float *cos_t, const float *sin_t,
+                      cudaStream_t s) {
   if (rows <= 0) return;
   const int G = n_heads / n_kv;
   int nt = ((G * hd + 31) / 32) * 32;
@@ -658,7 +742,8 @@ void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads
   }
   dim3 grid(rows, n_kv);
   k_attention<<<grid, nt, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache, max_pos,
-                                     tree ? 1 : 0, att, ars, acs, max_len);
+                                     tree ? 1 : 0, att, ars, acs, max_len, fuse_post ? 1 : 0, q_norm,
+                                     k_norm, eps, cos_t, sin_t);
 }
 
 // ============================================================ token selection
@@ -1087,12 +1172,6 @@ constexpr size_t SHA_STAGE_BYTES = (size_t)16 * 32 * sizeof(uint4);          // 
 constexpr size_t SHA_SMEM = (size_t)227 * 1024;                              // SM's maximum per CTA
 static_assert(SHA_WARPS * SHA_STAGES * SHA_STAGE_BYTES <= SHA_SMEM, "witness pipeline exceeds smem");
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __global__ void __launch_bounds__(32 * SHA_WARPS)
 k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,

@@ -45,9 +45,13 @@ void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n
                      const uint16_t *q_norm, const uint16_t *k_norm, float eps, bool tree,
                      const float *cos_t, const float *sin_t, float *kcache, float *vcache,
                      int max_pos, cudaStream_t s);
-void launch_attention(const float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
-                      const float *kcache, const float *vcache, int max_pos, bool tree, float *att,
-                      int ars, int acs, int max_len, cudaStream_t s);
+// fuse_post: also do launch_qkv_post's work for the row (decode only: every
+// row must be a different sequence's newest position).
+void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
+                      float *kcache, float *vcache, int max_pos, bool tree, float *att,
+                      int ars, int acs, int max_len, bool fuse_post, const uint16_t *q_norm,
+                      const uint16_t *k_norm, float eps, const float *cos_t, const float *sin_t,
+                      cudaStream_t s);
 // Shared memory (floats) the attention kernel needs; G = n_heads / n_kv.
 size_t attention_smem_floats(int G, int hd, int max_len);
 // Index of the GEMM tile the dispatcher picks for (M, N, K).

@@ -235,7 +235,7 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   m->QD = m->NH * m->HD;
   m->KVD = m->NKV * m->HD;
   if (m->NH % m->NKV) return fail(CIS2B_ERR_CONFIG, "num_attention_heads % num_key_value_heads != 0");
-  if (m->HD <= 0 || m->HD % 2) return fail(CIS2B_ERR_CONFIG, "head_dim must be even and positive");
+  if (m->HD <= 0 || m->HD % 4) return fail(CIS2B_ERR_CONFIG, "head_dim must be a positive multiple of 4");
   if (m->H % 8 || m->QD % 8 || m->I % 8)
     return fail(CIS2B_ERR_CONFIG, "hidden, q_dim and intermediate sizes must be multiples of 8");
   m->info.hidden = m->H; m->info.intermediate = m->I; m->info.n_layers = m->L;
@@ -444,9 +444,11 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
 // ------------------------------------------------------------------ forward
 // Runs `rows` activation rows (token ids, sequence index and position per
 // row, all on the device) through every layer.  Leaves the final hidden
-// state in m->h.  kv caches are [layer][seq][maxP][kvd].
+// state in m->h.  kv caches are [layer][seq][maxP][kvd].  `decode`: every
+// row is a different sequence's newest position, so the q/k post-processing
+// and the cache append run inside the attention kernel.
 int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *seq,
-                 const int32_t *pos, int n_seq_cache, int maxP) {
+                 const int32_t *pos, int n_seq_cache, int maxP, bool decode) {
   cudaStream_t s = m->s_main;
   const int H = m->H, I = m->I, QD = m->QD, KVD = m->KVD, NQKV = QD + 2 * KVD;
   float *h = m->h.as<float>(), *ln = m->ln.as<float>(), *qkv = m->qkv.as<float>();
@@ -467,11 +469,14 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     if (w.q_bias) { launch_add_bias(qkv, NQKV, rows, w.q_bias, QD, s); m->launches++; }
     if (w.k_bias) { launch_add_bias(qkv + QD, NQKV, rows, w.k_bias, KVD, s); m->launches++; }
     if (w.v_bias) { launch_add_bias(qkv + QD + KVD, NQKV, rows, w.v_bias, KVD, s); m->launches++; }
-    launch_qkv_post(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, w.q_norm, w.k_norm, m->eps, m->tree,
-                    m->cos_t.as<float>(), m->sin_t.as<float>(), kc, vc, maxP, s);
+    if (!decode) {
+      launch_qkv_post(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, w.q_norm, w.k_norm, m->eps, m->tree,
+                      m->cos_t.as<float>(), m->sin_t.as<float>(), kc, vc, maxP, s);
+      m->launches++;
+    }
     { ProfScope p(m, CIS2B_PROF_ATTENTION, s);
       launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, 1, ldm, maxP,
-                       s); }
+                       decode, w.q_norm, w.k_norm, m->eps, m->cos_t.as<float>(), m->sin_t.as<float>(), s); }
     { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
       launch_gemm(att, ldm, w.po, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
     launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, 1, ldm, s);
@@ -480,7 +485,7 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     launch_silu_mul(gu, I, rows, hid, 1, ldm, s);
     { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
       launch_gemm(hid, ldm, w.pdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
-    m->launches += 7;
+    m->launches += 6;
   }
   CU_LAUNCHED();
   return CIS2B_OK;
@@ -554,7 +559,7 @@ int prefill(cis2b_model *m, const std::vector<uint32_t> &tok, const std::vector<
   for (int c0 = 0; c0 < total; c0 += chunk, ++ci) {
     const int n = std::min(chunk, total - c0);
     rc = forward_rows(m, n, m->rows_tok.as<uint32_t>() + c0, m->rows_seq.as<int32_t>() + c0,
-                      m->rows_pos.as<int32_t>() + c0, n_seq_cache, maxP);
+                      m->rows_pos.as<int32_t>() + c0, n_seq_cache, maxP, false);
     if (rc) return rc;
     const auto &rg = ranges[(size_t)ci];
     if (rg.second) {
@@ -730,7 +735,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   // pointer (positions, ids, slot and step live in device memory), so the
   // step is captured once as a CUDA graph and replayed.
   auto step_body = [&]() -> int {
-    int r = forward_rows(m, B, d_next, m->d_seq.as<int32_t>(), m->d_pos.as<int32_t>(), B, maxP);
+    int r = forward_rows(m, B, d_next, m->d_seq.as<int32_t>(), m->d_pos.as<int32_t>(), B, maxP, true);
     if (r) return r;
     r = head_rows(m, m->h.as<float>(), B, ring_base, d_slot, (size_t)B * V);
     if (r) return r;
