@@ -25,6 +25,7 @@ CLI_PATH = os.path.join(PKG_DIR, "cis2b_ref")
 HEADER_PATH = os.path.join(ROOT_DIR, "include", "cis2b.h")
 
 SEQUENTIAL, TREE = 0, 1
+OP_MATMUL_DECODE = 2  # CIS2B_OP_MATMUL_DECODE: sequential order through the decode-step kernel
 PINNED_FUNCS = {"exp": 0, "sin": 1, "cos": 2, "ln": 3, "silu": 4, "rsqrt": 5}
 
 
@@ -199,13 +200,15 @@ def pinned_map(fn: str | int, x: np.ndarray, device: int = 0) -> np.ndarray:
     return y
 
 
-def matmul(W: np.ndarray, X: np.ndarray, tree: bool = False, device: int = 0) -> np.ndarray:
+def matmul(W: np.ndarray, X: np.ndarray, tree: bool = False, device: int = 0, decode: bool = False) -> np.ndarray:
+    """Y = X @ widen(W).T in the pinned order.  decode=True runs the
+    sequential order through the few-row kernel of the decode steps."""
     W = np.ascontiguousarray(W, dtype=np.uint16)
     X = np.ascontiguousarray(X, dtype=np.float32)
     rows, k = X.shape
     Y = np.zeros((rows, W.shape[0]), dtype=np.float32)
-    _check(lib().cis2b_op_matmul(device, _ptr(W), _ptr(X), rows, W.shape[0], k, TREE if tree else SEQUENTIAL,
-                                 _ptr(Y)))
+    mode = OP_MATMUL_DECODE if decode else (TREE if tree else SEQUENTIAL)
+    _check(lib().cis2b_op_matmul(device, _ptr(W), _ptr(X), rows, W.shape[0], k, mode, _ptr(Y)))
     return Y
 
 

@@ -84,6 +84,27 @@ __device__ __forceinline__ float serial_sum(const float *a, int n) {
   return acc;
 }
 
+// serial_sum for a 16-byte aligned array: the same adds, four operands per load.
+__device__ __forceinline__ float serial_sum4(const float *a, int n) {
+  const float4 *a4 = reinterpret_cast<const float4 *>(a);
+  float acc = 0.0f;
+  int q = 0;
+  for (; q + 8 <= n / 4; q += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = a4[q + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc = fadd(acc, v[u].x);
+      acc = fadd(acc, v[u].y);
+      acc = fadd(acc, v[u].z);
+      acc = fadd(acc, v[u].w);
+    }
+  }
+  for (int i = 4 * q; i < n; ++i) acc = fadd(acc, a[i]);
+  return acc;
+}
+
 // RMSNorm of one row by one warp (cis2_model.h:511-523):
 // sq = x*x; ss = fold(sq); mean = ss/n; inv = 1/sqrt(mean+eps); out = (x*inv)*w.
 // `sq` is warp-private shared scratch of 2n floats (squares, then a copy of
@@ -171,9 +192,84 @@ __global__ void k_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps,
   warp_rmsnorm(x + (size_t)r * ldx, w, eps, n, tree != 0, sm + (size_t)warp * 2 * n,
                out + (size_t)r * ors, ocs);
 }
+// Sequential-mode RMSNorm of up to 32 rows per block: the block stages its
+// rows in shared memory (row pitch n+4 floats, so the 16-byte loads of the
+// 32 lanes below hit distinct banks), lane r of warp 0 then runs row r's
+// dependent sum of squares -- 32 chains side by side, four squares per
+// load -- and every thread writes the scaled rows with coalesced stores.
+constexpr int RMS_ROWS = 32, RMS_THREADS = 256;
+__global__ void __launch_bounds__(RMS_THREADS, 1)
+k_rmsnorm_rows(const float *__restrict__ x, int ldx, const uint16_t *__restrict__ w, float eps, int n, int rows,
+               float *__restrict__ out, int ors, int ocs) {
+  extern __shared__ __align__(16) float sm[];  // [RMS_ROWS][n + 4], then [RMS_ROWS] inv
+  const int P = n + 4, nq = n / 4;
+  float *inv_s = sm + RMS_ROWS * P;
+  const int r0 = blockIdx.x * RMS_ROWS;
+  const int nr = min(RMS_ROWS, rows - r0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = RMS_THREADS / 32;
+  const uint32_t sb = (uint32_t)__cvta_generic_to_shared(sm);
+  for (int r = warp; r < nr; r += nw)
+    for (int q = lane; q < nq; q += 32)
+      cp_async16(sb + (uint32_t)((r * P + 4 * q) * 4), x + (size_t)(r0 + r) * ldx + 4 * q);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  if (threadIdx.x < nr) {
+    const float4 *row = reinterpret_cast<const float4 *>(sm + threadIdx.x * P);
+    float acc = 0.0f;
+    int q = 0;
+    for (; q + 8 <= nq; q += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = row[q + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc = fadd(acc, fmul(v[u].x, v[u].x));
+        acc = fadd(acc, fmul(v[u].y, v[u].y));
+        acc = fadd(acc, fmul(v[u].z, v[u].z));
+        acc = fadd(acc, fmul(v[u].w, v[u].w));
+      }
+    }
+    for (; q < nq; ++q) {
+      const float4 v = row[q];
+      acc = fadd(acc, fmul(v.x, v.x));
+      acc = fadd(acc, fmul(v.y, v.y));
+      acc = fadd(acc, fmul(v.z, v.z));
+      acc = fadd(acc, fmul(v.w, v.w));
+    }
+    const float mean = fdiv(acc, __int2float_rn(n));
+    inv_s[threadIdx.x] = rsqrt_cr(fadd(mean, eps));
+  }
+  __syncthreads();
+  if (ocs == 1) {  // row-major out: a warp per row, lanes along k
+    for (int r = warp; r < nr; r += nw) {
+      const float inv = inv_s[r];
+      float *o = out + (size_t)(r0 + r) * ors;
+      for (int k = lane; k < n; k += 32) o[k] = fmul(fmul(sm[r * P + k], inv), widen_bf16(w[k]));
+    }
+  } else {  // k-major out: lanes along rows, warps along k
+    if (lane < nr) {
+      const float inv = inv_s[lane];
+      for (int k = warp; k < n; k += nw)
+        out[(size_t)(r0 + lane) * ors + (size_t)k * ocs] = fmul(fmul(sm[lane * P + k], inv), widen_bf16(w[k]));
+    }
+  }
+}
+
 void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
                     float *out, int ors, int ocs, cudaStream_t s) {
   if (rows <= 0) return;
+  const size_t rsm = ((size_t)RMS_ROWS * (n + 4) + RMS_ROWS) * sizeof(float);
+  if (!tree && n % 4 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && rsm <= 227 * 1024) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      attr = true;
+    }
+    k_rmsnorm_rows<<<(rows + RMS_ROWS - 1) / RMS_ROWS, RMS_THREADS, rsm, s>>>(x, ldx, w, eps, n, rows, out, ors,
+                                                                              ocs);
+    return;
+  }
   const int wpb = 4;
   k_rmsnorm<<<(rows + wpb - 1) / wpb, 32 * wpb, (size_t)wpb * 2 * n * sizeof(float), s>>>(
       x, ldx, w, eps, n, rows, tree ? 1 : 0, out, ors, ocs);
@@ -249,7 +345,7 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t saddr, const void *g, 
 }
 
 template <int BM, int BP, int TM, int TN, bool TREE>
-__global__ void __launch_bounds__((BM / TM) * (8 * BP / TN))
+__global__ void __launch_bounds__((BM / TM) * (8 * BP / TN), 1)
 k_gemm_t(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp, int K, int N, int M,
          float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
          size_t y_slot_stride) {
@@ -481,6 +577,230 @@ void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t
 }
 size_t panel_elems(int N, int K) { return (size_t)((N + 7) / 8) * 8 * (size_t)K; }
 
+// ============================================================ decode GEMM
+//
+// Few activation rows (one per sequence at a decode step) against a large
+// weight matrix.  Lanes own output COLUMNS: lane j of a warp produces
+// column 32*tile + j for TM rows, walking k = 0..K-1 in order for each.
+// Per four k a lane reads its column's four weights with one 8-byte shared
+// load and each row's four activations with one broadcast 16-byte load, so
+// every shared load feeds at least four multiply-adds.  Rows are split over
+// the RW warps of a block; all RW*TM rows of the block sit in shared memory
+// for the whole K, weights stream through a STAGES-deep cp.async ring.
+//
+// Operand layouts:
+//   X   [M][ldx] fp32  row-major activations (ldx % 4 == 0)
+//   Wt  [N32][K/4][32][4] bf16  32-column tiles, four consecutive k of a
+//       column contiguous (same bf16 bits as the checkpoint's [N][K]);
+//       K % 4 == 0, zero columns past N.
+// The products of four k are formed as two packed pairs (mul.f32x2: two
+// independent, separately rounded products) and added to the accumulator
+// one at a time, k ascending, exactly as dot_seq does.
+constexpr int DEC_KC = 64;      // k per weight stage
+constexpr int DEC_STAGES = 6;
+
+__host__ __device__ size_t tile32_elems(int N, int K) { return (size_t)((N + 31) / 32) * 32 * (size_t)K; }
+
+// Wt[n32][kq][j][q] = W[src(n32, j)][4*kq + q] with src = 32*n32 + j, or,
+// for a gate/up pair (glu_half = I, N = 2I), gate row 16*n32 + j in lanes
+// 0..15 and up row I + 16*n32 + j - 16 in lanes 16..31.
+__global__ void k_tile32(const uint16_t *W, int N, int K, uint16_t *Wt, int glu_half) {
+  const size_t total = tile32_elems(N, K);
+  const size_t KQ = (size_t)K / 4;
+  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const size_t q = idx % 4, j = (idx / 4) % 32, kq = (idx / 128) % KQ, n32 = idx / 128 / KQ;
+    const size_t n = glu_half ? (j < 16 ? n32 * 16 + j : (size_t)glu_half + n32 * 16 + j - 16) : n32 * 32 + j;
+    Wt[idx] = n < (size_t)N ? W[n * K + kq * 4 + q] : (uint16_t)0;
+  }
+}
+void launch_tile32(const uint16_t *W, int N, int K, uint16_t *Wt, cudaStream_t s, int glu_half) {
+  k_tile32<<<1184, 256, 0, s>>>(W, N, K, Wt, glu_half);
+}
+
+__device__ __forceinline__ float2 fmul_pair(float a0, float a1, float b0, float b1) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rr;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.ftz.f32x2 rr, ra, rb;\n\tmov.b64 {%0, %1}, rr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  return r;
+}
+__device__ __forceinline__ float4 widen4(uint2 u) {
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
+template <int TM, int RW>
+__global__ void __launch_bounds__(32 * RW, 1)
+k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt, int K, int N, int M,
+           float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
+           size_t y_slot_stride, int glu) {
+  constexpr int ROWS = TM * RW, NT = 32 * RW;
+  constexpr int WST = DEC_KC * 32;  // bf16 per weight stage
+  constexpr int PF = 2;             // register prefetch distance in groups of four k
+  extern __shared__ __align__(16) float smem[];
+  float *Xs = smem;                                                   // [ROWS][K]
+  uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + (size_t)ROWS * K);  // [STAGES][KC/4][32][4]
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int n32 = blockIdx.x, m0 = blockIdx.y * ROWS;
+  const uint16_t *Wtile = Wt + (size_t)n32 * K * 32;
+  const uint32_t xs_b = (uint32_t)__cvta_generic_to_shared(Xs);
+  const uint32_t ws_b = (uint32_t)__cvta_generic_to_shared(Ws);
+  const int nc = (K + DEC_KC - 1) / DEC_KC;
+  const int KQ = K / 4;
+
+  // The block's rows, whole K (rows past M are zero-filled), in group 0.
+  for (int i = tid; i < ROWS * KQ; i += NT) {
+    const int r = i / KQ, q = i - r * KQ;
+    const bool ok = m0 + r < M;
+    cp_async16_zfill(xs_b + (uint32_t)((r * K + 4 * q) * 4), ok ? X + (size_t)(m0 + r) * ldx + 4 * q : X, ok);
+  }
+  auto issue_w = [&](int c) {
+    const int slot = c % DEC_STAGES, k0 = c * DEC_KC;
+    const int nchunk = min(DEC_KC, K - k0) * 4;  // 16-byte pieces: kn * 32 bf16 * 2 B / 16
+    for (int i = tid; i < nchunk; i += NT)
+      cp_async16(ws_b + (uint32_t)(slot * WST * 2 + i * 16), Wtile + (size_t)k0 * 32 + (size_t)i * 8);
+  };
+#pragma unroll
+  for (int s = 0; s < DEC_STAGES - 1; ++s) {
+    if (s < nc) issue_w(s);
+    cp_async_commit();
+  }
+
+  float acc[TM];
+#pragma unroll
+  for (int i = 0; i < TM; ++i) acc[i] = 0.0f;
+  const float *xw = Xs + (size_t)(w * TM) * K;
+  for (int c = 0; c < nc; ++c) {
+    cp_async_wait<DEC_STAGES - 2>();
+    __syncthreads();
+    if (c + DEC_STAGES - 1 < nc) issue_w(c + DEC_STAGES - 1);
+    cp_async_commit();
+    const uint2 *wsl = reinterpret_cast<const uint2 *>(Ws + (c % DEC_STAGES) * WST) + lane;
+    const float *xc = xw + c * DEC_KC;
+    const int kn = min(DEC_KC, K - c * DEC_KC);
+    if (kn == DEC_KC) {
+      constexpr int NQ = DEC_KC / 4;
+      float4 xb[PF][TM], wb[PF];
+      auto ld = [&](int sl, int kq) {
+        wb[sl] = widen4(wsl[kq * 32]);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) xb[sl][i] = *reinterpret_cast<const float4 *>(xc + (size_t)i * K + 4 * kq);
+      };
+#pragma unroll
+      for (int q = 0; q < PF; ++q) ld(q, q);
+#pragma unroll
+      for (int kq = 0; kq < NQ; ++kq) {
+        const int sl = kq % PF;
+        const float4 wv = wb[sl];
+        float4 xv[TM];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) xv[i] = xb[sl][i];
+        if (kq + PF < NQ) ld(sl, kq + PF);
+        float2 p01[TM], p23[TM];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          p01[i] = fmul_pair(wv.x, wv.y, xv[i].x, xv[i].y);
+          p23[i] = fmul_pair(wv.z, wv.w, xv[i].z, xv[i].w);
+        }
+#pragma unroll
+        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p01[i].x);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p01[i].y);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p23[i].x);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p23[i].y);
+      }
+    } else {
+      for (int kq = 0; kq < kn / 4; ++kq) {
+        const float4 wv = widen4(wsl[kq * 32]);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          const float4 xv = *reinterpret_cast<const float4 *>(xc + (size_t)i * K + 4 * kq);
+          acc[i] = fadd(acc[i], fmul(wv.x, xv.x));
+          acc[i] = fadd(acc[i], fmul(wv.y, xv.y));
+          acc[i] = fadd(acc[i], fmul(wv.z, xv.z));
+          acc[i] = fadd(acc[i], fmul(wv.w, xv.w));
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  if (glu) {
+    // Gate/up tile: lane j < 16 holds gate 16*n32 + j, lane j + 16 its up.
+    const int col = n32 * 16 + lane;
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const int m = m0 + w * TM + i;
+      if (m >= M) break;
+      const float up = __shfl_down_sync(FULL, acc[i], 16);
+      if (lane < 16 && col < glu) Y[(size_t)m * ldy + col] = fmul(silu_pinned(acc[i]), up);  // cis2_model.h:619-623
+    }
+    return;
+  }
+  const int n = n32 * 32 + lane;
+  if (n >= N) return;
+  float *Yb = Y + (y_slot ? (size_t)(*y_slot) * y_slot_stride : 0);
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int m = m0 + w * TM + i;
+    if (m >= M) break;
+    float v = acc[i];
+    if (R) v = fadd(R[(size_t)m * ldr + n], v);  // residual h + o (cis2_model.h:540-542)
+    Yb[(size_t)m * ldy + n] = v;
+  }
+}
+
+template <int TM, int RW>
+static void run_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, int M, float *Y, int ldy,
+                         const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
+                         cudaStream_t s) {
+  constexpr int ROWS = TM * RW;
+  const size_t smem = (size_t)ROWS * K * 4 + (size_t)DEC_STAGES * DEC_KC * 32 * 2;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_gemm_dec<TM, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr_set = true;
+  }
+  dim3 grid((N + 31) / 32, (M + ROWS - 1) / ROWS);
+  k_gemm_dec<TM, RW><<<grid, 32 * RW, smem, s>>>(X, ldx, Wt, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride, glu);
+}
+
+// Rows per block: the largest candidate that still gives at least two
+// blocks per SM and whose rows fit shared memory next to the weight ring.
+struct DecCfg { int tm, rw; };
+static const DecCfg kDecTiles[] = {{8, 4}, {4, 4}, {2, 4}, {2, 2}};
+constexpr int kNumDecTiles = 4;
+
+bool gemm_dec_ok(int K) { return K > 0 && K % 4 == 0 && (size_t)4 * K * 4 + DEC_STAGES * DEC_KC * 64 <= 227 * 1024; }
+
+int gemm_dec_choice(int M, int N, int K) {
+  const long n32 = (N + 31) / 32;
+  int pick = -1;
+  for (int i = 0; i < kNumDecTiles; ++i) {
+    const int rows = kDecTiles[i].tm * kDecTiles[i].rw;
+    if ((size_t)rows * K * 4 + (size_t)DEC_STAGES * DEC_KC * 64 > 227 * 1024) continue;
+    pick = i;
+    if (n32 * ((M + rows - 1) / rows) >= 2 * 148) break;
+  }
+  return pick;
+}
+
+void launch_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, int M, float *Y, int ldy,
+                     const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s,
+                     int glu) {
+  if (M <= 0 || N <= 0) return;
+  switch (gemm_dec_choice(M, N, K)) {
+    case 0: run_gemm_dec<8, 4>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
+    case 1: run_gemm_dec<4, 4>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
+    case 2: run_gemm_dec<2, 4>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
+    default: run_gemm_dec<2, 2>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
+  }
+}
+
 // ============================================================ attention
 
 // Per row: optional per-head q/k RMSNorm (qwen3-port.diff:66-80), RoPE of
@@ -553,7 +873,8 @@ __device__ __forceinline__ float max_comb(float a, float b) {
 constexpr int ATT_JC = 64;
 
 size_t attention_smem_floats(int G, int hd, int max_len) {
-  size_t f = (size_t)G * hd + (size_t)G * max_len + (size_t)G * (max_len / 32 + 1) + 64;
+  const size_t scs = ((size_t)max_len + 3) & ~(size_t)3;  // score rows start 16-byte aligned
+  size_t f = (size_t)G * hd + (size_t)G * scs + (size_t)G * (max_len / 32 + 1) + 64;
   f = (f + 3) & ~(size_t)3;                              // tiles start 16-byte aligned
   return f + (size_t)2 * ATT_JC * (hd + 4);
 }
@@ -569,9 +890,10 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
   const int G = nh / nkv, KV = nkv * hd;
   const int seq = rseq[r], pos = rpos[r], len = pos + 1;
   const int nb = (len + 31) / 32;
+  const int scs = (max_len + 3) & ~3;         // score row stride (16-byte aligned rows)
   float *q = sm;                              // [G][hd]
-  float *sc = q + G * hd;                     // [G][max_len]
-  float *part = sc + (size_t)G * max_len;     // [G][max_len/32 + 1]
+  float *sc = q + G * hd;                     // [G][scs]
+  float *part = sc + (size_t)G * scs;         // [G][max_len/32 + 1]
   float *red = part + (size_t)G * (max_len / 32 + 1);  // [64]
   size_t toff = (size_t)(red + 64 - sm);
   toff = (toff + 3) & ~(size_t)3;
@@ -637,20 +959,34 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
       const float *qg = q + g * hd, *kj = tile + jj * ts;
       float d;
       if (!tree) {
+        // 16-byte loads (hd % 4 == 0; the key rows' pitch hd+4 keeps the 32
+        // lanes' rows on distinct banks), four k per load, k ascending.
+        const float4 *q4 = reinterpret_cast<const float4 *>(qg), *k4 = reinterpret_cast<const float4 *>(kj);
         d = 0.0f;
         int i = 0;
-        for (; i + 16 <= hd; i += 16) {
-          float a[16], b[16];
+        for (; i + 4 <= hd / 4; i += 4) {
+          float4 a[4], b[4];
 #pragma unroll
-          for (int u = 0; u < 16; ++u) { a[u] = qg[i + u]; b[u] = kj[i + u]; }
+          for (int u = 0; u < 4; ++u) { a[u] = q4[i + u]; b[u] = k4[i + u]; }
 #pragma unroll
-          for (int u = 0; u < 16; ++u) d = fadd(d, fmul(a[u], b[u]));
+          for (int u = 0; u < 4; ++u) {
+            d = fadd(d, fmul(a[u].x, b[u].x));
+            d = fadd(d, fmul(a[u].y, b[u].y));
+            d = fadd(d, fmul(a[u].z, b[u].z));
+            d = fadd(d, fmul(a[u].w, b[u].w));
+          }
         }
-        for (; i < hd; ++i) d = fadd(d, fmul(qg[i], kj[i]));
+        for (; i < hd / 4; ++i) {
+          const float4 a = q4[i], b = k4[i];
+          d = fadd(d, fmul(a.x, b.x));
+          d = fadd(d, fmul(a.y, b.y));
+          d = fadd(d, fmul(a.z, b.z));
+          d = fadd(d, fmul(a.w, b.w));
+        }
       } else {
         d = dot_tree(qg, kj, hd);
       }
-      sc[(size_t)g * max_len + j0 + jj] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
+      sc[(size_t)g * scs + j0 + jj] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
     }
     __syncthreads();
   }
@@ -658,7 +994,7 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
   stage(vbase, 0, 0);
   // ---- max per head (serial-scan semantics, see max_comb)
   for (int g = warp; g < G; g += nw) {
-    const float *sg = sc + (size_t)g * max_len;
+    const float *sg = sc + (size_t)g * scs;
     float m = bitsf(0x7fc00000u);
     for (int j = lane; j < len; j += 32) m = max_comb(m, sg[j]);
 #pragma unroll
@@ -668,7 +1004,7 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
   __syncthreads();
   for (int i = tid; i < G * len; i += nt) {
     const int g = i / len, j = i - g * len;
-    float *p = sc + (size_t)g * max_len + j;
+    float *p = sc + (size_t)g * scs + j;
     *p = exp_pinned(fsub(*p, red[g]));
   }
   __syncthreads();
@@ -676,7 +1012,7 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
   if (tree) {
     for (int pb = warp; pb < G * nb; pb += nw) {
       const int g = pb / nb, b = pb - g * nb, j = b * 32 + lane;
-      float v = warp_tree32(j < len ? sc[(size_t)g * max_len + j] : 0.0f);
+      float v = warp_tree32(j < len ? sc[(size_t)g * scs + j] : 0.0f);
       if (lane == 0) part[(size_t)g * (max_len / 32 + 1) + b] = v;
     }
     __syncthreads();
@@ -684,7 +1020,7 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
   for (int g = warp; g < G; g += nw) {
     if (lane == 0) {
       float acc;
-      if (!tree) acc = serial_sum(sc + (size_t)g * max_len, len);
+      if (!tree) acc = serial_sum4(sc + (size_t)g * scs, len);
       else acc = serial_sum(part + (size_t)g * (max_len / 32 + 1), nb);
       red[32 + g] = acc;
     }
@@ -692,37 +1028,59 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
   __syncthreads();
   for (int i = tid; i < G * len; i += nt) {
     const int g = i / len, j = i - g * len;
-    float *p = sc + (size_t)g * max_len + j;
+    float *p = sc + (size_t)g * scs + j;
     *p = fdiv(*p, red[32 + g]);
   }
-  // ---- V-mix, V streamed through the two tile buffers
-  const int gd = tid;                  // (g, d) chain owned by this thread
-  const int g = gd / hd, d = gd - (gd / hd) * hd;
-  const bool owns = gd < G * hd;
-  float acc = 0.0f;
+  // ---- V-mix, V streamed through the two tile buffers.  A thread owns the
+  // four chains (g, d..d+3): one 16-byte load of V per position feeds four
+  // multiply-adds, and the weights come four positions per broadcast load.
+  const int hd4 = hd / 4;
+  const int g = tid / hd4, d = 4 * (tid - (tid / hd4) * hd4);
+  const bool owns = tid < G * hd4;
+  float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
   for (int c = 0; c < nch; ++c) {
     if (c + 1 < nch) stage(vbase, c + 1, (c + 1) & 1);
     else cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
     const int j0 = c * ATT_JC, jc = min(ATT_JC, len - j0);
-    const float *tile = tiles + (size_t)(c & 1) * ATT_JC * ts;
+    const float *tile = tiles + (size_t)(c & 1) * ATT_JC * ts + d;
     if (owns) {
-      const float *pg = sc + (size_t)g * max_len + j0;
+      const float *pg = sc + (size_t)g * scs + j0;  // j0 % 4 == 0: 16-byte aligned
       int jj = 0;
-      for (; jj + 16 <= jc; jj += 16) {
-        float a[16], b[16];
+      for (; jj + 4 <= jc; jj += 4) {
+        const float4 pw = *reinterpret_cast<const float4 *>(pg + jj);
+        float4 v[4];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) { a[u] = pg[jj + u]; b[u] = tile[(jj + u) * ts + d]; }
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4 *>(tile + (jj + u) * ts);
+        const float pu[4] = {pw.x, pw.y, pw.z, pw.w};
 #pragma unroll
-        for (int u = 0; u < 16; ++u) acc = fadd(acc, fmul(a[u], b[u]));
+        for (int u = 0; u < 4; ++u) {
+          acc0 = fadd(acc0, fmul(pu[u], v[u].x));
+          acc1 = fadd(acc1, fmul(pu[u], v[u].y));
+          acc2 = fadd(acc2, fmul(pu[u], v[u].z));
+          acc3 = fadd(acc3, fmul(pu[u], v[u].w));
+        }
       }
-      for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * ts + d]));
+      for (; jj < jc; ++jj) {
+        const float pj = pg[jj];
+        const float4 v = *reinterpret_cast<const float4 *>(tile + jj * ts);
+        acc0 = fadd(acc0, fmul(pj, v.x));
+        acc1 = fadd(acc1, fmul(pj, v.y));
+        acc2 = fadd(acc2, fmul(pj, v.z));
+        acc3 = fadd(acc3, fmul(pj, v.w));
+      }
     }
     __syncthreads();
   }
   cp_async_wait<0>();
-  if (owns) att[(size_t)r * ars + ((size_t)kvh * G + g) * hd * acs + (size_t)d * acs] = acc;
+  if (owns) {
+    float *o = att + (size_t)r * ars + ((size_t)kvh * G + g) * hd * acs + (size_t)d * acs;
+    o[0] = acc0;
+    o[acs] = acc1;
+    o[2 * (size_t)acs] = acc2;
+    o[3 * (size_t)acs] = acc3;
+  }
 }
 
 void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
@@ -1126,9 +1484,12 @@ __device__ __forceinline__ uint32_t step_word(const uint8_t *carry, int c, const
   return w;
 }
 
+// W+K scratch: [block][warp][16 quads][32 lanes] uint4, so each step of the
+// chain reads 512 contiguous bytes per warp and finds quad qd at a fixed
+// offset from its block pointer.
 size_t sha_wk_words(int V, int n_seq) {
   size_t nb_max = ((size_t)63 + 4 * (size_t)V + 4) / 64;
-  return nb_max * 64 * (size_t)n_seq;
+  return nb_max * 64 * (size_t)((n_seq + 31) / 32 * 32);
 }
 
 // Expand W+K for every full block of this step.  Layout [block][16 quads][seq]
@@ -1148,10 +1509,11 @@ __global__ void k_sha_prep(const ShaState *st, int n_seq, const float *logits, i
   for (int i = 0; i < 16; ++i) m[i] = step_word(st[s].carry, c, data, V, id, 64 * j + 4 * i);
   uint32_t w[64];
   sha_expand_wk(m, w);
-  uint4 *out = reinterpret_cast<uint4 *>(wk);
+  const int nw = (n_seq + 31) / 32;
+  uint4 *out = reinterpret_cast<uint4 *>(wk) + ((size_t)j * nw + s / 32) * 16 * 32 + (s & 31);
 #pragma unroll
   for (int qd = 0; qd < 16; ++qd)
-    out[((size_t)j * 16 + qd) * n_seq + s] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
+    out[qd * 32] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
 }
 
 // The chain: one thread per sequence compresses the step's blocks in order,
@@ -1173,9 +1535,10 @@ constexpr size_t SHA_SMEM = (size_t)227 * 1024;                              // 
 static_assert(SHA_WARPS * SHA_STAGES * SHA_STAGE_BYTES <= SHA_SMEM, "witness pipeline exceeds smem");
 
 
-__global__ void __launch_bounds__(32 * SHA_WARPS)
+__global__ void __launch_bounds__(32 * SHA_WARPS, 1)
 k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
-               const uint32_t *next_ids, const uint32_t *wk, uint8_t *digest_out, size_t digest_stride) {
+               const uint32_t *next_ids, const uint32_t *wk, uint8_t *digest_out, size_t digest_stride,
+               uint32_t one) {
   extern __shared__ uint4 smem_all[];  // [warp][SHA_STAGES][16][32 lanes]
   const int lane = threadIdx.x & 31;
   uint4 *stg = smem_all + (size_t)(threadIdx.x >> 5) * SHA_STAGES * 16 * 32;
@@ -1185,34 +1548,43 @@ k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_s
   const int c = (int)S.carry_n;
   const int total = c + 4 * V + 4;
   const int nb = total / 64;
-  const uint4 *in = reinterpret_cast<const uint4 *>(wk);
-  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(stg);
+  // This lane's quad qd of block j is at src + j * bstride + qd * 32 (uint4).
+  const int nw = (n_seq + 31) / 32;
+  const uint4 *src = reinterpret_cast<const uint4 *>(wk) + (size_t)(s / 32) * 16 * 32 + lane;
+  const size_t bstride = (size_t)nw * 16 * 32;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(stg) + (uint32_t)lane * 16;
   uint32_t h[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) h[i] = S.h[i];
-  auto issue = [&](int j) {
-    if (j < nb) {
-      const int slot = j % SHA_STAGES;
+  // Stage slot k holds quads at sbase + (k*16 + qd) * 512 bytes (lane-interleaved).
+  const uint4 *next_src = src;
+  int next_j = 0, issue_slot = 0;
+  auto issue = [&]() {
+    if (next_j < nb) {
+      const uint32_t d0 = sbase + (uint32_t)issue_slot * 16 * 512;
 #pragma unroll
-      for (int qd = 0; qd < 16; ++qd)
-        cp_async16(sbase + (uint32_t)(((slot * 16 + qd) * 32 + lane) * 16),
-                   in + ((size_t)j * 16 + qd) * n_seq + s);
+      for (int qd = 0; qd < 16; ++qd) cp_async16(d0 + (uint32_t)qd * 512, next_src + qd * 32);
     }
     cp_async_commit();  // empty groups keep the per-thread group count uniform
+    next_src += bstride;
+    ++next_j;
+    issue_slot = issue_slot == SHA_STAGES - 1 ? 0 : issue_slot + 1;
   };
 #pragma unroll
-  for (int j = 0; j < SHA_STAGES - 1; ++j) issue(j);
+  for (int j = 0; j < SHA_STAGES - 1; ++j) issue();
+  int slot = 0;
   for (int j = 0; j < nb; ++j) {
-    issue(j + SHA_STAGES - 1);
+    issue();
     cp_async_wait<SHA_STAGES - 1>();
-    const uint4 *src = stg + (size_t)(j % SHA_STAGES) * 16 * 32 + lane;
+    const uint4 *blk = stg + (size_t)slot * 16 * 32 + lane;
     uint32_t w[64];
 #pragma unroll
     for (int qd = 0; qd < 16; ++qd) {
-      uint4 v = src[qd * 32];
+      uint4 v = blk[qd * 32];
       w[4 * qd] = v.x; w[4 * qd + 1] = v.y; w[4 * qd + 2] = v.z; w[4 * qd + 3] = v.w;
     }
-    sha_compress_wk(h, w);
+    sha_compress_wk_m(h, w, one);
+    slot = slot == SHA_STAGES - 1 ? 0 : slot + 1;
   }
   cp_async_wait<0>();
   // New carry = stream bytes [64*nb, total).
@@ -1255,7 +1627,7 @@ void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, si
   const int per_cta = warps < SHA_WARPS ? warps : SHA_WARPS;
   const int ctas = (warps + per_cta - 1) / per_cta;
   k_sha_compress<<<ctas, 32 * per_cta, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
-                                                      wk_scratch, step_digest_out, digest_stride);
+                                                      wk_scratch, step_digest_out, digest_stride, 1u);
 }
 void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                      const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,

@@ -82,11 +82,13 @@ struct LayerW {
   const uint16_t *in_norm, *post_norm, *wqkv, *wo, *wgu, *wdown;  // row-major [N][K] as on disk
   const uint16_t *q_norm, *k_norm, *q_bias, *k_bias, *v_bias;
   const uint16_t *pqkv, *po, *pgu, *pdown;  // the same weights in GEMM panel layout
+  const uint16_t *tqkv, *to, *tgu, *tdown;  // and in 32-column decode tiles (sequential mode)
 };
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 constexpr int PREFILL_CHUNK = 8192;            // rows per prefill pass
+constexpr int DEC_HEAD_ROWS = 1024;            // lm_head rows up to which the decode GEMM is used
 constexpr size_t RING_BUDGET = 8ull << 30;     // bytes of logits kept for the witness
 
 }  // namespace
@@ -102,6 +104,9 @@ struct cis2b_model {
   DevBuf arena;   // all weights as on disk (embedding rows, norms, biases are read from here)
   DevBuf panels;  // GEMM weights re-laid in 8-row k-major panels
   const uint16_t *lm_head_p = nullptr;
+  DevBuf tiles;   // the same weights in 32-column tiles for the decode GEMM
+  const uint16_t *lm_head_t = nullptr;
+  bool dec_tiles = false;  // decode steps use launch_gemm_dec (sequential mode, K % 4 == 0)
   DevBuf inv_freq, cos_t, sin_t;
   cudaStream_t s_main = nullptr, s_sha = nullptr;
   // workspace
@@ -401,6 +406,45 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
     CU(cudaStreamSynchronize(m->s_main));
   }
 
+  // ---- decode tiles (same bf16 bits, 32 columns x 4 k per lane-row)
+  m->dec_tiles = !m->tree && gemm_dec_ok(m->H) && gemm_dec_ok(m->QD) && gemm_dec_ok(m->I) && m->I % 16 == 0;
+  if (m->dec_tiles) {
+    const int NQKV = m->QD + 2 * m->KVD;
+    size_t total = 0;
+    auto reserve = [&](int N, int K) {
+      size_t off = total;
+      total += (tile32_elems(N, K) * 2 + 255) & ~(size_t)255;
+      return off;
+    };
+    std::vector<size_t> offs;
+    for (int l = 0; l < m->L; ++l) {
+      offs.push_back(reserve(NQKV, m->H));
+      offs.push_back(reserve(m->H, m->QD));
+      offs.push_back(reserve(2 * m->I, m->H));
+      offs.push_back(reserve(m->H, m->I));
+    }
+    size_t off_lm = reserve(m->V, m->H);
+    if (m->tiles.ensure(total) != cudaSuccess)
+      return fail(CIS2B_ERR_NOMEM, "device allocation of the decode weight tiles failed");
+    uint16_t *tb = m->tiles.as<uint16_t>();
+    auto tat = [&](size_t off) { return tb + off / 2; };
+    for (int l = 0; l < m->L; ++l) {
+      LayerW &w = m->layers[(size_t)l];
+      w.tqkv = tat(offs[4 * l]);
+      w.to = tat(offs[4 * l + 1]);
+      w.tgu = tat(offs[4 * l + 2]);
+      w.tdown = tat(offs[4 * l + 3]);
+      launch_tile32(w.wqkv, NQKV, m->H, const_cast<uint16_t *>(w.tqkv), m->s_main);
+      launch_tile32(w.wo, m->H, m->QD, const_cast<uint16_t *>(w.to), m->s_main);
+      launch_tile32(w.wgu, 2 * m->I, m->H, const_cast<uint16_t *>(w.tgu), m->s_main, m->I);
+      launch_tile32(w.wdown, m->H, m->I, const_cast<uint16_t *>(w.tdown), m->s_main);
+    }
+    m->lm_head_t = tat(off_lm);
+    launch_tile32(m->lm_head, m->V, m->H, const_cast<uint16_t *>(m->lm_head_t), m->s_main);
+    CU_LAUNCHED();
+    CU(cudaStreamSynchronize(m->s_main));
+  }
+
   // ---- pinned tables on the device (cis2_model.h:456-476, 547-568)
   const int half = m->HD / 2;
   if (m->inv_freq.ensure(sizeof(float) * half) != cudaSuccess ||
@@ -458,13 +502,23 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
   RowMap rm{seq, pos};
   launch_embed(m->embed, H, tok, rows, h, s);
   m->launches += 1;
+  // Decode steps in sequential mode run the GEMMs in the few-row form: its
+  // activations are row-major, so every producer writes (row stride K, 1).
+  const bool dec = decode && m->dec_tiles;
+  const int lnr = dec ? H : 1, lnc = dec ? 1 : ldm;      // ln / att / hid (row, column) strides
+  const int atr = dec ? QD : 1, hir = dec ? I : 1;
+  auto gemm = [&](const float *X, const uint16_t *Wp, const uint16_t *Wt, int K, int N, float *Y, int ldy,
+                  const float *R, int ldr) {
+    ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+    if (dec) launch_gemm_dec(X, K, Wt, K, N, rows, Y, ldy, R, ldr, nullptr, 0, s);
+    else launch_gemm(X, ldm, Wp, K, N, rows, Y, ldy, R, ldr, m->tree, nullptr, 0, s);
+  };
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[(size_t)l];
     float *kc = m->kc.as<float>() + (size_t)l * layer_kv;
     float *vc = m->vc.as<float>() + (size_t)l * layer_kv;
-    launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, 1, ldm, s);
-    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(ln, ldm, w.pqkv, H, NQKV, rows, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s); }
+    launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, lnr, lnc, s);
+    gemm(ln, w.pqkv, w.tqkv, H, NQKV, qkv, NQKV, nullptr, 0);
     m->launches += 2;
     if (w.q_bias) { launch_add_bias(qkv, NQKV, rows, w.q_bias, QD, s); m->launches++; }
     if (w.k_bias) { launch_add_bias(qkv + QD, NQKV, rows, w.k_bias, KVD, s); m->launches++; }
@@ -475,17 +529,21 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
       m->launches++;
     }
     { ProfScope p(m, CIS2B_PROF_ATTENTION, s);
-      launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, 1, ldm, maxP,
-                       decode, w.q_norm, w.k_norm, m->eps, m->cos_t.as<float>(), m->sin_t.as<float>(), s); }
-    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(att, ldm, w.po, QD, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
-    launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, 1, ldm, s);
-    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(ln, ldm, w.pgu, H, 2 * I, rows, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s); }
-    launch_silu_mul(gu, I, rows, hid, 1, ldm, s);
-    { ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm(hid, ldm, w.pdown, I, H, rows, h, H, h, H, m->tree, nullptr, 0, s); }
-    m->launches += 6;
+      launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, atr,
+                       dec ? 1 : ldm, maxP, decode, w.q_norm, w.k_norm, m->eps, m->cos_t.as<float>(),
+                       m->sin_t.as<float>(), s); }
+    gemm(att, w.po, w.to, QD, H, h, H, h, H);
+    launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, lnr, lnc, s);
+    if (dec) {  // SwiGLU in the gate/up GEMM's epilogue
+      ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+      launch_gemm_dec(ln, H, w.tgu, H, 2 * I, rows, hid, I, nullptr, 0, nullptr, 0, s, I);
+    } else {
+      gemm(ln, w.pgu, w.tgu, H, 2 * I, gu, 2 * I, nullptr, 0);
+      launch_silu_mul(gu, I, rows, hid, hir, ldm, s);
+      m->launches++;
+    }
+    gemm(hid, w.pdown, w.tdown, I, H, h, H, h, H);
+    m->launches += 5;
   }
   CU_LAUNCHED();
   return CIS2B_OK;
@@ -495,12 +553,18 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
 int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_t *y_slot,
               size_t slot_stride) {
   cudaStream_t s = m->s_main;
-  const int ldb = round_up(rows, 64);  // lnlast is k-major [H][ldb]
-  launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(), 1, ldb, s);
+  const int ldb = round_up(rows, 64);  // lnlast is k-major [H][ldb] for the panel GEMM
+  const bool dec = m->dec_tiles && rows <= DEC_HEAD_ROWS;  // row-major [rows][H] for the decode GEMM
+  launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(),
+                 dec ? m->H : 1, dec ? 1 : ldb, s);
   {
     ProfScope p(m, CIS2B_PROF_LM_HEAD, s);
-    launch_gemm(m->lnlast.as<float>(), ldb, m->lm_head_p, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
-                y_slot, slot_stride, s);
+    if (dec)
+      launch_gemm_dec(m->lnlast.as<float>(), m->H, m->lm_head_t, m->H, m->V, rows, Y, m->V, nullptr, 0, y_slot,
+                      slot_stride, s);
+    else
+      launch_gemm(m->lnlast.as<float>(), ldb, m->lm_head_p, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
+                  y_slot, slot_stride, s);
   }
   m->launches += 2;
   CU_LAUNCHED();
@@ -966,7 +1030,25 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
                     int32_t reduction, float *Y) {
   if (!W || !X || !Y) return fail(CIS2B_ERR_ARG, "NULL buffer");
   if (rows <= 0 || n_out <= 0 || k <= 0 || k % 8) return fail(CIS2B_ERR_ARG, "bad shape (k must be a multiple of 8)");
+  if (reduction < 0 || reduction > CIS2B_OP_MATMUL_DECODE) return fail(CIS2B_ERR_ARG, "bad reduction");
+  if (reduction == CIS2B_OP_MATMUL_DECODE && (rows > 1024 || !gemm_dec_ok(k)))
+    return fail(CIS2B_ERR_ARG, "decode form: rows <= 1024 and k within shared memory");
   CU(cudaSetDevice(device));
+  if (reduction == CIS2B_OP_MATMUL_DECODE) {
+    Scoped<uint16_t> dw, dt;
+    Scoped<float> dx, dy;
+    CU(cudaMalloc(&dw.p, 2 * (size_t)n_out * k));
+    CU(cudaMalloc(&dt.p, 2 * tile32_elems(n_out, k)));
+    CU(cudaMalloc(&dx.p, 4 * (size_t)rows * k));
+    CU(cudaMalloc(&dy.p, 4 * (size_t)rows * n_out));
+    CU(cudaMemcpy(dw.p, W, 2 * (size_t)n_out * k, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(dx.p, X, 4 * (size_t)rows * k, cudaMemcpyHostToDevice));
+    launch_tile32(dw.p, n_out, k, dt.p, 0);
+    launch_gemm_dec(dx.p, k, dt.p, k, n_out, rows, dy.p, n_out, nullptr, 0, nullptr, 0, 0);
+    CU_LAUNCHED();
+    CU(cudaMemcpy(Y, dy.p, 4 * (size_t)rows * n_out, cudaMemcpyDeviceToHost));
+    return CIS2B_OK;
+  }
   // Same operand layouts as the decoder: W in 8-row panels, X k-major.
   const int ldm = round_up(rows, 4);
   std::vector<float> xt((size_t)k * ldm, 0.0f);

@@ -65,16 +65,20 @@ SHAPES = [(1, 576, 576), (3, 192, 576), (4, 100, 96), (7, 1536, 576), (16, 64, 1
           (64, 576, 1536), (64, 960, 576), (5, 4099, 64), (128, 1024, 3072), (65, 300, 8), (2, 49152, 576)]
 
 
-@pytest.mark.parametrize("tree", [False, True])
+@pytest.mark.parametrize("form", ["sequential", "tree", "decode"])
 @pytest.mark.parametrize("rows,n,k", SHAPES)
-def test_matmul_bit_exact(rows, n, k, tree, pkg, oracle):
+def test_matmul_bit_exact(rows, n, k, form, pkg, oracle):
+    """Both GEMM kernels (the panel kernel of the prompt pass in both orders,
+    the few-row kernel of decode steps in sequential order) against the
+    oracle's dot products, bit for bit."""
+    tree = form == "tree"
     rng = np.random.default_rng(rows * 1000003 + n * 31 + k)
     W = (rng.standard_normal((n, k)).astype(np.float32) * np.float32(0.02)).view(np.uint32)
     W = ((W + 0x7FFF + ((W >> 16) & 1)) >> 16).astype(np.uint16)
     X = rng.standard_normal((rows, k)).astype(np.float32)
     X[:, ::7] = 0.0  # signed zeros and cancellations in the chains
     X[:, 1::11] *= -0.0
-    got = pkg.matmul(W, X, tree=tree)
+    got = pkg.matmul(W, X, tree=tree, decode=form == "decode")
     want = oracle.matmul_bf16(W, X, tree=tree)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
