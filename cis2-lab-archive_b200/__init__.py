@@ -43,7 +43,19 @@ class _Opts(ctypes.Structure):
 
 
 class _Sample(ctypes.Structure):
-    _fields_ = [("seed", ctypes.c_uint64), ("temperature", ctypes.c_float), ("top_p", ctypes.c_float)]
+    _fields_ = [("seed", ctypes.c_uint64), ("temperature", ctypes.c_float), ("top_p", ctypes.c_float),
+                ("scheme", ctypes.c_uint32), ("top_k", ctypes.c_uint32)]
+
+
+SAMPLE_E23, SAMPLE_GUMBEL = 0, 1  # CIS2B_SAMPLE_*
+
+
+def _sample_struct(sample: dict) -> _Sample:
+    """sample: {"seed", "temperature", "top_p"} plus "scheme": "e23" (default)
+    or "gumbel" (the CIS2-SAMPLE-1 clause, which also takes "top_k")."""
+    scheme = SAMPLE_GUMBEL if sample.get("scheme", "e23") == "gumbel" else SAMPLE_E23
+    return _Sample(int(sample["seed"]), float(sample["temperature"]), float(sample["top_p"]), scheme,
+                   int(sample.get("top_k", 0)))
 
 
 class _Info(ctypes.Structure):
@@ -99,6 +111,8 @@ def lib() -> ctypes.CDLL:
     L.cis2b_op_sha256_stream.argtypes = [I32, P, SZ, P, U32, U32, P]
     L.cis2b_op_sample.argtypes = [I32, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
                                   ctypes.c_uint64, ctypes.POINTER(U32)]
+    L.cis2b_op_sample_gumbel.argtypes = [I32, P, I32, ctypes.c_float, U32, ctypes.c_float, ctypes.c_uint64, U32,
+                                         ctypes.POINTER(U32)]
     L.cis2b_op_sample_static.argtypes = [I32, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
                                          ctypes.c_uint64, P, P]
     _lib = L
@@ -159,10 +173,7 @@ class Model:
         steps = np.zeros((n, gen, 32), dtype=np.uint8) if step_digests else None
         wit = np.zeros((n, 32), dtype=np.uint8)
         arg = np.zeros((n, 32), dtype=np.uint8)
-        smp = None
-        if sample:
-            smp = ctypes.byref(_Sample(int(sample["seed"]), float(sample["temperature"]),
-                                       float(sample["top_p"])))
+        smp = ctypes.byref(_sample_struct(sample)) if sample else None
         _check(lib().cis2b_generate(self._h, _ptr(flat), _ptr(lens), n, gen, smp, _ptr(toks), _ptr(steps),
                                     _ptr(wit), _ptr(arg)))
         return {"tokens": toks, "step_digests": steps, "witness": wit, "argmax": arg}
@@ -228,4 +239,14 @@ def sample(logits: np.ndarray, temperature: float, top_p: float, seed: int, posi
     out = ctypes.c_uint32()
     _check(lib().cis2b_op_sample(device, _ptr(logits), logits.size, temperature, top_p, seed, position,
                                  ctypes.byref(out)))
+    return int(out.value)
+
+
+def sample_gumbel(logits: np.ndarray, temperature: float, top_k: int, top_p: float, seed: int, step: int,
+                  device: int = 0) -> int:
+    """One seeded Gumbel-max (CIS2-SAMPLE-1) draw on the device."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    out = ctypes.c_uint32()
+    _check(lib().cis2b_op_sample_gumbel(device, _ptr(logits), logits.size, temperature, top_k, top_p, seed, step,
+                                        ctypes.byref(out)))
     return int(out.value)

@@ -8,10 +8,14 @@
 // (code/cis2-fp/gpu/cis2_host.cpp:222-245; src/main.rs:1231-1262) and, in
 // sampled mode, the E23 line
 //   CIS2_SAMPLE digest=<hex> mode=sampled seed=S temperature=T top_p=P prompt_idx=N ...
-// (code/patches/cis2-fp__cm_e23-pinned-sampling.patch:770-779).
+// (code/patches/cis2-fp__cm_e23-pinned-sampling.patch:770-779).  With
+// --sample SEED,T,K,P (the seeded Gumbel-max clause "CIS2-SAMPLE-1", flag as
+// in labs/w1x-sample/reports/w1x-sample/RESULTS-hq-builder.md:11-12) the
+// lines are the greedy ones, the digest being that of the sampled run.
 //
 //   cis2b_ref --weights-dir D --ids F [--gen-toks N] [--reduction sequential|tree]
 //             [--mode greedy|sampled --seed S --temperature T --top-p P]
+//             [--sample SEED,T,K,P]
 //             [--device I] [--prompt-idx I] [--step-digests]
 // Each non-empty line of F is one prompt (decimal ids); all prompts are
 // decoded as one batch and reported in file order.
@@ -53,8 +57,8 @@ static std::string f32_str(float x) {
 int main(int argc, char **argv) {
   std::string weights_dir = "weights", ids_path;
   int gen = 16, device = 0, prompt_idx = 0;
-  bool tree = false, sampled = false, step_digests = false;
-  cis2b_sample smp{0, 0.8f, 0.95f};
+  bool tree = false, sampled = false, gumbel = false, step_digests = false;
+  cis2b_sample smp{0, 0.8f, 0.95f, CIS2B_SAMPLE_E23, 0};
   for (int i = 1; i < argc; ++i) {
     std::string a = argv[i];
     auto next = [&]() -> const char * {
@@ -75,6 +79,22 @@ int main(int argc, char **argv) {
       std::string v = next();
       if (v == "sampled") sampled = true;
       else if (v != "greedy") { fprintf(stderr, "FATAL: --mode greedy|sampled\n"); return 2; }
+    } else if (a == "--sample") {
+      // SEED,T,K,P: decimal seed, temperature and top_p as strtof reads them, top_k
+      std::string v = next();
+      unsigned long long sd = 0;
+      unsigned k = 0;
+      char tbuf[64], pbuf[64];
+      if (sscanf(v.c_str(), "%llu,%63[^,],%u,%63s", &sd, tbuf, &k, pbuf) != 4) {
+        fprintf(stderr, "FATAL: --sample SEED,T,K,P\n");
+        return 2;
+      }
+      smp.seed = sd;
+      smp.temperature = strtof(tbuf, nullptr);
+      smp.top_k = k;
+      smp.top_p = strtof(pbuf, nullptr);
+      smp.scheme = CIS2B_SAMPLE_GUMBEL;
+      gumbel = true;
     } else if (a == "--seed") smp.seed = strtoull(next(), nullptr, 10);
     else if (a == "--temperature") smp.temperature = strtof(next(), nullptr);
     else if (a == "--top-p") smp.top_p = strtof(next(), nullptr);
@@ -123,7 +143,11 @@ int main(int argc, char **argv) {
   for (auto &p : prompts) { flat.insert(flat.end(), p.begin(), p.end()); lens.push_back((uint32_t)p.size()); }
   std::vector<uint32_t> toks((size_t)n * gen);
   std::vector<uint8_t> steps((size_t)n * gen * 32), wit((size_t)n * 32), arg((size_t)n * 32);
-  if (cis2b_generate(m, flat.data(), lens.data(), n, (uint32_t)gen, sampled ? &smp : nullptr, toks.data(),
+  if (sampled && gumbel) {
+    fprintf(stderr, "FATAL: --mode sampled (E23) and --sample (CIS2-SAMPLE-1) exclude each other\n");
+    return 2;
+  }
+  if (cis2b_generate(m, flat.data(), lens.data(), n, (uint32_t)gen, (sampled || gumbel) ? &smp : nullptr, toks.data(),
                      steps.data(), wit.data(), arg.data()) != CIS2B_OK) {
     fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
     cis2b_free(m);

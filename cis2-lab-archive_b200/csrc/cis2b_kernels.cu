@@ -1194,6 +1194,59 @@ __device__ void serial_fold(int n, Load load, Op op, float *buf, int *stop_flag)
   }
 }
 
+// Stable LSD radix sort of (key, value) pairs by key ascending, 4 passes of
+// 8 bits, by the whole block; the result ends in (kA, vA).  Values that come
+// in index order therefore keep index order among equal keys.
+__device__ void block_radix_sort(uint32_t *kA, uint32_t *vA, uint32_t *kB, uint32_t *vB, int V, int *hist,
+                                 int *base, int (*wcnt)[256]) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  uint32_t *ki = kA, *vi = vA, *ko = kB, *vo = vB;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int sh = 8 * pass;
+    for (int d = tid; d < 256; d += nt) hist[d] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += nt) atomicAdd(&hist[(ki[i] >> sh) & 255], 1);
+    __syncthreads();
+    if (tid == 0) {
+      int run = 0;
+      for (int d = 0; d < 256; ++d) { base[d] = run; run += hist[d]; }
+    }
+    __syncthreads();
+    for (int t0 = 0; t0 < V; t0 += nt) {
+      for (int d = tid; d < (nt / 32) * 256; d += nt) (&wcnt[0][0])[d] = 0;
+      __syncthreads();
+      const int i = t0 + tid;
+      const bool valid = i < V;
+      uint32_t key = valid ? ki[i] : 0u, val = valid ? vi[i] : 0u;
+      int dg = valid ? (int)((key >> sh) & 255) : 256;
+      unsigned same = __match_any_sync(FULL, dg);
+      int rank = __popc(same & lt_mask);
+      if (valid && rank == 0) wcnt[warp][dg] = __popc(same);
+      __syncthreads();
+      // exclusive prefix over warps, per digit; then tile totals into base
+      if (tid < 256) {
+        int run = 0;
+        for (int w = 0; w < nt / 32; ++w) { int c = wcnt[w][tid]; wcnt[w][tid] = run; run += c; }
+        hist[tid] = run;  // tile total for digit tid
+      }
+      __syncthreads();
+      if (valid) {
+        int dst = base[dg] + wcnt[warp][dg] + rank;
+        ko[dst] = key;
+        vo[dst] = val;
+      }
+      __syncthreads();
+      if (tid < 256) base[tid] += hist[tid];
+      __syncthreads();
+    }
+    uint32_t *t;
+    t = ki; ki = ko; ko = t;
+    t = vi; vi = vo; vo = t;
+  }
+}
+
 __global__ void __launch_bounds__(SAMPLE_THREADS)
 k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, float temperature,
          float top_p, uint64_t seed, const int32_t *position, float *scratch, uint32_t *next) {
@@ -1245,52 +1298,9 @@ k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, fl
     vA[i] = (uint32_t)i;
   }
   __syncthreads();
-  // Step 3: stable LSD radix sort, 4 passes of 8 bits.
-  const int warp = tid >> 5, lane = tid & 31;
-  const unsigned lt_mask = (1u << lane) - 1u;
-  uint32_t *ki = kA, *vi = vA, *ko = kB, *vo = vB;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int sh = 8 * pass;
-    for (int d = tid; d < 256; d += nt) hist[d] = 0;
-    __syncthreads();
-    for (int i = tid; i < V; i += nt) atomicAdd(&hist[(ki[i] >> sh) & 255], 1);
-    __syncthreads();
-    if (tid == 0) {
-      int run = 0;
-      for (int d = 0; d < 256; ++d) { base[d] = run; run += hist[d]; }
-    }
-    __syncthreads();
-    for (int t0 = 0; t0 < V; t0 += nt) {
-      for (int d = tid; d < (nt / 32) * 256; d += nt) (&wcnt[0][0])[d] = 0;
-      __syncthreads();
-      const int i = t0 + tid;
-      const bool valid = i < V;
-      uint32_t key = valid ? ki[i] : 0u, val = valid ? vi[i] : 0u;
-      int dg = valid ? (int)((key >> sh) & 255) : 256;
-      unsigned same = __match_any_sync(FULL, dg);
-      int rank = __popc(same & lt_mask);
-      if (valid && rank == 0) wcnt[warp][dg] = __popc(same);
-      __syncthreads();
-      // exclusive prefix over warps, per digit; then tile totals into base
-      if (tid < 256) {
-        int run = 0;
-        for (int w = 0; w < nt / 32; ++w) { int c = wcnt[w][tid]; wcnt[w][tid] = run; run += c; }
-        hist[tid] = run;  // tile total for digit tid
-      }
-      __syncthreads();
-      if (valid) {
-        int dst = base[dg] + wcnt[warp][dg] + rank;
-        ko[dst] = key;
-        vo[dst] = val;
-      }
-      __syncthreads();
-      if (tid < 256) base[tid] += hist[tid];
-      __syncthreads();
-    }
-    uint32_t *t;
-    t = ki; ki = ko; ko = t;
-    t = vi; vi = vo; vo = t;
-  }
+  // Step 3: stable LSD radix sort on ~bits(p): probability descending, index ascending.
+  block_radix_sort(kA, vA, kB, vB, V, hist, base, wcnt);
+  uint32_t *ki = kA, *vi = vA;
   // After 4 passes the sorted keys/indices are back in (kA, vA).
   // Step 4: nucleus = shortest prefix with cumulative sum >= top_p.
   float cum = 0.0f;
@@ -1334,6 +1344,133 @@ void launch_sample(const float *logits, int V, int rows, const int32_t *slot, si
   if (rows <= 0) return;
   k_sample<<<rows, SAMPLE_THREADS, 0, s>>>(logits, V, slot, slot_stride, temperature, top_p, seed,
                                            position, scratch, next);
+}
+
+// ------------------------------------------------------------ seeded Gumbel-max sampler
+//
+// The "CIS2-SAMPLE-1" clause (code/patches/cis2-spec__seeded-sampling.patch
+// :81-145), one block per row:
+//   s_i = l_i / T;  rank order = s descending, index ascending (stable radix
+//   sort of an order-preserving key, -0 keyed as +0 since the clause compares
+//   values);  top-k keeps ranks < k;  top-p walks the kept ranks with the
+//   exp_pinned weights, their sequential denominator and running sum, keeping
+//   rank r while r == 0 or c_{r-1} < top_p;  z_i = s_i + g_i for kept i,
+//   g_i = -ln(-ln(u_i)) from MurmurHash3_x86_32(seed || step || i, 0x43495332);
+//   next = the first index of the maximum z.
+// MurmurHash3_x86_32 (Austin Appleby, public domain) is restated from the
+// published algorithm for the clause's fixed 16-byte key.
+
+__device__ __forceinline__ uint32_t mm3_rotl(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+__device__ __forceinline__ uint32_t mm3_block(uint32_t h, uint32_t k) {
+  k *= 0xcc9e2d51u;
+  k = mm3_rotl(k, 15);
+  k *= 0x1b873593u;
+  h ^= k;
+  h = mm3_rotl(h, 13);
+  return h * 5u + 0xe6546b64u;
+}
+__device__ __forceinline__ float gumbel_noise(uint64_t seed, uint32_t step, uint32_t index) {
+  uint32_t h = 0x43495332u;  // hash seed "CIS2"
+  h = mm3_block(h, (uint32_t)seed);
+  h = mm3_block(h, (uint32_t)(seed >> 32));
+  h = mm3_block(h, step);
+  h = mm3_block(h, index);
+  h ^= 16u;  // key length
+  h ^= h >> 16;
+  h *= 0x85ebca6bu;
+  h ^= h >> 13;
+  h *= 0xc2b2ae35u;
+  h ^= h >> 16;
+  const float u = fmul(__uint2float_rn((h >> 9) * 2u + 1u), bitsf(0x33800000u));  // exact: m < 2^24, times 2^-24
+  return fsub(0.0f, ln_pinned(fsub(0.0f, ln_pinned(u))));
+}
+
+__global__ void __launch_bounds__(SAMPLE_THREADS)
+k_sample_gumbel(const float *logits, int V, const int32_t *slot, size_t slot_stride, float temperature,
+                uint32_t top_k, float top_p, uint64_t seed, const int32_t *step, float *scratch, uint32_t *next) {
+  __shared__ float buf[2 * FOLD_CHUNK];
+  __shared__ int hist[256];
+  __shared__ int base[256];
+  __shared__ int wcnt[SAMPLE_THREADS / 32][256];
+  __shared__ float bz[SAMPLE_THREADS / 32];
+  __shared__ int bi[SAMPLE_THREADS / 32];
+  __shared__ float shared_f[4];
+  __shared__ int shared_i[4];
+  const int r = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const float *row = logits + (slot ? (size_t)(*slot) * slot_stride : 0) + (size_t)r * V;
+  float *sv = scratch + (size_t)r * 5 * V;  // s_i by index
+  uint32_t *kA = reinterpret_cast<uint32_t *>(sv + V), *vA = kA + V;
+  uint32_t *kB = vA + V, *vB = kB + V;
+  for (int i = tid; i < V; i += nt) {
+    const float x = fdiv(row[i], temperature);
+    sv[i] = x;
+    uint32_t u = __float_as_uint(x);
+    if (u == 0x80000000u) u = 0u;                       // -0 ranks as +0
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // ascending with the value
+    kA[i] = ~ord;                                        // descending
+    vA[i] = (uint32_t)i;
+  }
+  __syncthreads();
+  block_radix_sort(kA, vA, kB, vB, V, hist, base, wcnt);
+  const uint32_t *order = vA;
+  const int K = (top_k > 0 && top_k < (uint32_t)V) ? (int)top_k : V;
+  int P = K;
+  if (top_p < 1.0f) {
+    const float m0 = sv[order[0]];
+    float *e = reinterpret_cast<float *>(kB);  // e_r by rank
+    for (int q = tid; q < K; q += nt) e[q] = exp_pinned(fsub(sv[order[q]], m0));
+    __syncthreads();
+    float den = 0.0f;
+    serial_fold(K, [&](int q) { return e[q]; }, [&](int, float v) { den = fadd(den, v); return false; }, buf,
+                &shared_i[0]);
+    if (tid == 0) shared_f[0] = den;
+    __syncthreads();
+    den = shared_f[0];
+    float c = 0.0f;
+    int cut = K;
+    serial_fold(K, [&](int q) { return fdiv(e[q], den); },
+                [&](int q, float pq) {
+                  if (q > 0 && !(c < top_p)) { cut = q; return true; }
+                  c = fadd(c, pq);
+                  return false;
+                },
+                buf, &shared_i[0]);
+    if (tid == 0) shared_i[1] = cut;
+    __syncthreads();
+    P = shared_i[1];
+  }
+  const uint32_t st = (uint32_t)*step;
+  float best_z = 0.0f;
+  int best_i = -1;
+  for (int q = tid; q < P; q += nt) {
+    const int i = (int)order[q];
+    const float z = fadd(sv[i], gumbel_noise(seed, st, (uint32_t)i));
+    if (best_i < 0 || z > best_z || (z == best_z && i < best_i)) { best_z = z; best_i = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float oz = __shfl_xor_sync(FULL, best_z, o);
+    const int oi = __shfl_xor_sync(FULL, best_i, o);
+    if (oi >= 0 && (best_i < 0 || oz > best_z || (oz == best_z && oi < best_i))) { best_z = oz; best_i = oi; }
+  }
+  if ((tid & 31) == 0) { bz[tid >> 5] = best_z; bi[tid >> 5] = best_i; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < nt / 32; ++w)
+      if (bi[w] >= 0 && (best_i < 0 || bz[w] > best_z || (bz[w] == best_z && bi[w] < best_i))) {
+        best_z = bz[w];
+        best_i = bi[w];
+      }
+    next[r] = (uint32_t)best_i;
+  }
+}
+
+void launch_sample_gumbel(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
+                          float temperature, uint32_t top_k, float top_p, uint64_t seed, const int32_t *step,
+                          float *scratch, uint32_t *next, cudaStream_t s) {
+  if (rows <= 0) return;
+  k_sample_gumbel<<<rows, SAMPLE_THREADS, 0, s>>>(logits, V, slot, slot_stride, temperature, top_k, top_p, seed,
+                                                  step, scratch, next);
 }
 
 // ------------------------------------------------------------ sampler without allocation

@@ -82,6 +82,10 @@ void launch_argmax(const float *logits, int V, int rows, const int32_t *slot, si
 void launch_sample(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
                    float temperature, float top_p, uint64_t seed, const int32_t *position,
                    float *scratch, uint32_t *next, cudaStream_t s);
+// Seeded Gumbel-max sampler ("CIS2-SAMPLE-1"); step = 0-based generation step (device).
+void launch_sample_gumbel(const float *logits, int V, int rows, const int32_t *slot, size_t slot_stride,
+                          float temperature, uint32_t top_k, float top_p, uint64_t seed, const int32_t *step,
+                          float *scratch, uint32_t *next, cudaStream_t s);
 // Record the chosen ids (tokens_out[r][step], ids_hist[step][r]), advance positions, ring slot, step.
 void launch_step_advance(const uint32_t *next, int rows, const int32_t *step, int gen,
                          uint32_t *tokens_out, uint32_t *ids_hist, int32_t *pos, int32_t *sample_pos,

@@ -651,7 +651,12 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   if (!m) return fail(CIS2B_ERR_ARG, "model is NULL");
   if (n_seq == 0) return CIS2B_OK;
   if (!prompt_ids || !prompt_lens || !out_witness) return fail(CIS2B_ERR_ARG, "NULL input/output buffer");
-  if (sample && !(sample->temperature > 0.0f)) return fail(CIS2B_ERR_ARG, "temperature must be > 0");
+  if (sample && !(sample->temperature > 0.0f && sample->temperature <= 3.402823466e38f))
+    return fail(CIS2B_ERR_ARG, "temperature must be finite and > 0");
+  if (sample && sample->scheme != CIS2B_SAMPLE_E23 && sample->scheme != CIS2B_SAMPLE_GUMBEL)
+    return fail(CIS2B_ERR_ARG, "unknown sampling scheme");
+  if (sample && sample->scheme == CIS2B_SAMPLE_E23 && sample->top_k != 0)
+    return fail(CIS2B_ERR_ARG, "top_k applies to the Gumbel-max scheme only");
   if (sample && !(sample->top_p > 0.0f && sample->top_p <= 1.0f)) return fail(CIS2B_ERR_ARG, "top_p must be in (0, 1]");
   CU(cudaSetDevice(m->dev));
   const int B = (int)n_seq, G = (int)gen;
@@ -722,7 +727,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   std::vector<uint32_t> hoff(B + 1);
   for (int b = 0; b < B; ++b) {
     hoff[b] = (uint32_t)hb.size();
-    if (sample) {
+    if (sample && sample->scheme == CIS2B_SAMPLE_E23) {
       const char tag[] = "CIS2_SAMPLE_V1";
       hb.insert(hb.end(), tag, tag + 14);
       for (int i = 0; i < 8; ++i) hb.push_back((uint8_t)(sample->seed >> (8 * i)));
@@ -740,6 +745,18 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
     for (uint32_t p = 0; p < prompt_lens[b]; ++p) {
       uint32_t v = prompt_ids[poff[b] + p];
       for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(v >> (8 * i)));
+    }
+    if (sample && sample->scheme == CIS2B_SAMPLE_GUMBEL) {
+      // seeded-sampling patch :128-134: tag, seed, T bits, top_k, top_p bits, after the prompt ids
+      const char tag[] = "CIS2-SAMPLE-1";
+      hb.insert(hb.end(), tag, tag + 13);
+      for (int i = 0; i < 8; ++i) hb.push_back((uint8_t)(sample->seed >> (8 * i)));
+      uint32_t tb, pb;
+      memcpy(&tb, &sample->temperature, 4);
+      memcpy(&pb, &sample->top_p, 4);
+      for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(tb >> (8 * i)));
+      for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(sample->top_k >> (8 * i)));
+      for (int i = 0; i < 4; ++i) hb.push_back((uint8_t)(pb >> (8 * i)));
     }
   }
   hoff[B] = (uint32_t)hb.size();
@@ -785,7 +802,10 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   // Token selection for the step whose logits sit in ring slot *d_slot,
   // then the bookkeeping that points the next forward at its position.
   auto select = [&]() {
-    if (sample)
+    if (sample && sample->scheme == CIS2B_SAMPLE_GUMBEL)
+      launch_sample_gumbel(ring_base, m->V, B, d_slot, (size_t)B * V, sample->temperature, sample->top_k,
+                           sample->top_p, sample->seed, d_step, m->scratch.as<float>(), d_next, s);
+    else if (sample)
       launch_sample(ring_base, m->V, B, d_slot, (size_t)B * V, sample->temperature, sample->top_p,
                     sample->seed, m->d_spos.as<int32_t>(), m->scratch.as<float>(), d_next, s);
     else
@@ -1126,6 +1146,27 @@ int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temper
   CU(cudaMemcpy(dl.p, logits, 4 * (size_t)n, cudaMemcpyHostToDevice));
   CU(cudaMemcpy(dp.p, &pos32, 4, cudaMemcpyHostToDevice));
   launch_sample(dl.p, n, 1, nullptr, 0, temperature, top_p, seed, dp.p, scr.p, nx.p, 0);
+  CU_LAUNCHED();
+  CU(cudaMemcpy(out_index, nx.p, 4, cudaMemcpyDeviceToHost));
+  return CIS2B_OK;
+}
+
+int cis2b_op_sample_gumbel(int32_t device, const float *logits, int32_t n, float temperature, uint32_t top_k,
+                           float top_p, uint64_t seed, uint32_t step, uint32_t *out_index) {
+  if (!logits || !out_index || n <= 0) return fail(CIS2B_ERR_ARG, "bad argument");
+  if (!(temperature > 0.0f && temperature <= 3.402823466e38f) || !(top_p > 0.0f && top_p <= 1.0f))
+    return fail(CIS2B_ERR_ARG, "bad sampler parameters");
+  CU(cudaSetDevice(device));
+  Scoped<float> dl, scr;
+  Scoped<uint32_t> nx;
+  Scoped<int32_t> dst;
+  CU(cudaMalloc(&dl.p, 4 * (size_t)n));
+  CU(cudaMalloc(&scr.p, 4 * 5 * (size_t)n));
+  CU(cudaMalloc(&nx.p, 4));
+  CU(cudaMalloc(&dst.p, 4));
+  CU(cudaMemcpy(dl.p, logits, 4 * (size_t)n, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(dst.p, &step, 4, cudaMemcpyHostToDevice));
+  launch_sample_gumbel(dl.p, n, 1, nullptr, 0, temperature, top_k, top_p, seed, dst.p, scr.p, nx.p, 0);
   CU_LAUNCHED();
   CU(cudaMemcpy(out_index, nx.p, 4, cudaMemcpyDeviceToHost));
   return CIS2B_OK;

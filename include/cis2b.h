@@ -53,11 +53,21 @@ typedef struct {
   int32_t reserved[5];   /* must be zero */
 } cis2b_opts;
 
-/* E23 pinned sampler parameters (sampled mode).  Pass NULL for greedy. */
+/* Sampled-mode parameters.  Pass NULL for greedy.
+ * scheme CIS2B_SAMPLE_E23 (0): the E23 pinned sampler (SplitMix64 word,
+ *   nucleus over the sorted softmax, CDF walk), witness prefix
+ *   "CIS2_SAMPLE_V1" before the header; top_k must be 0.
+ * scheme CIS2B_SAMPLE_GUMBEL (1): the seeded Gumbel-max clause
+ *   "CIS2-SAMPLE-1" (MurmurHash3 noise, top-k then top-p on rank order),
+ *   its header absorbed after the prompt ids. */
+#define CIS2B_SAMPLE_E23 0
+#define CIS2B_SAMPLE_GUMBEL 1
 typedef struct {
   uint64_t seed;
-  float temperature; /* > 0 */
-  float top_p;       /* (0, 1] */
+  float temperature; /* > 0, finite */
+  float top_p;       /* (0, 1]; 1 = disabled */
+  uint32_t scheme;   /* CIS2B_SAMPLE_* */
+  uint32_t top_k;    /* CIS2B_SAMPLE_GUMBEL only; 0 (or >= vocab) = disabled */
 } cis2b_sample;
 
 typedef struct {
@@ -158,6 +168,10 @@ int cis2b_op_sha256_stream(int32_t device, const uint8_t *prefix, size_t prefix_
 /* E23 sampler on one logits row. */
 int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temperature, float top_p,
                     uint64_t seed, uint64_t position, uint32_t *out_index);
+/* Seeded Gumbel-max ("CIS2-SAMPLE-1") draw on one logits row; step is the
+ * 0-based generation step. */
+int cis2b_op_sample_gumbel(int32_t device, const float *logits, int32_t n, float temperature, uint32_t top_k,
+                           float top_p, uint64_t seed, uint32_t step, uint32_t *out_index);
 
 /* No counterpart in the reference.  The E23 sampler on one logits row that
  * ALLOCATES NOTHING: for callers that cannot call cudaMalloc -- code whose

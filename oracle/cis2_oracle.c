@@ -414,6 +414,119 @@ static uint32_t sample_e23(const float *logits, int n, float temperature, float 
   return order[nuc - 1].i;
 }
 
+/* -------------------------------------------- seeded Gumbel-max sampler
+ * The "CIS2-SAMPLE-1" clause (code/patches/cis2-spec__seeded-sampling.patch
+ * :81-145).  Its one new primitive is MurmurHash3_x86_32 (Austin Appleby,
+ * public domain), restated here from the published algorithm; the clause
+ * pins it with the hash seed 0x43495332 over a 16-byte key. */
+
+static uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+uint32_t cis2o_murmur3_32(const uint8_t *key, size_t len, uint32_t seed) {
+  const uint32_t c1 = 0xcc9e2d51u, c2 = 0x1b873593u;
+  uint32_t h = seed;
+  const size_t nb = len / 4;
+  for (size_t b = 0; b < nb; ++b) {
+    uint32_t k = (uint32_t)key[4 * b] | (uint32_t)key[4 * b + 1] << 8 | (uint32_t)key[4 * b + 2] << 16 |
+                 (uint32_t)key[4 * b + 3] << 24;
+    k *= c1;
+    k = rotl32(k, 15);
+    k *= c2;
+    h ^= k;
+    h = rotl32(h, 13);
+    h = h * 5u + 0xe6546b64u;
+  }
+  const uint8_t *tail = key + 4 * nb;
+  uint32_t k = 0;
+  switch (len & 3) {
+    case 3: k ^= (uint32_t)tail[2] << 16; /* fall through */
+    case 2: k ^= (uint32_t)tail[1] << 8;  /* fall through */
+    case 1:
+      k ^= tail[0];
+      k *= c1;
+      k = rotl32(k, 15);
+      k *= c2;
+      h ^= k;
+  }
+  h ^= (uint32_t)len;
+  h ^= h >> 16;
+  h *= 0x85ebca6bu;
+  h ^= h >> 13;
+  h *= 0xc2b2ae35u;
+  h ^= h >> 16;
+  return h;
+}
+
+/* 14.2: key = seed (u64 LE) || step (u32 LE) || index (u32 LE);
+ * u = f32((h >> 9) * 2 + 1) * 2^-24 (exact); g = 0 - ln(0 - ln(u)). */
+static float gumbel_noise(uint64_t seed, uint32_t step, uint32_t index, uint32_t *h_out, float *u_out) {
+  uint8_t key[16];
+  for (int i = 0; i < 8; ++i) key[i] = (uint8_t)(seed >> (8 * i));
+  for (int i = 0; i < 4; ++i) key[8 + i] = (uint8_t)(step >> (8 * i));
+  for (int i = 0; i < 4; ++i) key[12 + i] = (uint8_t)(index >> (8 * i));
+  const uint32_t h = cis2o_murmur3_32(key, 16, 0x43495332u);
+  const uint32_t m = (h >> 9) * 2u + 1u;
+  const float u = (float)m * 0x1p-24f;
+  if (h_out) *h_out = h;
+  if (u_out) *u_out = u;
+  return 0.0f - p_ln(0.0f - p_ln(u));
+}
+
+void cis2o_gumbel_noise(uint64_t seed, uint32_t step, uint32_t index, uint32_t *hash, float *u, float *g) {
+  fpenv_guard fg = fp_enter();
+  *g = gumbel_noise(seed, step, index, hash, u);
+  fp_leave(fg);
+}
+
+typedef struct { float s; uint32_t i; } si_t;
+static int cmp_rank(const void *a, const void *b) { /* 14.3 step 2: s descending, index ascending */
+  const si_t *x = (const si_t *)a, *y = (const si_t *)b;
+  if (x->s > y->s) return -1;
+  if (y->s > x->s) return 1;
+  return (x->i < y->i) ? -1 : (x->i > y->i);
+}
+
+/* 14.3-14.4.  z_out (optional, [n]) receives z (-inf where masked). */
+static uint32_t sample_gumbel(const float *logits, int n, float temperature, uint32_t top_k, float top_p,
+                              uint64_t seed, uint32_t step, si_t *order, float *z_out) {
+  for (int i = 0; i < n; ++i) { order[i].s = logits[i] / temperature; order[i].i = (uint32_t)i; }
+  qsort(order, (size_t)n, sizeof(si_t), cmp_rank);
+  const int K = (top_k > 0 && top_k < (uint32_t)n) ? (int)top_k : n;
+  int P = K;
+  if (top_p < 1.0f) {
+    const float m = order[0].s;
+    float den = 0.0f;
+    for (int r = 0; r < K; ++r) den = den + p_exp(order[r].s - m);
+    float c = 0.0f;
+    for (int r = 0; r < K; ++r) {
+      if (r > 0 && !(c < top_p)) { P = r; break; }
+      c = c + p_exp(order[r].s - m) / den;
+    }
+  }
+  if (z_out)
+    for (int i = 0; i < n; ++i) z_out[i] = ffrom(0xff800000u);
+  uint32_t best_i = 0;
+  float best_z = ffrom(0xff800000u);
+  int have = 0;
+  for (int r = 0; r < P; ++r) {
+    const uint32_t i = order[r].i;
+    const float z = order[r].s + gumbel_noise(seed, step, i, NULL, NULL);
+    if (z_out) z_out[i] = z;
+    if (!have || z > best_z || (z == best_z && i < best_i)) { best_z = z; best_i = i; have = 1; }
+  }
+  return best_i;
+}
+
+uint32_t cis2o_sample_gumbel(const float *logits, int32_t n, float temperature, uint32_t top_k, float top_p,
+                             uint64_t seed, uint32_t step, float *z_out) {
+  fpenv_guard fg = fp_enter();
+  si_t *order = (si_t *)malloc(sizeof(si_t) * (size_t)n);
+  const uint32_t r = sample_gumbel(logits, n, temperature, top_k, top_p, seed, step, order, z_out);
+  free(order);
+  fp_leave(fg);
+  return r;
+}
+
 /* ------------------------------------------------------------ model */
 
 typedef struct {
@@ -682,9 +795,11 @@ int cis2o_generate(const void *mp, const uint32_t *prompt_ids, const uint32_t *p
   for (uint32_t s = 0; s < n_seq; ++s) if (prompt_lens[s] > max_prompt) max_prompt = prompt_lens[s];
   ws_t w;
   if (ws_alloc(&w, m, (int)(max_prompt + gen)) != 0) { fp_leave(g); return -1; }
-  int sampled = sample && sample->enabled;
+  const int scheme = sample ? sample->enabled : 0;  /* 0 greedy, 1 E23, 2 CIS2-SAMPLE-1 */
+  const int sampled = scheme == 1;
   float *scratch = sampled ? (float *)malloc(sizeof(float) * (size_t)c->vocab) : NULL;
   pi_t *order = sampled ? (pi_t *)malloc(sizeof(pi_t) * (size_t)c->vocab) : NULL;
+  si_t *gorder = scheme == 2 ? (si_t *)malloc(sizeof(si_t) * (size_t)c->vocab) : NULL;
   FILE *tr = trace_path ? fopen(trace_path, "w") : NULL;
   size_t off = 0;
   for (uint32_t s = 0; s < n_seq; ++s) {
@@ -707,13 +822,24 @@ int cis2o_generate(const void *mp, const uint32_t *prompt_ids, const uint32_t *p
     sha_update(&wit, m->table_digest, 32);
     sha_update(&wit, m->inv_freq_digest, 32);
     for (uint32_t i = 0; i < np; ++i) { sha_u32le(&wit, ids[i]); sha_u32le(&ah, ids[i]); }
+    if (scheme == 2) { /* seeded-sampling patch :128-134: after the prompt ids */
+      sha_update(&wit, "CIS2-SAMPLE-1", 13);
+      uint8_t le[8];
+      for (int i = 0; i < 8; ++i) le[i] = (uint8_t)(sample->seed >> (8 * i));
+      sha_update(&wit, le, 8);
+      sha_u32le(&wit, fbits(sample->temperature));
+      sha_u32le(&wit, sample->top_k);
+      sha_u32le(&wit, fbits(sample->top_p));
+    }
     for (uint32_t p = 0; p < np; ++p)
       forward_token(m, &w, (int)p, ids[p], p + 1 == np, trs);
     for (uint32_t t = 0; t < gen; ++t) {
       uint32_t next = sampled
           ? sample_e23(w.logits, c->vocab, sample->temperature, sample->top_p, sample->seed,
                        (uint64_t)np + t, scratch, order)
-          : argmax_first(w.logits, c->vocab);
+          : scheme == 2 ? sample_gumbel(w.logits, c->vocab, sample->temperature, sample->top_k, sample->top_p,
+                                        sample->seed, t, gorder, NULL)
+                        : argmax_first(w.logits, c->vocab);
       for (int i = 0; i < c->vocab; ++i) sha_u32le(&wit, fbits(w.logits[i]));
       sha_u32le(&wit, next);
       sha_u32le(&ah, next);
@@ -727,6 +853,7 @@ int cis2o_generate(const void *mp, const uint32_t *prompt_ids, const uint32_t *p
   if (tr) fclose(tr);
   free(scratch);
   free(order);
+  free(gorder);
   ws_free(&w);
   fp_leave(g);
   return 0;

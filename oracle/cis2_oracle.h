@@ -37,10 +37,11 @@ typedef struct {
 } cis2o_config;
 
 typedef struct {
-  int32_t enabled;    /* 0: greedy argmax; 1: E23 pinned sampler */
+  int32_t enabled;    /* 0: greedy argmax; 1: E23 pinned sampler; 2: seeded Gumbel-max "CIS2-SAMPLE-1" */
   uint64_t seed;
   float temperature;
   float top_p;
+  uint32_t top_k;     /* scheme 2 only; 0 = disabled */
 } cis2o_sample;
 
 /* tensors: embed, final_norm, lm_head (NULL if tied), then n_layers *
@@ -91,6 +92,12 @@ uint32_t cis2o_argmax(const float *v, int32_t n);
 uint32_t cis2o_sample_pinned(const float *logits, int32_t n, float temperature, float top_p,
                              uint64_t seed, uint64_t position);
 uint64_t cis2o_rng_word(uint64_t seed, uint64_t position);
+/* Seeded Gumbel-max sampling ("CIS2-SAMPLE-1"): MurmurHash3_x86_32 over a
+ * byte key, the noise of one (seed, step, index), and one draw. */
+uint32_t cis2o_murmur3_32(const uint8_t *key, size_t len, uint32_t seed);
+void cis2o_gumbel_noise(uint64_t seed, uint32_t step, uint32_t index, uint32_t *hash, float *u, float *g);
+uint32_t cis2o_sample_gumbel(const float *logits, int32_t n, float temperature, uint32_t top_k, float top_p,
+                             uint64_t seed, uint32_t step, float *z_out);
 void cis2o_sha256(const uint8_t *data, size_t n, uint8_t out[32]);
 /* Evaluate one pinned function over an array (f: 0 exp,1 sin,2 cos,3 ln,4 silu,5 rsqrt). */
 void cis2o_map(int32_t f, const float *x, float *y, size_t n);

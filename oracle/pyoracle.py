@@ -42,7 +42,17 @@ class _Cfg(ctypes.Structure):
 
 class _Sample(ctypes.Structure):
     _fields_ = [("enabled", ctypes.c_int32), ("seed", ctypes.c_uint64),
-                ("temperature", ctypes.c_float), ("top_p", ctypes.c_float)]
+                ("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("top_k", ctypes.c_uint32)]
+
+
+def sample_struct(sample: dict | None) -> _Sample:
+    """sample: None (greedy) or {"seed", "temperature", "top_p"} plus
+    "scheme": "e23" (default) or "gumbel" (the CIS2-SAMPLE-1 clause, with "top_k")."""
+    if not sample:
+        return _Sample(0, 0, 0.8, 0.95, 0)
+    scheme = 2 if sample.get("scheme", "e23") == "gumbel" else 1
+    return _Sample(scheme, int(sample["seed"]), float(sample["temperature"]), float(sample["top_p"]),
+                   int(sample.get("top_k", 0)))
 
 
 _lib = None
@@ -77,6 +87,12 @@ def lib() -> ctypes.CDLL:
         L.cis2o_softmax.argtypes = [P, ctypes.c_int32, ctypes.c_int32]
         L.cis2o_argmax.restype = ctypes.c_uint32
         L.cis2o_argmax.argtypes = [P, ctypes.c_int32]
+        L.cis2o_murmur3_32.restype = ctypes.c_uint32
+        L.cis2o_murmur3_32.argtypes = [P, ctypes.c_size_t, ctypes.c_uint32]
+        L.cis2o_gumbel_noise.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, P, P, P]
+        L.cis2o_sample_gumbel.restype = ctypes.c_uint32
+        L.cis2o_sample_gumbel.argtypes = [P, ctypes.c_int32, ctypes.c_float, ctypes.c_uint32, ctypes.c_float,
+                                          ctypes.c_uint64, ctypes.c_uint32, P]
         L.cis2o_sample_pinned.restype = ctypes.c_uint32
         L.cis2o_sample_pinned.argtypes = [P, ctypes.c_int32, ctypes.c_float, ctypes.c_float,
                                           ctypes.c_uint64, ctypes.c_uint64]
@@ -178,9 +194,7 @@ class PortOracle:
         steps = np.zeros((n, gen, 32), dtype=np.uint8) if step_digests else None
         wit = np.zeros((n, 32), dtype=np.uint8)
         arg = np.zeros((n, 32), dtype=np.uint8)
-        s = _Sample(0, 0, 0.8, 0.95)
-        if sample:
-            s = _Sample(1, int(sample["seed"]), float(sample["temperature"]), float(sample["top_p"]))
+        s = sample_struct(sample)
         hdr = np.frombuffer(self.hashes, dtype=np.uint8).copy()
         rc = lib().cis2o_generate(self.h, _ptr(flat), _ptr(lens), n, gen, ctypes.byref(s), _ptr(hdr),
                                   _ptr(toks), None if steps is None else _ptr(steps), _ptr(wit),
@@ -274,3 +288,22 @@ def run_refdrv(weights_dir: str, prompts, gen: int, tree: bool = False, sample: 
                         out.append(d)
         out.sort(key=lambda d: d["seq"])
         return out
+
+
+def gumbel_noise(seed: int, step: int, index: int) -> tuple[int, int, int]:
+    """(hash, u bits, g bits) of one (seed, step, index) of the CIS2-SAMPLE-1 noise."""
+    h = ctypes.c_uint32()
+    u = ctypes.c_float()
+    g = ctypes.c_float()
+    lib().cis2o_gumbel_noise(seed, step, index, ctypes.byref(h), ctypes.byref(u), ctypes.byref(g))
+    ub = np.array([u.value], dtype=np.float32).view(np.uint32)[0]
+    gb = np.array([g.value], dtype=np.float32).view(np.uint32)[0]
+    return int(h.value), int(ub), int(gb)
+
+
+def sample_gumbel(logits, temperature: float, top_k: int, top_p: float, seed: int, step: int):
+    """(next_id, z[V]) of one CIS2-SAMPLE-1 draw."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    z = np.zeros_like(x)
+    r = lib().cis2o_sample_gumbel(_ptr(x), x.size, temperature, top_k, top_p, seed, step, _ptr(z))
+    return int(r), z

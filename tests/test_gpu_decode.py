@@ -72,6 +72,26 @@ def test_ragged_batch_matches_oracle(model, reduction, sampled, pkg, oracle, syn
         assert np.array_equal(r[k], o[k]), k
 
 
+@pytest.mark.parametrize("model,top_k,top_p", [("tiny", 40, 0.95), ("tiny_qwen3", 0, 0.9), ("mid", 1, 1.0),
+                                               ("tiny_bias", 0, 1.0)])
+def test_gumbel_sampled_decode_matches_oracle(model, top_k, top_p, pkg, oracle, synth, synth_root):
+    """Sampled decode under the seeded Gumbel-max clause (CIS2-SAMPLE-1):
+    tokens, per-step digests (with the clause's header after the prompt ids)
+    and final digests equal the oracle's."""
+    d = synth.ensure_model(model, synth_root)
+    lens = [1, 9, 33, 4]
+    prompts = [synth.random_prompts(model, 1, L, 404, first=i)[0] for i, L in enumerate(lens)]
+    sample = {"scheme": "gumbel", "seed": 0xC0FFEE, "temperature": 0.8, "top_k": top_k, "top_p": top_p}
+    m = model_for(pkg, synth, synth_root, model, "sequential")
+    r = m.generate(prompts, 12, sample=sample)
+    o = oracle.PortOracle(d).generate(prompts, 12, sample=sample)
+    for k in ("tokens", "step_digests", "witness", "argmax"):
+        assert np.array_equal(r[k], o[k]), k
+    # the two schemes differ (different noise and header), as they should
+    e23 = m.generate(prompts[:1], 12, sample={"seed": 0xC0FFEE, "temperature": 0.8, "top_p": top_p})
+    assert e23["witness"][0].tobytes() != r["witness"][0].tobytes()
+
+
 def test_batch_rows_equal_solo_runs(pkg, synth, synth_root):
     """Batch invariance (code/patches/cis2-fp__cm_gpu3-batched-full.patch:79-108):
     every row of a batched decode equals its own batch-1 decode."""
@@ -128,6 +148,10 @@ def test_generate_rejects_bad_arguments(pkg, synth, synth_root):
         m.generate([[1, 2]], 5000)  # exceeds max_positions
     with pytest.raises(pkg.Cis2Error):
         m.generate([[1]], 2, sample={"seed": 1, "temperature": 0.0, "top_p": 0.9})
+    with pytest.raises(pkg.Cis2Error):  # top_k belongs to the Gumbel-max scheme
+        m.generate([[1]], 2, sample={"seed": 1, "temperature": 0.8, "top_p": 0.9, "top_k": 5})
+    with pytest.raises(pkg.Cis2Error):
+        m.generate([[1]], 2, sample={"scheme": "gumbel", "seed": 1, "temperature": float("inf"), "top_p": 0.9})
     r = m.generate([[1, 2]], 2)  # still usable after errors
     assert r["tokens"].shape == (1, 2)
 

@@ -121,3 +121,30 @@ def test_sampler_unit_cases_gpu(pkg):
     l2[7] = 50.0
     assert pkg.sample(l2, 1.0, 1e-6, 999, 3) == 7
     assert pkg.sample(np.zeros(4, np.float32), 1.0, 1e-6, 0, 0) == 0
+
+
+# ---------------------------------------------------------------- seeded Gumbel-max sampler (CIS2-SAMPLE-1)
+
+def test_gumbel_toy_vector_gpu(pkg):
+    # code/patches/cis2-spec__seeded-sampling.patch:157-164: next_id = 1
+    logits = np.array([1.0, 2.0, 2.0, -1.0, 0.5, 3.0, 3.0, -4.0], dtype=np.float32)
+    t = float(np.uint32(0x3F4CCCCD).view(np.float32))
+    p = float(np.uint32(0x3F666666).view(np.float32))
+    assert pkg.sample_gumbel(logits, t, 4, p, 1, 0) == 1
+
+
+@pytest.mark.parametrize("n", [8, 1000, 49152, 151936])
+@pytest.mark.parametrize("T,top_k,top_p", [(0.8, 40, 0.95), (1.0, 0, 1.0), (0.7, 0, 0.9), (1.3, 5, 1.0),
+                                           (0.5, 100000, 0.5), (2.0, 1, 0.3)])
+def test_gumbel_sampler_matches_oracle(n, T, top_k, top_p, pkg, oracle):
+    rng = np.random.default_rng(n * 7 + top_k)
+    for trial in range(3):
+        logits = (rng.standard_normal(n) * (0.5 + trial)).astype(np.float32)
+        if trial == 1:
+            logits[::3] = logits[1]      # exact ties: index order decides the rank
+        if trial == 2:
+            logits[: n // 2] = 0.0
+            logits[1: n // 2: 2] = -0.0  # -0 and +0 rank as equal values
+        for seed, step in ((1, 0), (0xFFFFFFFFFFFFFFFF, 7), (12345, 255)):
+            want, _ = oracle.sample_gumbel(logits, T, top_k, top_p, seed, step)
+            assert pkg.sample_gumbel(logits, T, top_k, top_p, seed, step) == want, (trial, seed, step)

@@ -182,3 +182,56 @@ def test_batch_equals_solo(oracle, synth, synth_root):
     for i, p in enumerate(ps):
         solo = o.generate([p], 6)
         assert solo["witness"][0].tobytes() == both["witness"][i].tobytes()
+
+
+# ---------------------------------------------------------------- seeded Gumbel-max sampler (CIS2-SAMPLE-1)
+
+def test_murmur3_published_answers(oracle):
+    # MurmurHash3_x86_32 of the empty key (seeded-sampling patch :91-93)
+    assert oracle.lib().cis2o_murmur3_32(None, 0, 0) == 0x00000000
+    assert oracle.lib().cis2o_murmur3_32(None, 0, 1) == 0x514E28B7
+
+
+@pytest.mark.parametrize("seed,step,index,h,u,g", [
+    # seeded-sampling patch :150-155 (hash seed 0x43495332)
+    (0x0000000000000001, 0, 0, 0x07731EA2, 0x3CEE63E0, 0xBFA1B32B),
+    (0x0000000000000001, 0, 1, 0xC832451B, 0x3F483245, 0x3FB392C7),
+    (0x0000000000000001, 1, 0, 0xC0D0C4FA, 0x3F40D0C5, 0x3FA15FFE),
+    (0xFFFFFFFFFFFFFFFF, 7, 49151, 0xE682298D, 0x3F668229, 0x40104F5A),
+    # toy vector rows of labs/w1x-sample/reports/w1x-sample/RESULTS-hq-builder.md:31-38
+    (1, 0, 2, 0x68663A0B, 0x3ED0CC76, 0x3DDEB89E),
+    (1, 0, 3, 0x0F68EB80, 0x3D768EB0, 0xBF844163),
+    (1, 0, 4, 0xEF1F23D1, 0x3F6F1F23, 0x402BDAE7),
+    (1, 0, 5, 0x62C78D96, 0x3EC58F1A, 0x3D483F2A),
+    (1, 0, 6, 0x03469A9A, 0x3C51A6C0, 0xBFBC6F8D),
+    (1, 0, 7, 0xDE644043, 0x3F5E6441, 0x3FFAFD67),
+])
+def test_gumbel_noise_known_answers(seed, step, index, h, u, g, oracle):
+    assert oracle.gumbel_noise(seed, step, index) == (h, u, g)
+
+
+def test_gumbel_toy_vector(oracle):
+    # seeded-sampling patch :157-164: V = 8, seed 1, step 0, T = 0.8, top_k 4, top_p 0.9
+    logits = np.array([1.0, 2.0, 2.0, -1.0, 0.5, 3.0, 3.0, -4.0], dtype=np.float32)
+    t = np.uint32(0x3F4CCCCD).view(np.float32)
+    p = np.uint32(0x3F666666).view(np.float32)
+    nxt, z = oracle.sample_gumbel(logits, float(t), 4, float(p), 1, 0)
+    assert nxt == 1
+    want = [0xFF800000, 0x4079C964, 0x4026F5C5, 0xFF800000, 0xFF800000, 0x407320FD, 0x4011C83A, 0xFF800000]
+    assert [int(v) for v in z.view(np.uint32)] == want
+
+
+def test_gumbel_candidate_set_rules(oracle):
+    rng = np.random.default_rng(11)
+    logits = rng.standard_normal(1000).astype(np.float32)
+    logits[10] = logits[20] = 9.0          # tie at the top: rank order puts index 10 first
+    # top_k = 1 keeps rank 0 only: the lowest index among the maximal logits
+    assert oracle.sample_gumbel(logits, 0.7, 1, 1.0, 5, 3)[0] == 10
+    # a tiny top_p keeps rank 0 only as well
+    assert oracle.sample_gumbel(logits, 0.7, 0, 1e-7, 5, 3)[0] == 10
+    # -0 and +0 are equal for the rank order
+    z = np.zeros(6, dtype=np.float32)
+    z[2] = -0.0
+    nxt, zz = oracle.sample_gumbel(z, 1.0, 3, 1.0, 9, 0)
+    kept = [i for i, v in enumerate(zz.view(np.uint32)) if v != 0xFF800000]
+    assert kept == [0, 1, 2]
