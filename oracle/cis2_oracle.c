@@ -17,6 +17,7 @@
  * library is safe to call from many threads at once.
  */
 #include "cis2_oracle.h"
+#include "math_sweep.h"
 
 #include <stdio.h>
 #include <stdlib.h>
@@ -950,4 +951,15 @@ void cis2o_sha256(const uint8_t *data, size_t n, uint8_t out[32]) {
   sha_init(&s);
   sha_update(&s, data, n);
   sha_final(&s, out);
+}
+
+/* Points of the pinned-function sweep (math_sweep.h), with this port's
+ * ln and exp for the RoPE family; out may be NULL to count. */
+static float sweep_ln(float x) { return p_ln(x); }
+static float sweep_exp(float x) { return p_exp(x); }
+size_t cis2o_math_sweep(float *out) {
+  fpenv_guard g = fp_enter();
+  const size_t n = cis2_math_sweep_inputs(out, sweep_ln, sweep_exp);
+  fp_leave(g);
+  return n;
 }

@@ -99,6 +99,8 @@ void cis2o_gumbel_noise(uint64_t seed, uint32_t step, uint32_t index, uint32_t *
 uint32_t cis2o_sample_gumbel(const float *logits, int32_t n, float temperature, uint32_t top_k, float top_p,
                              uint64_t seed, uint32_t step, float *z_out);
 void cis2o_sha256(const uint8_t *data, size_t n, uint8_t out[32]);
+/* The 242,428 points of the pinned-function sweep (math_sweep.h); out may be NULL. */
+size_t cis2o_math_sweep(float *out);
 /* Evaluate one pinned function over an array (f: 0 exp,1 sin,2 cos,3 ln,4 silu,5 rsqrt). */
 void cis2o_map(int32_t f, const float *x, float *y, size_t n);
 

@@ -87,6 +87,8 @@ def lib() -> ctypes.CDLL:
         L.cis2o_softmax.argtypes = [P, ctypes.c_int32, ctypes.c_int32]
         L.cis2o_argmax.restype = ctypes.c_uint32
         L.cis2o_argmax.argtypes = [P, ctypes.c_int32]
+        L.cis2o_math_sweep.restype = ctypes.c_size_t
+        L.cis2o_math_sweep.argtypes = [P]
         L.cis2o_murmur3_32.restype = ctypes.c_uint32
         L.cis2o_murmur3_32.argtypes = [P, ctypes.c_size_t, ctypes.c_uint32]
         L.cis2o_gumbel_noise.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, P, P, P]
@@ -307,3 +309,40 @@ def sample_gumbel(logits, temperature: float, top_k: int, top_p: float, seed: in
     z = np.zeros_like(x)
     r = lib().cis2o_sample_gumbel(_ptr(x), x.size, temperature, top_k, top_p, seed, step, _ptr(z))
     return int(r), z
+
+
+def math_sweep_inputs() -> np.ndarray:
+    """The pinned-function sweep points (oracle/math_sweep.h), fp32."""
+    n = lib().cis2o_math_sweep(None)
+    x = np.zeros(n, dtype=np.float32)
+    lib().cis2o_math_sweep(_ptr(x))
+    return x
+
+
+MATH_FUNCS = ("exp", "sin", "cos", "ln", "silu", "rsqrt")
+
+
+def sweep_digests(x: np.ndarray, outs: dict) -> dict:
+    """Digests of a sweep's outputs: NaNs canonicalised to 0x7FC00000 (their
+    encoding differs between x86 SSE and the GPU for NaNs produced by
+    arithmetic), plus the set of indices that are NaN."""
+    import hashlib
+    res = {"n": int(x.size), "inputs_sha256": hashlib.sha256(x.view(np.uint32).astype("<u4").tobytes()).hexdigest()}
+    for f in MATH_FUNCS:
+        y = np.ascontiguousarray(outs[f], dtype=np.float32).view(np.uint32).copy()
+        nan = np.isnan(outs[f])
+        y[nan] = 0x7FC00000
+        res[f] = {"canon_sha256": hashlib.sha256(y.astype("<u4").tobytes()).hexdigest(),
+                  "nan_count": int(nan.sum()),
+                  "nan_index_sha256": hashlib.sha256(np.nonzero(nan)[0].astype("<u4").tobytes()).hexdigest()}
+    return res
+
+
+def read_refmath(path: str) -> tuple[np.ndarray, dict]:
+    """Reads oracle/_ref/refmath output: (x, {fn: y})."""
+    raw = open(path, "rb").read()
+    assert raw[:8] == b"CIS2MSW1"
+    n = int(np.frombuffer(raw[8:12], dtype="<u4")[0])
+    rec = np.frombuffer(raw[12:12 + 28 * n], dtype="<u4").reshape(n, 7)
+    x = rec[:, 0].copy().view(np.float32)
+    return x, {f: rec[:, i + 1].copy().view(np.float32) for i, f in enumerate(MATH_FUNCS)}

@@ -51,7 +51,8 @@ def load_golden(name: str) -> dict:
 
 
 def golden_names() -> list[str]:
-    return sorted(f[:-5] for f in os.listdir(GOLDEN) if f.endswith(".json"))
+    """Decode fixtures (math_sweep.json holds the pinned-function sweep instead)."""
+    return sorted(f[:-5] for f in os.listdir(GOLDEN) if f.endswith(".json") and not f.startswith("math_"))
 
 
 def golden_prompts(synth, g: dict) -> list:

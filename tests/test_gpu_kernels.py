@@ -41,6 +41,27 @@ def sweep_inputs() -> np.ndarray:
     return np.array(v, dtype=np.float32)
 
 
+def test_pinned_math_reference_sweep(pkg, oracle):
+    """The device's six pinned functions over the reference sweep's 242,428
+    points: every non-NaN output bit-identical to the reference's
+    cis2_math.h (digests in tests/golden/math_sweep.json), NaN exactly where
+    the reference gives NaN, and the explicit NaN returns of exp and ln
+    (0x7FC00000 for a NaN input) bit for bit."""
+    import json
+    import os
+    with open(os.path.join(os.path.dirname(__file__), "golden", "math_sweep.json")) as f:
+        g = json.load(f)
+    x = oracle.math_sweep_inputs()
+    outs = {f: pkg.pinned_map(f, x) for f in oracle.MATH_FUNCS}
+    d = oracle.sweep_digests(x, outs)
+    assert d["inputs_sha256"] == g["inputs_sha256"]
+    for f in oracle.MATH_FUNCS:
+        assert d[f] == g[f], f
+    nan_in = np.isnan(x)
+    for f in ("exp", "ln"):
+        assert np.all(outs[f][nan_in].view(np.uint32) == 0x7FC00000), f
+
+
 @pytest.mark.parametrize("fn", ["exp", "sin", "cos", "ln", "silu", "rsqrt"])
 def test_pinned_math_bit_exact(fn, pkg, oracle):
     x = sweep_inputs()

@@ -235,3 +235,43 @@ def test_gumbel_candidate_set_rules(oracle):
     nxt, zz = oracle.sample_gumbel(z, 1.0, 3, 1.0, 9, 0)
     kept = [i for i, v in enumerate(zz.view(np.uint32)) if v != 0xFF800000]
     assert kept == [0, 1, 2]
+
+
+# ---------------------------------------------------------------- pinned-function sweep
+
+def _math_fixture():
+    import json
+    import os
+    with open(os.path.join(os.path.dirname(__file__), "golden", "math_sweep.json")) as f:
+        return json.load(f)
+
+
+def test_math_sweep_port_matches_reference_digests(oracle):
+    """The port's six pinned functions over the 242,428-point sweep equal the
+    reference's cis2_math.h (fixture written by tests/golden/make_math_golden.py)."""
+    g = _math_fixture()
+    x = oracle.math_sweep_inputs()
+    outs = {f: oracle.pinned_map(i, x) for i, f in enumerate(oracle.MATH_FUNCS)}
+    d = oracle.sweep_digests(x, outs)
+    assert d["n"] == g["n"] == 242428
+    assert d["inputs_sha256"] == g["inputs_sha256"]
+    for f in oracle.MATH_FUNCS:
+        assert d[f] == g[f], f
+    # x86 SSE on both sides: the exact rows, NaN encodings included
+    for i, row in zip(g["row_index"], g["rows"]):
+        assert int(x.view(np.uint32)[i]) == row[0]
+        assert [int(outs[f].view(np.uint32)[i]) for f in oracle.MATH_FUNCS] == row[1:], i
+
+
+def test_math_sweep_port_equals_reference_binary(oracle, tmp_path):
+    """Bit for bit against the reference functions run live, when oracle/_ref is built."""
+    import os
+    import subprocess
+    exe = os.path.join(oracle.REF_DIR, "refmath")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref not built")
+    subprocess.run([exe, str(tmp_path / "s.bin")], check=True, capture_output=True)
+    x, ref = oracle.read_refmath(str(tmp_path / "s.bin"))
+    assert np.array_equal(x.view(np.uint32), oracle.math_sweep_inputs().view(np.uint32))
+    for i, f in enumerate(oracle.MATH_FUNCS):
+        assert np.array_equal(oracle.pinned_map(i, x).view(np.uint32), ref[f].view(np.uint32)), f
