@@ -100,6 +100,7 @@ def lib() -> ctypes.CDLL:
     L.cis2b_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(_Opts), ctypes.POINTER(P)]
     L.cis2b_info_get.argtypes = [P, ctypes.POINTER(_Info)]
     L.cis2b_generate.argtypes = [P, P, P, U32, U32, ctypes.POINTER(_Sample), P, P, P, P]
+    L.cis2b_verify.argtypes = [P, P, P, U32, P, U32, ctypes.POINTER(_Sample), P, P, P, P, P]
     L.cis2b_last_timing.argtypes = [P, ctypes.POINTER(_Timing)]
     L.cis2b_logits.argtypes = [P, P, U32, U32, P]
     L.cis2b_profile.argtypes = [P, U32]
@@ -177,6 +178,25 @@ class Model:
         _check(lib().cis2b_generate(self._h, _ptr(flat), _ptr(lens), n, gen, smp, _ptr(toks), _ptr(steps),
                                     _ptr(wit), _ptr(arg)))
         return {"tokens": toks, "step_digests": steps, "witness": wit, "argmax": arg}
+
+    def verify(self, prompts, claimed, sample: dict | None = None, step_digests: bool = True) -> dict:
+        """Teacher-forced receipt verification: claimed[i] is sequence i's
+        generated id list (all the same length).  Returns the recomputed
+        tokens, first_mismatch per sequence (-1 = none) and the digests."""
+        rows = [np.asarray(p, dtype=np.uint32).ravel() for p in prompts]
+        lens = np.array([len(r) for r in rows], dtype=np.uint32)
+        flat = np.ascontiguousarray(np.concatenate(rows) if rows else np.zeros(0, np.uint32))
+        cl = np.ascontiguousarray(np.asarray(claimed, dtype=np.uint32).reshape(len(rows), -1))
+        n, gen = cl.shape
+        toks = np.zeros((n, gen), dtype=np.uint32)
+        first = np.zeros(n, dtype=np.int32)
+        steps = np.zeros((n, gen, 32), dtype=np.uint8) if step_digests else None
+        wit = np.zeros((n, 32), dtype=np.uint8)
+        arg = np.zeros((n, 32), dtype=np.uint8)
+        smp = ctypes.byref(_sample_struct(sample)) if sample else None
+        _check(lib().cis2b_verify(self._h, _ptr(flat), _ptr(lens), n, _ptr(cl), gen, smp, _ptr(toks), _ptr(first),
+                                  _ptr(steps), _ptr(wit), _ptr(arg)))
+        return {"tokens": toks, "first_mismatch": first, "step_digests": steps, "witness": wit, "argmax": arg}
 
     def timing(self) -> dict:
         t = _Timing()

@@ -645,9 +645,17 @@ int alloc_cache(cis2b_model *m, int n_seq, int maxP) {
   return CIS2B_OK;
 }
 
+// Generation, or -- with `claimed` ([n_seq][gen] ids) -- teacher-forced
+// receipt verification (verify3/model.c:923-1004): ONE prompt pass over
+// prompt + claimed[0 .. gen-2] per sequence yields the hidden state of every
+// claimed position; each step then runs the same head, the same selection
+// (argmax or sampler: the token is RECOMPUTED, never taken from the claim)
+// and the same witness absorb as generation, so an honest claim reproduces
+// the generation digests exactly.
 int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *prompt_lens,
                   uint32_t n_seq, uint32_t gen, const cis2b_sample *sample, uint32_t *out_tokens,
-                  uint8_t *out_steps, uint8_t *out_witness, uint8_t *out_argmax) {
+                  uint8_t *out_steps, uint8_t *out_witness, uint8_t *out_argmax,
+                  const uint32_t *claimed = nullptr) {
   if (!m) return fail(CIS2B_ERR_ARG, "model is NULL");
   if (n_seq == 0) return CIS2B_OK;
   if (!prompt_ids || !prompt_lens || !out_witness) return fail(CIS2B_ERR_ARG, "NULL input/output buffer");
@@ -669,6 +677,10 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   }
   for (size_t i = 0; i < total_prompt; ++i)
     if (prompt_ids[i] >= (uint32_t)m->V) return fail(CIS2B_ERR_ARG, "prompt id out of vocabulary range");
+  const bool tf = claimed != nullptr;  // teacher-forced verification
+  if (tf)
+    for (size_t i = 0; i < (size_t)B * G; ++i)
+      if (claimed[i] >= (uint32_t)m->V) return fail(CIS2B_ERR_ARG, "claimed id out of vocabulary range");
   const int maxP = (int)maxP0 + G;
   if (maxP > m->max_pos)
     return fail(CIS2B_ERR_ARG, "prompt + gen_toks exceeds max_positions (" + std::to_string(m->max_pos) + ")");
@@ -679,7 +691,8 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   ring = std::min(ring, std::max(1, G));
   int rc = alloc_cache(m, B, maxP);
   if (rc) return rc;
-  if (m->ring.ensure((size_t)ring * per_slot) || m->hlast.ensure(4 * (size_t)B * m->H) ||
+  const size_t hrows = tf ? (size_t)B * std::max(G, 1) : (size_t)B;  // hidden rows kept from the prompt pass
+  if (m->ring.ensure((size_t)ring * per_slot) || m->hlast.ensure(4 * hrows * m->H) ||
       m->lnlast.ensure(4 * (size_t)round_up(B, 64) * m->H) || m->d_next.ensure(4 * (size_t)B) ||
       m->d_pos.ensure(4 * (size_t)B) || m->d_spos.ensure(4 * (size_t)B) || m->d_seq.ensure(4 * (size_t)B) ||
       m->d_ctl.ensure(64) || m->d_tokens.ensure(4 * (size_t)B * std::max(G, 1)) ||
@@ -702,21 +715,37 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   m->prof_events.clear();
 
   // ---- host-side staging (all before the first launch)
-  std::vector<uint32_t> rtok(total_prompt);
-  std::vector<int32_t> rseq(total_prompt), rpos(total_prompt), osrc(B), odst(B), iota(B), pos0(B), spos0(B);
+  const size_t tf_rows = tf && G > 1 ? (size_t)B * (G - 1) : 0;  // claimed tokens fed back as inputs
+  std::vector<uint32_t> rtok(total_prompt + tf_rows);
+  std::vector<int32_t> rseq(total_prompt + tf_rows), rpos(total_prompt + tf_rows), osrc, odst;
+  std::vector<int32_t> iota(B), pos0(B), spos0(B);
   std::vector<uint32_t> poff(B), plen(B);
   {
-    size_t r = 0;
+    size_t r = 0, pr = 0;
     for (int b = 0; b < B; ++b) {
-      poff[b] = (uint32_t)r;
+      poff[b] = (uint32_t)pr;
       plen[b] = prompt_lens[b];
-      for (uint32_t p = 0; p < prompt_lens[b]; ++p, ++r) {
-        rtok[r] = prompt_ids[r];
+      const size_t r0 = r;
+      for (uint32_t p = 0; p < prompt_lens[b]; ++p, ++r, ++pr) {
+        rtok[r] = prompt_ids[pr];
         rseq[r] = b;
         rpos[r] = (int32_t)p;
       }
-      osrc[b] = (int32_t)(r - 1);
-      odst[b] = b;
+      if (tf) {
+        for (int t = 0; t + 1 < G; ++t, ++r) {
+          rtok[r] = claimed[(size_t)b * G + t];
+          rseq[r] = b;
+          rpos[r] = (int32_t)(prompt_lens[b] + t);
+        }
+        // step t's logits come from position prompt_len - 1 + t (model.c:936-941)
+        for (int t = 0; t < G; ++t) {
+          osrc.push_back((int32_t)(r0 + prompt_lens[b] - 1 + t));
+          odst.push_back(t * B + b);
+        }
+      } else {
+        osrc.push_back((int32_t)(r - 1));
+        odst.push_back(b);
+      }
       iota[b] = b;
       pos0[b] = (int32_t)prompt_lens[b] - 1;
       spos0[b] = (int32_t)prompt_lens[b];
@@ -775,7 +804,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   CU(cudaMemcpyAsync(m->hdr_bytes.p, hb.data(), hb.size(), cudaMemcpyHostToDevice, s));
   CU(cudaMemcpyAsync(m->hdr_off.p, hoff.data(), 4 * hoff.size(), cudaMemcpyHostToDevice, s));
   CU(cudaMemcpyAsync(m->sha_state.p, st0.data(), sizeof(ShaState) * st0.size(), cudaMemcpyHostToDevice, s));
-  CU(cudaMemcpyAsync(m->p_flat.p, rtok.data(), 4 * total_prompt, cudaMemcpyHostToDevice, s));
+  CU(cudaMemcpyAsync(m->p_flat.p, prompt_ids, 4 * total_prompt, cudaMemcpyHostToDevice, s));
   CU(cudaMemcpyAsync(m->p_off.p, poff.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
   CU(cudaMemcpyAsync(m->p_len.p, plen.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
   CU(cudaMemcpyAsync(m->d_seq.p, iota.data(), 4 * (size_t)B, cudaMemcpyHostToDevice, s));
@@ -827,7 +856,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
     return CIS2B_OK;
   };
   const uint32_t in_graph = CIS2B_PROF_LM_HEAD | CIS2B_PROF_LAYER_GEMM | CIS2B_PROF_ATTENTION;
-  const bool use_graph = G >= 3 && !(m->prof_mask & in_graph);
+  const bool use_graph = !tf && G >= 3 && !(m->prof_mask & in_graph);
   cudaGraphExec_t gexec = nullptr;
   int64_t step_launches = 0;
   if (use_graph) {
@@ -850,6 +879,11 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   } guard{gexec};
   for (int t = 0; t < G; ++t) {
     if (t == 0) {
+      select();
+    } else if (tf) {
+      if (t >= ring) CU(cudaStreamWaitEvent(s, m->ev_sha[(size_t)(t % ring)], 0));
+      rc = head_rows(m, m->hlast.as<float>() + (size_t)t * B * m->H, B, ring_base, d_slot, (size_t)B * V);
+      if (rc) return rc;
       select();
     } else {
       if (t >= ring) CU(cudaStreamWaitEvent(s, m->ev_sha[(size_t)(t % ring)], 0));
@@ -905,7 +939,8 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   // bytes the call moved across PCIe: header bytes, offsets, states, prompt
   // ids and row maps in; tokens, digests out.
   m->timing.h2d_bytes = (int64_t)(hb.size() + 4 * hoff.size() + sizeof(ShaState) * st0.size() +
-                                  4 * total_prompt * 4 + 4 * (size_t)B * 6 + 8 * (size_t)B);
+                                  4 * total_prompt + 4 * rtok.size() * 3 + 8 * osrc.size() +
+                                  4 * (size_t)B * 6 + 8 * (size_t)B);
   m->timing.d2h_bytes = (int64_t)((out_tokens ? 4 * (size_t)B * G : 0) + (out_steps ? 32 * (size_t)B * G : 0) +
                                   32 * (size_t)B + (out_argmax ? 32 * (size_t)B : 0));
   for (auto &k : m->prof) k = cis2b_kernel_time{0, 0.0};
@@ -986,6 +1021,27 @@ int cis2b_generate(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *p
                          out_witness, out_argmax);
   if (rc == CIS2B_OK) g_err.clear();
   return rc;
+}
+
+int cis2b_verify(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *prompt_lens, uint32_t n_seq,
+                 const uint32_t *claimed, uint32_t gen_toks, const cis2b_sample *sample, uint32_t *out_tokens,
+                 int32_t *out_first_mismatch, uint8_t *out_step_digests, uint8_t *out_witness,
+                 uint8_t *out_argmax) {
+  if (!claimed && n_seq && gen_toks) return fail(CIS2B_ERR_ARG, "claimed ids are NULL");
+  std::vector<uint32_t> toks((size_t)n_seq * gen_toks + 1);
+  static const uint32_t no_claim = 0;
+  int rc = generate_impl(m, prompt_ids, prompt_lens, n_seq, gen_toks, sample, toks.data(), out_step_digests,
+                         out_witness, out_argmax, claimed ? claimed : &no_claim);
+  if (rc) return rc;
+  for (uint32_t b = 0; b < n_seq; ++b) {
+    int32_t first = -1;
+    for (uint32_t t = 0; t < gen_toks; ++t)
+      if (toks[(size_t)b * gen_toks + t] != claimed[(size_t)b * gen_toks + t]) { first = (int32_t)t; break; }
+    if (out_first_mismatch) out_first_mismatch[b] = first;
+  }
+  if (out_tokens && n_seq && gen_toks) memcpy(out_tokens, toks.data(), 4 * (size_t)n_seq * gen_toks);
+  g_err.clear();
+  return CIS2B_OK;
 }
 
 int cis2b_last_timing(const cis2b_model *m, cis2b_timing *out) {

@@ -136,6 +136,24 @@ int cis2b_profile(cis2b_model *m, uint32_t class_mask);
 /* Totals of the last cis2b_generate for ONE class bit. */
 int cis2b_profile_read(const cis2b_model *m, uint32_t class_bit, cis2b_kernel_time *out);
 
+/* Receipt verification, teacher-forced (replaces cis2_verify_receipt_prefill,
+ * code/cis2-fp/verify3/model.h:151-157, and the claim check of
+ * verify3/main.c:230-265, batched over sequences).  For each sequence ONE
+ * forward pass over prompt + claimed[0 .. gen-2] gives the logits of every
+ * claimed step; the token of each step is RECOMPUTED from them (argmax, or
+ * the sampler in `sample`) and the witness is rebuilt exactly as
+ * cis2b_generate builds it.  An honest claim therefore reproduces the
+ * generation's tokens and digests.
+ *   claimed           [n_seq][gen]  the receipt's generated ids
+ *   out_tokens        [n_seq][gen]  recomputed ids (may be NULL)
+ *   out_first_mismatch [n_seq]      first step whose recomputed id differs
+ *                                   from the claim, -1 if none (may be NULL)
+ *   out_step_digests, out_witness, out_argmax as cis2b_generate. */
+int cis2b_verify(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *prompt_lens, uint32_t n_seq,
+                 const uint32_t *claimed, uint32_t gen_toks, const cis2b_sample *sample, uint32_t *out_tokens,
+                 int32_t *out_first_mismatch, uint8_t *out_step_digests, uint8_t *out_witness,
+                 uint8_t *out_argmax);
+
 /* Teacher-forced logits of ONE sequence: runs ids[0 .. n_prompt+n_rows-2]
  * and writes the fp32 logits after positions n_prompt-1 .. n_prompt+n_rows-2
  * into out_logits[n_rows][vocab]. */
