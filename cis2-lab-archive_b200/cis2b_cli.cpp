@@ -15,8 +15,15 @@
 //
 //   cis2b_ref --weights-dir D --ids F [--gen-toks N] [--reduction sequential|tree]
 //             [--mode greedy|sampled --seed S --temperature T --top-p P]
-//             [--sample SEED,T,K,P]
+//             [--sample SEED,T,K,P] [--receipt F]
 //             [--device I] [--prompt-idx I] [--step-digests]
+// With --receipt F (one line of claimed generated ids per prompt, all the
+// same length) the prompts are VERIFIED instead of decoded: one
+// teacher-forced pass (cis2b_verify), and per prompt the lines
+//   CIS2_VERIFY3 digest=<hex> prompt_idx=N prompt_toks=N gen_toks=N dtype=fp32
+//   CIS2_VERIFY3 argmax_digest= / table_digest= / inv_freq_table_digest=
+//   CIS2_VERIFY3 generated_token_ids=a,b,... / first_mismatch_pos=K
+// of code/cis2-fp/verify3/main.c:272-318; exit status 1 if any claim differs.
 // Each non-empty line of F is one prompt (decimal ids); all prompts are
 // decoded as one batch and reported in file order.
 #include "cis2b.h"
@@ -54,8 +61,31 @@ static std::string f32_str(float x) {
   return buf;
 }
 
+// Lines of decimal ids separated by blanks or commas; empty lines skipped.
+static bool read_id_lines(const std::string &path, std::vector<std::vector<uint32_t>> &lines) {
+  FILE *f = fopen(path.c_str(), "rb");
+  if (!f) { fprintf(stderr, "FATAL: cannot open %s\n", path.c_str()); return false; }
+  std::vector<uint32_t> cur;
+  std::string num;
+  int c;
+  auto flush_num = [&]() {
+    if (!num.empty()) { cur.push_back((uint32_t)strtoul(num.c_str(), nullptr, 10)); num.clear(); }
+  };
+  bool ok = true;
+  while ((c = fgetc(f)) != EOF) {
+    if (c >= '0' && c <= '9') num.push_back((char)c);
+    else if (c == '\n') { flush_num(); if (!cur.empty()) lines.push_back(cur); cur.clear(); }
+    else if (c == ' ' || c == '\t' || c == ',' || c == '\r') flush_num();
+    else { fprintf(stderr, "FATAL: %s: unexpected character\n", path.c_str()); ok = false; break; }
+  }
+  flush_num();
+  if (!cur.empty()) lines.push_back(cur);
+  fclose(f);
+  return ok;
+}
+
 int main(int argc, char **argv) {
-  std::string weights_dir = "weights", ids_path;
+  std::string weights_dir = "weights", ids_path, receipt_path;
   int gen = 16, device = 0, prompt_idx = 0;
   bool tree = false, sampled = false, gumbel = false, step_digests = false;
   cis2b_sample smp{0, 0.8f, 0.95f, CIS2B_SAMPLE_E23, 0};
@@ -95,34 +125,29 @@ int main(int argc, char **argv) {
       smp.top_p = strtof(pbuf, nullptr);
       smp.scheme = CIS2B_SAMPLE_GUMBEL;
       gumbel = true;
-    } else if (a == "--seed") smp.seed = strtoull(next(), nullptr, 10);
+    } else if (a == "--receipt") receipt_path = next();
+    else if (a == "--seed") smp.seed = strtoull(next(), nullptr, 10);
     else if (a == "--temperature") smp.temperature = strtof(next(), nullptr);
     else if (a == "--top-p") smp.top_p = strtof(next(), nullptr);
     else { fprintf(stderr, "FATAL: unknown CLI argument: %s\n", a.c_str()); return 2; }
   }
   if (ids_path.empty() || gen < 0) { fprintf(stderr, "FATAL: --ids FILE is required\n"); return 2; }
 
-  std::vector<std::vector<uint32_t>> prompts;
-  {
-    FILE *f = fopen(ids_path.c_str(), "rb");
-    if (!f) { fprintf(stderr, "FATAL: cannot open %s\n", ids_path.c_str()); return 2; }
-    std::vector<uint32_t> cur;
-    std::string num;
-    int c;
-    auto flush_num = [&]() {
-      if (!num.empty()) { cur.push_back((uint32_t)strtoul(num.c_str(), nullptr, 10)); num.clear(); }
-    };
-    while ((c = fgetc(f)) != EOF) {
-      if (c >= '0' && c <= '9') num.push_back((char)c);
-      else if (c == '\n') { flush_num(); if (!cur.empty()) prompts.push_back(cur); cur.clear(); }
-      else if (c == ' ' || c == '\t' || c == ',' || c == '\r') flush_num();
-      else { fprintf(stderr, "FATAL: %s: unexpected character\n", ids_path.c_str()); return 2; }
-    }
-    flush_num();
-    if (!cur.empty()) prompts.push_back(cur);
-    fclose(f);
-  }
+  std::vector<std::vector<uint32_t>> prompts, claims;
+  if (!read_id_lines(ids_path, prompts)) return 2;
   if (prompts.empty()) { fprintf(stderr, "FATAL: %s: no token ids\n", ids_path.c_str()); return 2; }
+  const bool verify = !receipt_path.empty();
+  if (verify) {
+    if (!read_id_lines(receipt_path, claims)) return 2;
+    if (claims.size() != prompts.size()) {
+      fprintf(stderr, "FATAL: %s: %zu claim lines for %zu prompts\n", receipt_path.c_str(), claims.size(),
+              prompts.size());
+      return 2;
+    }
+    gen = (int)claims[0].size();
+    for (auto &c : claims)
+      if ((int)c.size() != gen) { fprintf(stderr, "FATAL: %s: claim lines differ in length\n", receipt_path.c_str()); return 2; }
+  }
 
   cis2b_opts o{};
   o.device = device;
@@ -147,8 +172,35 @@ int main(int argc, char **argv) {
     fprintf(stderr, "FATAL: --mode sampled (E23) and --sample (CIS2-SAMPLE-1) exclude each other\n");
     return 2;
   }
-  if (cis2b_generate(m, flat.data(), lens.data(), n, (uint32_t)gen, (sampled || gumbel) ? &smp : nullptr, toks.data(),
-                     steps.data(), wit.data(), arg.data()) != CIS2B_OK) {
+  const cis2b_sample *sp = (sampled || gumbel) ? &smp : nullptr;
+  if (verify) {
+    std::vector<uint32_t> cl;
+    for (auto &c : claims) cl.insert(cl.end(), c.begin(), c.end());
+    std::vector<int32_t> first(n);
+    if (cis2b_verify(m, flat.data(), lens.data(), n, cl.data(), (uint32_t)gen, sp, toks.data(), first.data(),
+                     nullptr, wit.data(), arg.data()) != CIS2B_OK) {
+      fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
+      cis2b_free(m);
+      return 2;
+    }
+    int bad = 0;
+    for (uint32_t s = 0; s < n; ++s) {
+      const int pi = prompt_idx + (int)s;
+      printf("CIS2_VERIFY3 digest=%s prompt_idx=%d prompt_toks=%u gen_toks=%d dtype=fp32\n",
+             hexs(&wit[(size_t)s * 32], 32).c_str(), pi, lens[s], gen);
+      printf("CIS2_VERIFY3 argmax_digest=%s\n", hexs(&arg[(size_t)s * 32], 32).c_str());
+      printf("CIS2_VERIFY3 table_digest=%s\n", hexs(info.table_digest, 32).c_str());
+      printf("CIS2_VERIFY3 inv_freq_table_digest=%s\n", hexs(info.inv_freq_table_digest, 32).c_str());
+      printf("CIS2_VERIFY3 generated_token_ids=");
+      for (int t = 0; t < gen; ++t) printf("%s%u", t ? "," : "", toks[(size_t)s * gen + t]);
+      printf("\nCIS2_VERIFY3 first_mismatch_pos=%d\n", first[s]);
+      bad += first[s] >= 0;
+    }
+    cis2b_free(m);
+    return bad ? 1 : 0;
+  }
+  if (cis2b_generate(m, flat.data(), lens.data(), n, (uint32_t)gen, sp, toks.data(), steps.data(), wit.data(),
+                     arg.data()) != CIS2B_OK) {
     fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
     cis2b_free(m);
     return 2;

@@ -91,3 +91,29 @@ def test_verify_rejects_out_of_range_claims(pkg, synth, synth_root):
     assert e.value.code == 1
     r = m.verify([[1, 2]], [[3, 4]])     # still usable
     assert r["tokens"].shape == (1, 2)
+
+
+def test_cli_verifies_a_receipt(pkg, synth, synth_root, tmp_path):
+    """cis2b_ref --receipt prints the verify3 lines (verify3/main.c:272-318)
+    and exits 1 when a claim differs from the recomputed tokens."""
+    import subprocess
+    m = model_for(pkg, synth, synth_root, "tiny", "sequential")
+    prompts = _prompts(synth, "tiny", [3, 7], 111)
+    g = m.generate(prompts, 8)
+    ids = tmp_path / "ids.txt"
+    ids.write_text("\n".join(" ".join(str(int(v)) for v in p) for p in prompts) + "\n")
+    rec = tmp_path / "receipt.txt"
+    rec.write_text("\n".join(",".join(str(int(v)) for v in t) for t in g["tokens"]) + "\n")
+    cmd = [pkg.CLI_PATH, "--weights-dir", synth.ensure_model("tiny", synth_root), "--ids", str(ids),
+           "--receipt", str(rec)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    dig = [ln.split()[1].split("=")[1] for ln in r.stdout.splitlines() if ln.startswith("CIS2_VERIFY3 digest=")]
+    assert dig == [w.tobytes().hex() for w in g["witness"]]
+    assert r.stdout.count("CIS2_VERIFY3 first_mismatch_pos=-1") == 2
+    bad = g["tokens"].copy()
+    bad[0, 2] = (bad[0, 2] + 1) % 512
+    rec.write_text("\n".join(",".join(str(int(v)) for v in t) for t in bad) + "\n")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 1
+    assert "CIS2_VERIFY3 first_mismatch_pos=2" in r.stdout
