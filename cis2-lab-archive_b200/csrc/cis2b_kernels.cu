@@ -783,6 +783,9 @@ int gemm_dec_choice(int M, int N, int K) {
   for (int i = 0; i < kNumDecTiles; ++i) {
     const int rows = kDecTiles[i].tm * kDecTiles[i].rw;
     if ((size_t)rows * K * 4 + (size_t)DEC_STAGES * DEC_KC * 64 > 227 * 1024) continue;
+    // Eight rows per lane pay off only on very wide products (lm_head):
+    // measured on B200, 4 x 4 is faster for the layer projections at 64 and 300 rows.
+    if (kDecTiles[i].tm == 8 && N < 16384) continue;
     pick = i;
     if (n32 * ((M + rows - 1) / rows) >= 2 * 148) break;
   }
@@ -1169,7 +1172,10 @@ __device__ __forceinline__ uint64_t sm64_round(uint64_t x) {
 }
 
 // Serial fold driver: thread 0 calls op(i, value) for i = 0..n-1 in order,
-// op returns true to stop early.  Other threads stage the next chunk.
+// op returns true to stop early.  The other threads stage the next chunk
+// (computing load(i) in parallel), thread 0 reads its chunk 32 values at a
+// time with 16-byte loads, so its chain waits on adds, not on shared-memory
+// latency.  buf: 2 * FOLD_CHUNK floats, 16-byte aligned.
 template <class Load, class Op>
 __device__ void serial_fold(int n, Load load, Op op, float *buf, int *stop_flag) {
   const int tid = threadIdx.x;
@@ -1182,9 +1188,24 @@ __device__ void serial_fold(int n, Load load, Op op, float *buf, int *stop_flag)
     float *nxt = buf + ((c + 1) & 1) * FOLD_CHUNK;
     const int base = c * FOLD_CHUNK, cnt = min(FOLD_CHUNK, n - base);
     if (tid == 0) {
-      if (!*stop_flag)
-        for (int i = 0; i < cnt; ++i)
-          if (op(base + i, cur[i])) { *stop_flag = 1; break; }
+      if (!*stop_flag) {
+        bool stop = false;
+        int i = 0;
+        for (; i + 32 <= cnt && !stop; i += 32) {
+          float v[32];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float4 q = reinterpret_cast<const float4 *>(cur + i)[u];
+            v[4 * u] = q.x; v[4 * u + 1] = q.y; v[4 * u + 2] = q.z; v[4 * u + 3] = q.w;
+          }
+#pragma unroll
+          for (int u = 0; u < 32; ++u)
+            if (op(base + i + u, v[u])) { stop = true; break; }
+        }
+        for (; i < cnt && !stop; ++i)
+          if (op(base + i, cur[i])) stop = true;
+        if (stop) *stop_flag = 1;
+      }
     } else if (c + 1 < nch) {
       const int nb = base + FOLD_CHUNK, ncnt = min(FOLD_CHUNK, n - nb);
       for (int i = tid - 1; i < ncnt; i += blockDim.x - 1) nxt[i] = load(nb + i);
@@ -1250,7 +1271,7 @@ __device__ void block_radix_sort(uint32_t *kA, uint32_t *vA, uint32_t *kB, uint3
 __global__ void __launch_bounds__(SAMPLE_THREADS)
 k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, float temperature,
          float top_p, uint64_t seed, const int32_t *position, float *scratch, uint32_t *next) {
-  __shared__ float buf[2 * FOLD_CHUNK];
+  __shared__ __align__(16) float buf[2 * FOLD_CHUNK];
   __shared__ int hist[256];
   __shared__ int base[256];
   __shared__ int wcnt[SAMPLE_THREADS / 32][256];
@@ -1328,9 +1349,9 @@ k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, fl
   const double u = __dmul_rn((double)(word >> 11), 1.0 / 9007199254740992.0);
   float cdf = 0.0f;
   int pick = nuc - 1;
-  serial_fold(nuc, [&](int i) { return __uint_as_float(~ki[i]); },
+  serial_fold(nuc, [&](int i) { return fdiv(__uint_as_float(~ki[i]), total); },
               [&](int i, float v) {
-                cdf = fadd(cdf, fdiv(v, total));
+                cdf = fadd(cdf, v);
                 if ((double)cdf > u) { pick = i; return true; }
                 return false;
               },
@@ -1388,7 +1409,7 @@ __device__ __forceinline__ float gumbel_noise(uint64_t seed, uint32_t step, uint
 __global__ void __launch_bounds__(SAMPLE_THREADS)
 k_sample_gumbel(const float *logits, int V, const int32_t *slot, size_t slot_stride, float temperature,
                 uint32_t top_k, float top_p, uint64_t seed, const int32_t *step, float *scratch, uint32_t *next) {
-  __shared__ float buf[2 * FOLD_CHUNK];
+  __shared__ __align__(16) float buf[2 * FOLD_CHUNK];
   __shared__ int hist[256];
   __shared__ int base[256];
   __shared__ int wcnt[SAMPLE_THREADS / 32][256];
