@@ -1218,53 +1218,92 @@ __device__ void serial_fold(int n, Load load, Op op, float *buf, int *stop_flag)
 // Stable LSD radix sort of (key, value) pairs by key ascending, 4 passes of
 // 8 bits, by the whole block; the result ends in (kA, vA).  Values that come
 // in index order therefore keep index order among equal keys.
+//
+// Each warp owns one contiguous segment of the input.  Per pass it counts
+// its segment's digits (32 at a time: lanes with equal digits find each
+// other with match_any and the lowest of them adds the group's size), one
+// block-wide scan turns the (digit, warp) counts into output offsets, and
+// each warp then writes its segment in order, every element at
+// offset(digit, warp) + (equal digits before it in the segment).  The
+// output order is (digit, warp, position in segment) = (digit, index): the
+// pass is stable, with block barriers only between the phases of a pass.
+// A pass whose digit is the same for every key moves nothing and is
+// skipped.  wcnt holds [blockDim.x / 32][256] counters.
 __device__ void block_radix_sort(uint32_t *kA, uint32_t *vA, uint32_t *kB, uint32_t *vB, int V, int *hist,
                                  int *base, int (*wcnt)[256]) {
   const int tid = threadIdx.x, nt = blockDim.x;
-  const int warp = tid >> 5, lane = tid & 31;
+  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
   const unsigned lt_mask = (1u << lane) - 1u;
+  const int seg = (V + nw - 1) / nw;
+  const int lo = min(V, warp * seg), hi = min(V, lo + seg);
+  __shared__ int skip[4];  // per pass, so no flag is reset while another thread may still read it
+  if (tid < 4) skip[tid] = 0;
+  __syncthreads();
   uint32_t *ki = kA, *vi = vA, *ko = kB, *vo = vB;
   for (int pass = 0; pass < 4; ++pass) {
     const int sh = 8 * pass;
-    for (int d = tid; d < 256; d += nt) hist[d] = 0;
-    __syncthreads();
-    for (int i = tid; i < V; i += nt) atomicAdd(&hist[(ki[i] >> sh) & 255], 1);
-    __syncthreads();
-    if (tid == 0) {
-      int run = 0;
-      for (int d = 0; d < 256; ++d) { base[d] = run; run += hist[d]; }
+    for (int d = lane; d < 256; d += 32) wcnt[warp][d] = 0;
+    __syncwarp();
+    // ---- counts per (warp, digit)
+#pragma unroll 4
+    for (int g = lo; g < hi; g += 32) {
+      const int i = g + lane;
+      const bool valid = i < hi;
+      const int dg = valid ? (int)((ki[i] >> sh) & 255u) : 256;
+      const unsigned same = __match_any_sync(FULL, dg);
+      if (valid && (same & lt_mask) == 0) wcnt[warp][dg] += __popc(same);
+      __syncwarp();
     }
     __syncthreads();
-    for (int t0 = 0; t0 < V; t0 += nt) {
-      for (int d = tid; d < (nt / 32) * 256; d += nt) (&wcnt[0][0])[d] = 0;
-      __syncthreads();
-      const int i = t0 + tid;
-      const bool valid = i < V;
-      uint32_t key = valid ? ki[i] : 0u, val = valid ? vi[i] : 0u;
-      int dg = valid ? (int)((key >> sh) & 255) : 256;
-      unsigned same = __match_any_sync(FULL, dg);
-      int rank = __popc(same & lt_mask);
-      if (valid && rank == 0) wcnt[warp][dg] = __popc(same);
-      __syncthreads();
-      // exclusive prefix over warps, per digit; then tile totals into base
-      if (tid < 256) {
-        int run = 0;
-        for (int w = 0; w < nt / 32; ++w) { int c = wcnt[w][tid]; wcnt[w][tid] = run; run += c; }
-        hist[tid] = run;  // tile total for digit tid
+    // ---- offsets: digit-major, then warp
+    if (tid < 256) {
+      int run = 0;
+      for (int w = 0; w < nw; ++w) { const int c = wcnt[w][tid]; wcnt[w][tid] = run; run += c; }
+      hist[tid] = run;
+      if (run == V) skip[pass] = 1;  // every key has this digit: the pass is the identity
+    }
+    __syncthreads();
+    if (skip[pass]) continue;  // uniform across the block (read after the barrier)
+    if (tid < 32) {      // exclusive scan of the 256 digit totals by one warp
+      int v[8], t = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { v[j] = hist[tid * 8 + j]; t += v[j]; }
+      int incl = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(FULL, incl, o);
+        if (tid >= o) incl += n;
       }
-      __syncthreads();
+      int run = incl - t;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { base[tid * 8 + j] = run; run += v[j]; }
+    }
+    __syncthreads();
+    // ---- scatter, segment order kept within each digit
+#pragma unroll 4
+    for (int g = lo; g < hi; g += 32) {
+      const int i = g + lane;
+      const bool valid = i < hi;
+      const uint32_t key = valid ? ki[i] : 0u, val = valid ? vi[i] : 0u;
+      const int dg = valid ? (int)((key >> sh) & 255u) : 256;
+      const unsigned same = __match_any_sync(FULL, dg);
       if (valid) {
-        int dst = base[dg] + wcnt[warp][dg] + rank;
+        const int dst = base[dg] + wcnt[warp][dg] + __popc(same & lt_mask);
         ko[dst] = key;
         vo[dst] = val;
       }
-      __syncthreads();
-      if (tid < 256) base[tid] += hist[tid];
-      __syncthreads();
+      __syncwarp();
+      if (valid && (same & lt_mask) == 0) wcnt[warp][dg] += __popc(same);
+      __syncwarp();
     }
+    __syncthreads();
     uint32_t *t;
     t = ki; ki = ko; ko = t;
     t = vi; vi = vo; vo = t;
+  }
+  if (ki != kA) {  // an odd number of passes moved data: bring the result back to (kA, vA)
+    for (int i = tid; i < V; i += nt) { kA[i] = ki[i]; vA[i] = vi[i]; }
+    __syncthreads();
   }
 }
 
