@@ -1769,19 +1769,30 @@ k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_s
   };
 #pragma unroll
   for (int j = 0; j < SHA_STAGES - 1; ++j) issue();
+  // The first two quads of block j+1 are read during block j, so a block's
+  // first rounds never wait for a shared-memory load; the wait below
+  // therefore keeps one block fewer in flight (blocks up to j+1 landed).
   int slot = 0;
+  cp_async_wait<SHA_STAGES - 2>();
+  uint4 qa = stg[lane], qb = stg[32 + lane];
   for (int j = 0; j < nb; ++j) {
     issue();
-    cp_async_wait<SHA_STAGES - 1>();
+    cp_async_wait<SHA_STAGES - 2>();
     const uint4 *blk = stg + (size_t)slot * 16 * 32 + lane;
+    const int nslot = slot == SHA_STAGES - 1 ? 0 : slot + 1;
     uint32_t w[64];
+    w[0] = qa.x; w[1] = qa.y; w[2] = qa.z; w[3] = qa.w;
+    w[4] = qb.x; w[5] = qb.y; w[6] = qb.z; w[7] = qb.w;
 #pragma unroll
-    for (int qd = 0; qd < 16; ++qd) {
+    for (int qd = 2; qd < 16; ++qd) {
       uint4 v = blk[qd * 32];
       w[4 * qd] = v.x; w[4 * qd + 1] = v.y; w[4 * qd + 2] = v.z; w[4 * qd + 3] = v.w;
     }
+    const uint4 *nblk = stg + (size_t)nslot * 16 * 32 + lane;  // next block (stale past the last: unused)
+    qa = nblk[0];
+    qb = nblk[32];
     sha_compress_wk_m(h, w, one);
-    slot = slot == SHA_STAGES - 1 ? 0 : slot + 1;
+    slot = nslot;
   }
   cp_async_wait<0>();
   // New carry = stream bytes [64*nb, total).
