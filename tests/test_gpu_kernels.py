@@ -83,7 +83,8 @@ def test_pinned_math_bit_exact(fn, pkg, oracle):
 
 
 SHAPES = [(1, 576, 576), (3, 192, 576), (4, 100, 96), (7, 1536, 576), (16, 64, 1536), (33, 200, 40),
-          (64, 576, 1536), (64, 960, 576), (5, 4099, 64), (128, 1024, 3072), (65, 300, 8), (2, 49152, 576)]
+          (64, 576, 1536), (64, 960, 576), (5, 4099, 64), (128, 1024, 3072), (65, 300, 8), (2, 49152, 576),
+          (2048, 2560, 96), (1970, 2500, 40)]  # the last two take the 128 x 128 prompt-pass tile
 
 
 @pytest.mark.parametrize("form", ["sequential", "tree", "decode"])
@@ -99,6 +100,11 @@ def test_matmul_bit_exact(rows, n, k, form, pkg, oracle):
     X = rng.standard_normal((rows, k)).astype(np.float32)
     X[:, ::7] = 0.0  # signed zeros and cancellations in the chains
     X[:, 1::11] *= -0.0
+    if form == "decode" and rows > 1024:  # the few-row form refuses large row counts
+        with pytest.raises(pkg.Cis2Error) as e:
+            pkg.matmul(W, X, decode=True)
+        assert e.value.code == 1
+        return
     got = pkg.matmul(W, X, tree=tree, decode=form == "decode")
     want = oracle.matmul_bf16(W, X, tree=tree)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
