@@ -542,7 +542,7 @@ int gemm_tile_choice(int M, int N, int K, bool tree) {
 // order.  Products are rounded singly and added as pairs of independent
 // accumulators with add.rn.ftz.f32x2, which halves the issue slots the adds
 // take.  Operands arrive through a BIG_STAGES-deep cp.async ring.
-constexpr int BIG_BM = 128, BIG_BN = 128, BIG_KT = 16, BIG_STAGES = 4, BIG_THREADS = 256;
+constexpr int BIG_BN = 128, BIG_KT = 16, BIG_STAGES = 4, BIG_THREADS = 256;
 
 __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   float2 r;
@@ -553,12 +553,17 @@ __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   return r;
 }
 
+// BIG_BM = 128 (8 rows per thread) or 64 (4 rows per thread, for products
+// with too few 128-row tiles to fill the GPU).
+template <int BIG_BM>
 __global__ void __launch_bounds__(BIG_THREADS, 2)
 k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp, int K, int N, int M,
            float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
            size_t y_slot_stride) {
   constexpr int XF = BIG_KT * BIG_BM;  // floats per X stage
   constexpr int WH = BIG_KT * BIG_BN;  // bf16 per W stage
+  constexpr int TMR = BIG_BM / 16;     // rows per thread: (i / 4) * 64 + ty * 4 + i % 4
+  constexpr int XCH = XF / 4;          // 16-byte X chunks per stage
   extern __shared__ __align__(16) float smem[];
   float *Xs = smem;                                                     // [S][KT][BM]
   uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + BIG_STAGES * XF);  // [S][KT][BN]
@@ -569,8 +574,8 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   auto issue = [&](int kt) {
     const int slot = kt % BIG_STAGES, k0 = kt * BIG_KT;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {  // X: KT rows of 128 floats = 512 chunks
-      const int c = tid + r * BIG_THREADS, k = c >> 5, q = c & 31;
+    for (int r = 0; r < XCH / BIG_THREADS; ++r) {  // X: KT rows of BM floats
+      const int c = tid + r * BIG_THREADS, k = c / (BIG_BM / 4), q = c % (BIG_BM / 4);
       const bool ok = (k0 + k < K) && (m0 + 4 * q < ldm);
       const float *src = ok ? XT + (size_t)(k0 + k) * ldm + m0 + 4 * q : XT;
       cp_async16_zfill(xs_b + (uint32_t)((slot * XF + k * BIG_BM + 4 * q) * 4), src, ok);
@@ -582,9 +587,9 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
       cp_async16_zfill(ws_b + (uint32_t)((slot * WH + k * BIG_BN + pnl * 8) * 2), src, ok);
     }
   };
-  float2 acc[8][4];
+  float2 acc[TMR][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < TMR; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
   const int nk = (K + BIG_KT - 1) / BIG_KT;
@@ -603,17 +608,20 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
     const uint16_t *ws = Ws + slot * WH + tx * 4;
 #pragma unroll
     for (int k = 0; k < BIG_KT; ++k) {
-      const float4 xa = *reinterpret_cast<const float4 *>(xs + k * BIG_BM);
-      const float4 xb = *reinterpret_cast<const float4 *>(xs + k * BIG_BM + 64);
+      float x[TMR];
+#pragma unroll
+      for (int g = 0; g < TMR / 4; ++g) {
+        const float4 xv = *reinterpret_cast<const float4 *>(xs + k * BIG_BM + g * 64);
+        x[4 * g] = xv.x; x[4 * g + 1] = xv.y; x[4 * g + 2] = xv.z; x[4 * g + 3] = xv.w;
+      }
       const uint2 wa = *reinterpret_cast<const uint2 *>(ws + k * BIG_BN);
       const uint2 wb = *reinterpret_cast<const uint2 *>(ws + k * BIG_BN + 64);
-      const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
       const float w[8] = {__uint_as_float(wa.x << 16), __uint_as_float(wa.x & 0xffff0000u),
                           __uint_as_float(wa.y << 16), __uint_as_float(wa.y & 0xffff0000u),
                           __uint_as_float(wb.x << 16), __uint_as_float(wb.x & 0xffff0000u),
                           __uint_as_float(wb.y << 16), __uint_as_float(wb.y & 0xffff0000u)};
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < TMR; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           acc[i][j] = fadd_pair(acc[i][j], fmul(w[2 * j], x[i]), fmul(w[2 * j + 1], x[i]));
@@ -622,8 +630,8 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   cp_async_wait<0>();
   float *Yb = Y + (y_slot ? (size_t)(*y_slot) * y_slot_stride : 0);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+  for (int i = 0; i < TMR; ++i) {
+    const int m = m0 + (i / 4) * 64 + ty * 4 + (i % 4);
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -639,34 +647,47 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   }
 }
 
+template <int BIG_BM>
 static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s) {
   const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BIG_BM * 4 + BIG_KT * BIG_BN * 2);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_big, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_gemm_big<BIG_BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set = true;
   }
   dim3 grid((N + BIG_BN - 1) / BIG_BN, (M + BIG_BM - 1) / BIG_BM);
-  k_gemm_big<<<grid, BIG_THREADS, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride);
+  k_gemm_big<BIG_BM><<<grid, BIG_THREADS, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride);
 }
 
-// The large tile pays off once there are enough of its blocks to fill the
-// GPU twice over (two blocks fit per SM) and its row tiles are nearly full
-// (measured on B200: 0.70-0.81 of the FP32 pipe on 4,096- and 8,192-row
-// products against 0.62-0.64 for the 64 x 32 tile, slower below that).
-bool gemm_big_ok(int M, int N) {
-  const long mt = (M + BIG_BM - 1) / BIG_BM;
-  return mt * ((N + BIG_BN - 1) / BIG_BN) >= 2 * 148 && (long)M * 10 >= mt * BIG_BM * 9;
+// A tile height pays off once there are enough of its blocks to fill the
+// GPU twice over (two blocks fit per SM) and its row tiles are nearly full.
+// Measured on B200:
+// - the 128-row tile reaches 0.70-0.81 of the FP32 pipe on the 3,072- and
+//   6,144-wide products of 4,096 and 8,192 rows, against 0.62-0.64 for the
+//   64 x 32 tile of k_gemm_t;
+// - the 64-row tile wins only on vocabulary-wide products (0.66 vs 0.59 on
+//   300 x 32,000);
+// - both lose on the narrow (576-960 wide) projections.
+// Returns the row tile, 0 for k_gemm_t.
+int gemm_big_rows(int M, int N) {
+  const long nt = (N + BIG_BN - 1) / BIG_BN;
+  for (int bm : {128, 64}) {
+    if (bm == 64 && N < 16384) continue;
+    const long mt = (M + bm - 1) / bm;
+    if (mt * nt >= 2 * 148 && (long)M * 10 >= mt * bm * 9) return bm;
+  }
+  return 0;
 }
 
 void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                  const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
-  if (!tree && gemm_big_ok(M, N)) {
-    run_gemm_big(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s);
-    return;
+  if (!tree) {
+    const int bm = gemm_big_rows(M, N);
+    if (bm == 128) { run_gemm_big<128>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s); return; }
+    if (bm == 64) { run_gemm_big<64>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s); return; }
   }
 #define CIS2B_GEMM(BM_, BP_, TM_, TN_)                                                           \
   do {                                                                                           \
