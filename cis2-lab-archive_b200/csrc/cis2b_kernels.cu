@@ -1867,29 +1867,37 @@ __global__ void k_sha_prep(const ShaState *st, int n_seq, const float *logits, i
 // The chain: one thread per sequence compresses the step's blocks in order,
 // keeps the tail as the new carry and emits the per-step digest (a
 // finalised copy of the running state).  The expanded W+K words stream
-// into shared memory through an SHA_STAGES-deep cp.async pipeline, so the
+// into shared memory through an ST-deep cp.async pipeline, so the
 // compression never waits on L2/HBM latency; each lane copies and reads
 // only its own slots, so no warp-level synchronisation is involved.
 //
-// The chain is issue-bound (~14 integer instructions per round, one warp),
-// so a chain warp must not share its scheduler with forward-pass warps: a
-// CTA holds up to 4 chain warps (one per SM sub-partition) and asks for the
-// whole shared memory of the SM, which keeps every other kernel's CTAs off
-// that SM while the witness runs.
+// The chain is issue-bound (11 integer-pipe instructions and 5 multiply-adds
+// per round, one warp), so a chain warp must not share its scheduler with
+// forward-pass warps: a CTA asks for the whole shared memory of the SM,
+// which keeps every other kernel's CTAs off that SM while the witness runs.
+// With up to SHA_SOLO_WARPS chain warps, each gets an SM of its own and a
+// SHA_SOLO_STAGES-deep ring: measured on B200, two chain warps on one SM
+// slow down by a quarter while a vocabulary-wide decode GEMM loads L2 from
+// the other SMs, and one warp per SM does not.  Beyond that, SHA_WARPS warps
+// (one per SM sub-partition) share an SM with SHA_STAGES stages each.
 constexpr int SHA_WARPS = 4;
 constexpr int SHA_STAGES = 7;
+constexpr int SHA_SOLO_WARPS = 4;
+constexpr int SHA_SOLO_STAGES = 28;
 constexpr size_t SHA_STAGE_BYTES = (size_t)16 * 32 * sizeof(uint4);          // one block, 32 chains
 constexpr size_t SHA_SMEM = (size_t)227 * 1024;                              // SM's maximum per CTA
 static_assert(SHA_WARPS * SHA_STAGES * SHA_STAGE_BYTES <= SHA_SMEM, "witness pipeline exceeds smem");
+static_assert(SHA_SOLO_STAGES * SHA_STAGE_BYTES <= SHA_SMEM, "witness pipeline exceeds smem");
 
 
+template <int ST>
 __global__ void __launch_bounds__(32 * SHA_WARPS, 1)
 k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                const uint32_t *next_ids, const uint32_t *wk, uint8_t *digest_out, size_t digest_stride,
                uint32_t one) {
-  extern __shared__ uint4 smem_all[];  // [warp][SHA_STAGES][16][32 lanes]
+  extern __shared__ uint4 smem_all[];  // [warp][ST][16][32 lanes]
   const int lane = threadIdx.x & 31;
-  uint4 *stg = smem_all + (size_t)(threadIdx.x >> 5) * SHA_STAGES * 16 * 32;
+  uint4 *stg = smem_all + (size_t)(threadIdx.x >> 5) * ST * 16 * 32;
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= n_seq) return;
   ShaState S = st[s];
@@ -1916,21 +1924,21 @@ k_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_s
     cp_async_commit();  // empty groups keep the per-thread group count uniform
     next_src += bstride;
     ++next_j;
-    issue_slot = issue_slot == SHA_STAGES - 1 ? 0 : issue_slot + 1;
+    issue_slot = issue_slot == ST - 1 ? 0 : issue_slot + 1;
   };
 #pragma unroll
-  for (int j = 0; j < SHA_STAGES - 1; ++j) issue();
+  for (int j = 0; j < ST - 1; ++j) issue();
   // The first two quads of block j+1 are read during block j, so a block's
   // first rounds never wait for a shared-memory load; the wait below
   // therefore keeps one block fewer in flight (blocks up to j+1 landed).
   int slot = 0;
-  cp_async_wait<SHA_STAGES - 2>();
+  cp_async_wait<ST - 2>();
   uint4 qa = stg[lane], qb = stg[32 + lane];
   for (int j = 0; j < nb; ++j) {
     issue();
-    cp_async_wait<SHA_STAGES - 2>();
+    cp_async_wait<ST - 2>();
     const uint4 *blk = stg + (size_t)slot * 16 * 32 + lane;
-    const int nslot = slot == SHA_STAGES - 1 ? 0 : slot + 1;
+    const int nslot = slot == ST - 1 ? 0 : slot + 1;
     uint32_t w[64];
     w[0] = qa.x; w[1] = qa.y; w[2] = qa.z; w[3] = qa.w;
     w[4] = qb.x; w[5] = qb.y; w[6] = qb.z; w[7] = qb.w;
@@ -1979,14 +1987,20 @@ void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, si
   if (n_seq <= 0) return;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_sha_compress, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SHA_SMEM);
+    cudaFuncSetAttribute(k_sha_compress<SHA_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SHA_SMEM);
+    cudaFuncSetAttribute(k_sha_compress<SHA_SOLO_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)SHA_SMEM);
     attr = true;
   }
   const int warps = (n_seq + 31) / 32;
-  const int per_cta = warps < SHA_WARPS ? warps : SHA_WARPS;
-  const int ctas = (warps + per_cta - 1) / per_cta;
-  k_sha_compress<<<ctas, 32 * per_cta, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
-                                                      wk_scratch, step_digest_out, digest_stride, 1u);
+  if (warps <= SHA_SOLO_WARPS) {
+    k_sha_compress<SHA_SOLO_STAGES><<<warps, 32, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
+                                                                 wk_scratch, step_digest_out, digest_stride, 1u);
+    return;
+  }
+  const int ctas = (warps + SHA_WARPS - 1) / SHA_WARPS;
+  k_sha_compress<SHA_STAGES><<<ctas, 32 * SHA_WARPS, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
+                                                                    wk_scratch, step_digest_out, digest_stride, 1u);
 }
 void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                      const uint32_t *next_ids, uint32_t *wk_scratch, uint8_t *step_digest_out,
