@@ -1306,12 +1306,14 @@ void launch_argmax(const float *logits, int V, int rows, const int32_t *slot, si
 
 // ---- E23 pinned sampler (e23 patch, src/sampling.rs hunk :650-725) ----
 //
-// One CTA per row.  Element-wise steps run on all threads; the four
-// order-pinned folds (softmax denominator, nucleus cumulative sum,
-// renormalisation total, CDF walk) run in thread 0 over chunks that the
-// other threads stage into shared memory.  The (probability desc, index asc)
-// order is a stable LSD radix sort of key = ~bits(p) (p >= +0, so bit order
-// is value order) over ascending indices.
+// One CTA per row.  Element-wise steps run on all threads; the
+// order-pinned folds (softmax denominator, nucleus cumulative sum, CDF walk)
+// run in thread 0 over chunks that the other threads stage into shared
+// memory.  The renormalisation total is not folded again: it is the sum of
+// the nucleus in sorted order, the very sequence of additions the nucleus
+// walk made, so it equals the nucleus walk's final sum bit for bit.  The
+// (probability desc, index asc) order is a stable LSD radix sort of key =
+// ~bits(p) (p >= +0, so bit order is value order) over ascending indices.
 constexpr int SAMPLE_THREADS = 1024;
 constexpr int FOLD_CHUNK = 1024;
 
@@ -1322,48 +1324,74 @@ __device__ __forceinline__ uint64_t sm64_round(uint64_t x) {
   return z ^ (z >> 31);
 }
 
-// Serial fold driver: thread 0 calls op(i, value) for i = 0..n-1 in order,
-// op returns true to stop early.  The other threads stage the next chunk
-// (computing load(i) in parallel), thread 0 reads its chunk 32 values at a
-// time with 16-byte loads, so its chain waits on adds, not on shared-memory
-// latency.  buf: 2 * FOLD_CHUNK floats, 16-byte aligned.
-template <class Load, class Op>
-__device__ void serial_fold(int n, Load load, Op op, float *buf, int *stop_flag) {
+// Pinned running sum: thread 0 forms acc_i = ((0 + v_0) + v_1) + ... + v_i
+// for i = 0..n-1 in order, v_i = load(i), and stops at the first i with
+// stop(acc_i).  The other threads compute load() for the next chunk and
+// stage it in shared memory while thread 0 folds the current one.  Thread 0
+// reads 8 values at a time with 16-byte loads, one batch ahead, and tests
+// stop() once per 8 additions without a branch, so its chain waits only on
+// the additions;
+// stop must therefore be monotone along the walk, which holds for a running
+// sum of non-negative values and a threshold test.  When a 64-value stretch
+// has crossed, the stretch is walked again one value at a time from its
+// saved start to find the exact index (the same additions, so the same
+// values).  Result, after the final barrier: sh_i[1] = the stop index (n if
+// none), sh_f[0] = acc at that index (the full sum if none).
+// buf: 2 * FOLD_CHUNK floats, 16-byte aligned; sh_i[0] is the stop flag.
+template <class Load, class Stop>
+__device__ void fold_until(int n, Load load, Stop stop, float *buf, int *sh_i, float *sh_f) {
   const int tid = threadIdx.x;
-  if (tid == 0) *stop_flag = 0;
+  if (tid == 0) sh_i[0] = 0;
   for (int i = tid; i < FOLD_CHUNK && i < n; i += blockDim.x) buf[i] = load(i);
   __syncthreads();
+  float acc = 0.0f;
+  int at = n;
   const int nch = (n + FOLD_CHUNK - 1) / FOLD_CHUNK;
   for (int c = 0; c < nch; ++c) {
     float *cur = buf + (c & 1) * FOLD_CHUNK;
     float *nxt = buf + ((c + 1) & 1) * FOLD_CHUNK;
     const int base = c * FOLD_CHUNK, cnt = min(FOLD_CHUNK, n - base);
     if (tid == 0) {
-      if (!*stop_flag) {
-        bool stop = false;
-        int i = 0;
-        for (; i + 32 <= cnt && !stop; i += 32) {
-          float v[32];
+      int i = 0;
+      const float4 *q4 = reinterpret_cast<const float4 *>(cur);
+      float4 na, nb;  // the next 8 values, loaded one batch ahead
+      if (cnt >= 64) { na = q4[0]; nb = q4[1]; }
+      for (; i + 64 <= cnt; i += 64) {
+        const float a0 = acc;
+        bool crossed = false;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float4 q = reinterpret_cast<const float4 *>(cur + i)[u];
-            v[4 * u] = q.x; v[4 * u + 1] = q.y; v[4 * u + 2] = q.z; v[4 * u + 3] = q.w;
-          }
-#pragma unroll
-          for (int u = 0; u < 32; ++u)
-            if (op(base + i + u, v[u])) { stop = true; break; }
+        for (int h = 0; h < 8; ++h) {
+          const float4 a = na, b = nb;
+          const int nx = (i + 8 * h + 8) >> 2;  // float4 index of the next batch
+          if (h < 7 || i + 128 <= cnt) { na = q4[nx]; nb = q4[nx + 1]; }
+          acc = fadd(acc, a.x); acc = fadd(acc, a.y); acc = fadd(acc, a.z); acc = fadd(acc, a.w);
+          acc = fadd(acc, b.x); acc = fadd(acc, b.y); acc = fadd(acc, b.z); acc = fadd(acc, b.w);
+          crossed |= stop(acc);
         }
-        for (; i < cnt && !stop; ++i)
-          if (op(base + i, cur[i])) stop = true;
-        if (stop) *stop_flag = 1;
+        if (crossed) {
+          acc = a0;
+          for (int u = 0; u < 64; ++u) {
+            acc = fadd(acc, cur[i + u]);
+            if (stop(acc)) { at = base + i + u; break; }
+          }
+          break;
+        }
       }
+      if (at == n)
+        for (; i < cnt; ++i) {
+          acc = fadd(acc, cur[i]);
+          if (stop(acc)) { at = base + i; break; }
+        }
+      if (at != n) sh_i[0] = 1;
     } else if (c + 1 < nch) {
       const int nb = base + FOLD_CHUNK, ncnt = min(FOLD_CHUNK, n - nb);
       for (int i = tid - 1; i < ncnt; i += blockDim.x - 1) nxt[i] = load(nb + i);
     }
     __syncthreads();
-    if (*stop_flag) break;
+    if (sh_i[0]) break;
   }
+  if (tid == 0) { sh_i[1] = at; sh_f[0] = acc; }
+  __syncthreads();
 }
 
 // Stable LSD radix sort of (key, value) pairs by key ascending, 4 passes of
@@ -1496,11 +1524,7 @@ k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, fl
   for (int i = tid; i < V; i += nt) p[i] = exp_pinned(fsub(p[i], mx));
   __syncthreads();
   // Step 2b: denominator, strict left-to-right over index order.
-  float den_acc = 0.0f;
-  serial_fold(V, [&](int i) { return p[i]; },
-              [&](int, float v) { den_acc = fadd(den_acc, v); return false; }, buf, &shared_i[0]);
-  if (tid == 0) shared_f[1] = den_acc;
-  __syncthreads();
+  fold_until(V, [&](int i) { return p[i]; }, [](float) { return false; }, buf, shared_i, &shared_f[1]);
   const float den = shared_f[1];
   for (int i = tid; i < V; i += nt) {
     float pv = fdiv(p[i], den);
@@ -1513,39 +1537,19 @@ k_sample(const float *logits, int V, const int32_t *slot, size_t slot_stride, fl
   block_radix_sort(kA, vA, kB, vB, V, hist, base, wcnt);
   uint32_t *ki = kA, *vi = vA;
   // After 4 passes the sorted keys/indices are back in (kA, vA).
-  // Step 4: nucleus = shortest prefix with cumulative sum >= top_p.
-  float cum = 0.0f;
-  int nuc = V;
-  serial_fold(V, [&](int i) { return __uint_as_float(~ki[i]); },
-              [&](int i, float v) {
-                cum = fadd(cum, v);
-                if (cum >= top_p) { nuc = i + 1; return true; }
-                return false;
-              },
-              buf, &shared_i[0]);
-  if (tid == 0) shared_i[1] = nuc;
-  __syncthreads();
-  nuc = shared_i[1];
-  // Step 5: renormalisation total over the nucleus.
-  float total = 0.0f;
-  serial_fold(nuc, [&](int i) { return __uint_as_float(~ki[i]); },
-              [&](int, float v) { total = fadd(total, v); return false; }, buf, &shared_i[0]);
-  if (tid == 0) shared_f[2] = total;
-  __syncthreads();
-  total = shared_f[2];
+  // Step 4: nucleus = shortest prefix with cumulative sum >= top_p.  Step 5's
+  // total (the nucleus summed again in the same order) is that prefix's sum.
+  fold_until(V, [&](int i) { return __uint_as_float(~ki[i]); }, [&](float c) { return c >= top_p; }, buf,
+             shared_i, &shared_f[2]);
+  const int nuc = shared_i[1] < V ? shared_i[1] + 1 : V;
+  const float total = shared_f[2];
   // Step 6: draw u = (word >> 11) * 2^-53, walk the CDF.
   const uint64_t pos64 = (uint64_t)(int64_t)position[r];
   const uint64_t word = sm64_round(seed ^ sm64_round(pos64));
   const double u = __dmul_rn((double)(word >> 11), 1.0 / 9007199254740992.0);
-  float cdf = 0.0f;
-  int pick = nuc - 1;
-  serial_fold(nuc, [&](int i) { return fdiv(__uint_as_float(~ki[i]), total); },
-              [&](int i, float v) {
-                cdf = fadd(cdf, v);
-                if ((double)cdf > u) { pick = i; return true; }
-                return false;
-              },
-              buf, &shared_i[0]);
+  fold_until(nuc, [&](int i) { return fdiv(__uint_as_float(~ki[i]), total); },
+             [&](float c) { return (double)c > u; }, buf, shared_i, &shared_f[3]);
+  const int pick = shared_i[1] < nuc ? shared_i[1] : nuc - 1;
   if (tid == 0) next[r] = vi[pick];
 }
 
@@ -1631,24 +1635,13 @@ k_sample_gumbel(const float *logits, int V, const int32_t *slot, size_t slot_str
     float *e = reinterpret_cast<float *>(kB);  // e_r by rank
     for (int q = tid; q < K; q += nt) e[q] = exp_pinned(fsub(sv[order[q]], m0));
     __syncthreads();
-    float den = 0.0f;
-    serial_fold(K, [&](int q) { return e[q]; }, [&](int, float v) { den = fadd(den, v); return false; }, buf,
-                &shared_i[0]);
-    if (tid == 0) shared_f[0] = den;
-    __syncthreads();
-    den = shared_f[0];
-    float c = 0.0f;
-    int cut = K;
-    serial_fold(K, [&](int q) { return fdiv(e[q], den); },
-                [&](int q, float pq) {
-                  if (q > 0 && !(c < top_p)) { cut = q; return true; }
-                  c = fadd(c, pq);
-                  return false;
-                },
-                buf, &shared_i[0]);
-    if (tid == 0) shared_i[1] = cut;
-    __syncthreads();
-    P = shared_i[1];
+    fold_until(K, [&](int q) { return e[q]; }, [](float) { return false; }, buf, shared_i, &shared_f[0]);
+    const float den = shared_f[0];
+    // Keep ranks up to and including the first whose cumulative sum is no
+    // longer below top_p.
+    fold_until(K, [&](int q) { return fdiv(e[q], den); }, [&](float c) { return !(c < top_p); }, buf,
+               shared_i, &shared_f[1]);
+    P = shared_i[1] < K ? shared_i[1] + 1 : K;
   }
   const uint32_t st = (uint32_t)*step;
   float best_z = 0.0f;
