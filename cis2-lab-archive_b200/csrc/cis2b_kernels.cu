@@ -1857,6 +1857,68 @@ __global__ void k_sha_prep(const ShaState *st, int n_seq, const float *logits, i
     out[qd * 32] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
 }
 
+// The same expansion for decode step t, without reading the chain state, so
+// that it can run while the chain still compresses step t - 1 (which
+// rewrites the state at its end).  The carry in front of step t's bytes is
+// fully determined: its length is (c0 + t * (4V + 4)) mod 64, c0 being the
+// carry length before step 0, and its bytes are the last ones of step t - 1's
+// stream (logits || id), since a carry is shorter than a step.  At t = 0 the
+// carry comes from the state, and c0 is recorded for the later steps.
+__device__ __forceinline__ uint32_t prev_stream_byte(const uint32_t *prev, int V, uint32_t prev_id, int b) {
+  const uint32_t d = (b >> 2) < V ? prev[b >> 2] : prev_id;
+  return (d >> (8 * (b & 3))) & 0xffu;
+}
+__global__ void k_sha_prep_at(const ShaState *st, uint32_t *c0, int t, int n_seq, const float *prev_logits,
+                              const uint32_t *prev_ids, const float *logits, int V, size_t row_stride,
+                              const uint32_t *next_ids, uint32_t *wk, int nb_max) {
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int s = (int)(idx % n_seq), j = (int)(idx / n_seq);
+  if (j >= nb_max) return;
+  int c;
+  if (t == 0) {
+    c = (int)st[s].carry_n;
+    if (j == 0) c0[s] = (uint32_t)c;
+  } else {
+    c = (int)(((uint64_t)c0[s] + (uint64_t)t * (4ull * (uint64_t)V + 4ull)) & 63ull);
+  }
+  const int total = c + 4 * V + 4;
+  if (j >= total / 64) return;
+  const uint32_t *data = reinterpret_cast<const uint32_t *>(logits + (size_t)s * row_stride);
+  const uint32_t id = next_ids[s];
+  uint32_t m[16];
+  if (64 * j >= c) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m[i] = step_word(nullptr, c, data, V, id, 64 * j + 4 * i);
+  } else {  // block 0 starts with the carry
+    uint8_t cb[64];
+    if (t == 0) {
+      for (int b = 0; b < c; ++b) cb[b] = st[s].carry[b];
+    } else {
+      const uint32_t *prev = reinterpret_cast<const uint32_t *>(prev_logits + (size_t)s * row_stride);
+      const uint32_t pid = prev_ids[s];
+      for (int b = 0; b < c; ++b) cb[b] = (uint8_t)prev_stream_byte(prev, V, pid, 4 * V + 4 - c + b);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m[i] = step_word(cb, c, data, V, id, 64 * j + 4 * i);
+  }
+  uint32_t w[64];
+  sha_expand_wk(m, w);
+  const int nw = (n_seq + 31) / 32;
+  uint4 *out = reinterpret_cast<uint4 *>(wk) + ((size_t)j * nw + s / 32) * 16 * 32 + (s & 31);
+#pragma unroll
+  for (int qd = 0; qd < 16; ++qd)
+    out[qd * 32] = make_uint4(w[4 * qd], w[4 * qd + 1], w[4 * qd + 2], w[4 * qd + 3]);
+}
+void launch_sha_prep_at(const ShaState *st, uint32_t *c0, int t, int n_seq, const float *prev_logits,
+                        const uint32_t *prev_ids, const float *logits, int V, size_t row_stride,
+                        const uint32_t *next_ids, uint32_t *wk_scratch, cudaStream_t s) {
+  if (n_seq <= 0) return;
+  const int nb_max = (int)((63 + 4 * (size_t)V + 4) / 64);
+  const size_t threads = (size_t)nb_max * n_seq;
+  k_sha_prep_at<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(st, c0, t, n_seq, prev_logits, prev_ids, logits,
+                                                                  V, row_stride, next_ids, wk_scratch, nb_max);
+}
+
 // The chain: one thread per sequence compresses the step's blocks in order,
 // keeps the tail as the new carry and emits the per-step digest (a
 // finalised copy of the running state).  The expanded W+K words stream

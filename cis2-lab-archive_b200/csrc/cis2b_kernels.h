@@ -105,6 +105,12 @@ void launch_sha_step(ShaState *st, int n_seq, const float *logits, int V, size_t
 // per-sequence compression chain.
 void launch_sha_prep(const ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                      const uint32_t *next_ids, uint32_t *wk_scratch, cudaStream_t s);
+// launch_sha_prep for decode step t that does not read the chain state, so
+// it may overlap the chain's step t - 1: prev_logits / prev_ids are step
+// t - 1's (unused at t = 0); c0[n_seq] is written at t = 0 and read after.
+void launch_sha_prep_at(const ShaState *st, uint32_t *c0, int t, int n_seq, const float *prev_logits,
+                        const uint32_t *prev_ids, const float *logits, int V, size_t row_stride,
+                        const uint32_t *next_ids, uint32_t *wk_scratch, cudaStream_t s);
 void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, size_t row_stride,
                          const uint32_t *next_ids, const uint32_t *wk_scratch, uint8_t *step_digest_out,
                          size_t digest_stride, cudaStream_t s);

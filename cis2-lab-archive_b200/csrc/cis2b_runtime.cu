@@ -108,16 +108,17 @@ struct cis2b_model {
   const uint16_t *lm_head_t = nullptr;
   bool dec_tiles = false;  // decode steps use launch_gemm_dec (sequential mode, K % 4 == 0)
   DevBuf inv_freq, cos_t, sin_t;
-  cudaStream_t s_main = nullptr, s_sha = nullptr;
+  cudaStream_t s_main = nullptr, s_sha = nullptr, s_prep = nullptr;
   // workspace
   DevBuf h, ln, qkv, att, gu, hid, hlast, lnlast, kc, vc, ring, scratch;
   int act_ldm = 0;  // column count of the k-major activation buffers
   DevBuf rows_seq, rows_pos, rows_tok, gsrc, gdst;
   DevBuf d_next, d_pos, d_spos, d_seq, d_ctl, d_tokens, d_ids_hist;
-  DevBuf sha_state, sha_wk, step_dig, d_witness, d_argmax;
+  DevBuf sha_state, sha_wk, sha_c0, step_dig, d_witness, d_argmax;
   DevBuf hdr_bytes, hdr_off, p_flat, p_off, p_len;
   std::vector<cudaEvent_t> ev_sha;
   cudaEvent_t ev_sel = nullptr, ev0 = nullptr, ev_pref = nullptr, ev_dec = nullptr, ev_end = nullptr;
+  cudaEvent_t ev_prep[2] = {nullptr, nullptr}, ev_comp[2] = {nullptr, nullptr};  // witness expansion halves
   cis2b_timing timing{};
   int64_t launches = 0, h2d = 0, d2h = 0;
   // per-launch event timing of selected kernel classes (cis2b_profile)
@@ -347,6 +348,7 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   int lo_pri = 0, hi_pri = 0;
   CU(cudaDeviceGetStreamPriorityRange(&lo_pri, &hi_pri));
   CU(cudaStreamCreateWithPriority(&m->s_sha, cudaStreamNonBlocking, hi_pri));
+  CU(cudaStreamCreateWithPriority(&m->s_prep, cudaStreamNonBlocking, hi_pri));
   if (m->arena.ensure(arena_bytes) != cudaSuccess)
     return fail(CIS2B_ERR_NOMEM, "device allocation of the weight arena failed");
   uint8_t *base = m->arena.as<uint8_t>();
@@ -482,6 +484,10 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   CU(cudaEventCreate(&m->ev_pref));
   CU(cudaEventCreate(&m->ev_dec));
   CU(cudaEventCreate(&m->ev_end));
+  for (int i = 0; i < 2; ++i) {
+    CU(cudaEventCreateWithFlags(&m->ev_prep[i], cudaEventDisableTiming));
+    CU(cudaEventCreateWithFlags(&m->ev_comp[i], cudaEventDisableTiming));
+  }
   return CIS2B_OK;
 }
 
@@ -698,7 +704,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
       m->d_ctl.ensure(64) || m->d_tokens.ensure(4 * (size_t)B * std::max(G, 1)) ||
       m->d_ids_hist.ensure(4 * (size_t)B * std::max(G, 1)) ||
       m->sha_state.ensure(sizeof(ShaState) * (size_t)B) ||
-      m->sha_wk.ensure(4 * sha_wk_words(m->V, B)) || m->step_dig.ensure(32 * (size_t)B * std::max(G, 1)) ||
+      m->sha_wk.ensure(2 * 4 * sha_wk_words(m->V, B)) || m->sha_c0.ensure(4 * (size_t)B) || m->step_dig.ensure(32 * (size_t)B * std::max(G, 1)) ||
       m->d_witness.ensure(32 * (size_t)B) || m->d_argmax.ensure(32 * (size_t)B) ||
       (sample && m->scratch.ensure(4 * (size_t)B * 5 * V)))
     return fail(CIS2B_ERR_NOMEM, "device allocation of decode buffers failed");
@@ -709,7 +715,8 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
       m->ev_sha.push_back(e);
     }
   }
-  cudaStream_t s = m->s_main, ss = m->s_sha;
+  cudaStream_t s = m->s_main, ss = m->s_sha, sp = m->s_prep;
+  const size_t wk_words = sha_wk_words(m->V, B);
   m->launches = 0;
   m->ev_used = 0;
   m->prof_events.clear();
@@ -817,6 +824,7 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
   launch_sha_absorb_bytes(m->sha_state.as<ShaState>(), m->hdr_bytes.as<uint8_t>(), m->hdr_off.as<uint32_t>(),
                           B, ss);
   m->launches++;
+  CU(cudaEventRecord(m->ev_comp[0], ss));  // step 0's expansion reads the carry the header left
 
   // ---- prefill: every prompt position of every sequence
   rc = prefill(m, rtok, rseq, rpos, osrc, odst, B, maxP);
@@ -895,19 +903,33 @@ int generate_impl(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pr
         if (rc) return rc;
       }
     }
+    // Witness of step t.  The W+K expansion runs on s_prep into one half of
+    // the double buffer and may overlap the chain's step t - 1; it needs this
+    // step's logits and the chain to be done with the half (step t - 2).
+    // Ring slot t - 1 is released once the chain has finished it and this
+    // expansion has read its tail (the carry in front of step t).
+    uint32_t *wk_t = m->sha_wk.as<uint32_t>() + (size_t)(t & 1) * wk_words;
+    const float *logits_t = ring_base + (size_t)(t % ring) * B * V;
     CU(cudaEventRecord(m->ev_sel, s));
-    CU(cudaStreamWaitEvent(ss, m->ev_sel, 0));
-    launch_sha_prep(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
-                    m->d_ids_hist.as<uint32_t>() + (size_t)t * B, m->sha_wk.as<uint32_t>(), ss);
+    CU(cudaStreamWaitEvent(sp, m->ev_sel, 0));
+    CU(cudaStreamWaitEvent(sp, m->ev_comp[t & 1], 0));
+    launch_sha_prep_at(m->sha_state.as<ShaState>(), m->sha_c0.as<uint32_t>(), t, B,
+                       t ? ring_base + (size_t)((t - 1) % ring) * B * V : nullptr,
+                       t ? m->d_ids_hist.as<uint32_t>() + (size_t)(t - 1) * B : nullptr, logits_t, m->V, V,
+                       m->d_ids_hist.as<uint32_t>() + (size_t)t * B, wk_t, sp);
+    CU(cudaEventRecord(m->ev_prep[t & 1], sp));
+    CU(cudaStreamWaitEvent(ss, m->ev_prep[t & 1], 0));
+    if (t > 0) CU(cudaEventRecord(m->ev_sha[(size_t)((t - 1) % ring)], ss));
     {
       ProfScope p(m, CIS2B_PROF_WITNESS, ss);
-      launch_sha_compress(m->sha_state.as<ShaState>(), B, ring_base + (size_t)(t % ring) * B * V, m->V, V,
-                          m->d_ids_hist.as<uint32_t>() + (size_t)t * B, m->sha_wk.as<uint32_t>(),
+      launch_sha_compress(m->sha_state.as<ShaState>(), B, logits_t, m->V, V,
+                          m->d_ids_hist.as<uint32_t>() + (size_t)t * B, wk_t,
                           m->step_dig.as<uint8_t>() + (size_t)t * 32, (size_t)G * 32, ss);
     }
     m->launches += 2;
-    CU(cudaEventRecord(m->ev_sha[(size_t)(t % ring)], ss));
+    CU(cudaEventRecord(m->ev_comp[t & 1], ss));
   }
+  if (G > 0) CU(cudaEventRecord(m->ev_sha[(size_t)((G - 1) % ring)], ss));
   CU_LAUNCHED();
   CU(cudaEventRecord(m->ev_dec, s));
   // Join the witness stream; the final digest and the argmax digest run on
@@ -1076,13 +1098,19 @@ void cis2b_free(cis2b_model *m) {
   cudaSetDevice(m->dev);
   if (m->s_main) cudaStreamSynchronize(m->s_main);
   if (m->s_sha) cudaStreamSynchronize(m->s_sha);
+  if (m->s_prep) cudaStreamSynchronize(m->s_prep);
   for (cudaEvent_t e : m->ev_sha) cudaEventDestroy(e);
+  for (int i = 0; i < 2; ++i) {
+    if (m->ev_prep[i]) cudaEventDestroy(m->ev_prep[i]);
+    if (m->ev_comp[i]) cudaEventDestroy(m->ev_comp[i]);
+  }
   for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
   cudaEvent_t evs[] = {m->ev_sel, m->ev0, m->ev_pref, m->ev_dec, m->ev_end};
   for (cudaEvent_t e : evs)
     if (e) cudaEventDestroy(e);
   if (m->s_main) cudaStreamDestroy(m->s_main);
   if (m->s_sha) cudaStreamDestroy(m->s_sha);
+  if (m->s_prep) cudaStreamDestroy(m->s_prep);
   delete m;
 }
 
