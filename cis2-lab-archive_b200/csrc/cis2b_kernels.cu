@@ -534,15 +534,15 @@ int gemm_tile_choice(int M, int N, int K, bool tree) {
   return best;
 }
 
-// ---- many rows (the prompt pass), sequential order: 128 x 128 block tile,
-// 8 x 8 outputs per thread.  Per k a thread reads its 8 activations as two
-// broadcast 16-byte loads and its 8 weights as two 8-byte loads (the
-// activation tile is [k][m], the weight tile [k][n], both conflict-free),
-// then does its 64 multiply-adds; each output still walks k = 0..K-1 in
-// order.  Products are rounded singly and added as pairs of independent
+// ---- many rows (the prompt pass, and lm_head over 64 rows or more),
+// sequential order: a block tile of up to 128 x 128 outputs over 256
+// threads, up to 8 x 8 per thread.  Per k a thread reads its activations as
+// broadcast 16-byte loads and its weights as 8-byte loads (the activation
+// tile is [k][m], the weight tile [k][n], both conflict-free), then does its
+// multiply-adds; each output still walks k = 0..K-1 in order.  Products are rounded singly and added as pairs of independent
 // accumulators with add.rn.ftz.f32x2, which halves the issue slots the adds
 // take.  Operands arrive through a BIG_STAGES-deep cp.async ring.
-constexpr int BIG_BN = 128, BIG_KT = 16, BIG_STAGES = 4, BIG_THREADS = 256;
+constexpr int BIG_KT = 16, BIG_STAGES = 4, BIG_THREADS = 256;
 
 __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   float2 r;
@@ -553,22 +553,26 @@ __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   return r;
 }
 
-// BIG_BM = 128 (8 rows per thread) or 64 (4 rows per thread, for products
-// with too few 128-row tiles to fill the GPU).
-template <int BIG_BM>
+// Block tile BIG_BM x BN: BIG_BM = 128 (8 rows per thread) or 64 (4 rows per
+// thread); BN = 128 (8 columns per thread: 4 at tx*4, 4 at 64 + tx*4) or 64
+// (4 columns per thread).  The dispatcher below uses the 64-wide forms.
+template <int BIG_BM, int BN>
 __global__ void __launch_bounds__(BIG_THREADS, 2)
 k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp, int K, int N, int M,
            float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
            size_t y_slot_stride) {
+  static_assert(BN == 128 || BN == 64, "column tile");
   constexpr int XF = BIG_KT * BIG_BM;  // floats per X stage
-  constexpr int WH = BIG_KT * BIG_BN;  // bf16 per W stage
+  constexpr int WH = BIG_KT * BN;      // bf16 per W stage
   constexpr int TMR = BIG_BM / 16;     // rows per thread: (i / 4) * 64 + ty * 4 + i % 4
+  constexpr int TNP = BN / 32;         // column pairs per thread
   constexpr int XCH = XF / 4;          // 16-byte X chunks per stage
+  constexpr int WCH = WH / 8;          // 16-byte W chunks per stage
   extern __shared__ __align__(16) float smem[];
   float *Xs = smem;                                                     // [S][KT][BM]
   uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + BIG_STAGES * XF);  // [S][KT][BN]
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int m0 = blockIdx.y * BIG_BM, n0 = blockIdx.x * BIG_BN, n8_0 = n0 / 8;
+  const int m0 = blockIdx.y * BIG_BM, n0 = blockIdx.x * BN, n8_0 = n0 / 8;
   const int N8 = (N + 7) / 8;
   const uint32_t xs_b = (uint32_t)__cvta_generic_to_shared(Xs), ws_b = (uint32_t)__cvta_generic_to_shared(Ws);
   auto issue = [&](int kt) {
@@ -580,18 +584,18 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
       const float *src = ok ? XT + (size_t)(k0 + k) * ldm + m0 + 4 * q : XT;
       cp_async16_zfill(xs_b + (uint32_t)((slot * XF + k * BIG_BM + 4 * q) * 4), src, ok);
     }
-    {  // W: KT x 16 panels of 8 bf16 = 256 chunks, to [k][n]
-      const int k = tid >> 4, pnl = tid & 15;
+    if (tid < WCH) {  // W: KT x BN/8 panels of 8 bf16, to [k][n]
+      const int k = tid / (BN / 8), pnl = tid % (BN / 8);
       const bool ok = (k0 + k < K) && (n8_0 + pnl < N8);
       const uint16_t *src = ok ? Wp + ((size_t)(n8_0 + pnl) * K + k0 + k) * 8 : Wp;
-      cp_async16_zfill(ws_b + (uint32_t)((slot * WH + k * BIG_BN + pnl * 8) * 2), src, ok);
+      cp_async16_zfill(ws_b + (uint32_t)((slot * WH + k * BN + pnl * 8) * 2), src, ok);
     }
   };
-  float2 acc[TMR][4];
+  float2 acc[TMR][TNP];
 #pragma unroll
   for (int i = 0; i < TMR; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
+    for (int j = 0; j < TNP; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
   const int nk = (K + BIG_KT - 1) / BIG_KT;
 #pragma unroll
   for (int st = 0; st < BIG_STAGES - 1; ++st) {
@@ -614,16 +618,19 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
         const float4 xv = *reinterpret_cast<const float4 *>(xs + k * BIG_BM + g * 64);
         x[4 * g] = xv.x; x[4 * g + 1] = xv.y; x[4 * g + 2] = xv.z; x[4 * g + 3] = xv.w;
       }
-      const uint2 wa = *reinterpret_cast<const uint2 *>(ws + k * BIG_BN);
-      const uint2 wb = *reinterpret_cast<const uint2 *>(ws + k * BIG_BN + 64);
-      const float w[8] = {__uint_as_float(wa.x << 16), __uint_as_float(wa.x & 0xffff0000u),
-                          __uint_as_float(wa.y << 16), __uint_as_float(wa.y & 0xffff0000u),
-                          __uint_as_float(wb.x << 16), __uint_as_float(wb.x & 0xffff0000u),
-                          __uint_as_float(wb.y << 16), __uint_as_float(wb.y & 0xffff0000u)};
+      float w[2 * TNP];
+#pragma unroll
+      for (int h = 0; h < TNP / 2; ++h) {
+        const uint2 wv = *reinterpret_cast<const uint2 *>(ws + k * BN + 64 * h);
+        w[4 * h] = __uint_as_float(wv.x << 16);
+        w[4 * h + 1] = __uint_as_float(wv.x & 0xffff0000u);
+        w[4 * h + 2] = __uint_as_float(wv.y << 16);
+        w[4 * h + 3] = __uint_as_float(wv.y & 0xffff0000u);
+      }
 #pragma unroll
       for (int i = 0; i < TMR; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < TNP; ++j)
           acc[i][j] = fadd_pair(acc[i][j], fmul(w[2 * j], x[i]), fmul(w[2 * j + 1], x[i]));
     }
   }
@@ -634,8 +641,8 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
     const int m = m0 + (i / 4) * 64 + ty * 4 + (i % 4);
     if (m >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + (j < 2 ? tx * 4 + 2 * j : 64 + tx * 4 + 2 * (j - 2));
+    for (int j = 0; j < TNP; ++j) {
+      const int n = n0 + 64 * (j / 2) + tx * 4 + 2 * (j % 2);
       float2 v = acc[i][j];
       if (R) {  // residual h + o (cis2_model.h:540-542)
         if (n < N) v.x = fadd(R[(size_t)m * ldr + n], v.x);
@@ -647,48 +654,52 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   }
 }
 
-template <int BIG_BM>
+template <int BIG_BM, int BN>
 static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s) {
-  const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BIG_BM * 4 + BIG_KT * BIG_BN * 2);
+  const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BIG_BM * 4 + BIG_KT * BN * 2);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_big<BIG_BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_gemm_big<BIG_BM, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set = true;
   }
-  dim3 grid((N + BIG_BN - 1) / BIG_BN, (M + BIG_BM - 1) / BIG_BM);
-  k_gemm_big<BIG_BM><<<grid, BIG_THREADS, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride);
+  dim3 grid((N + BN - 1) / BN, (M + BIG_BM - 1) / BIG_BM);
+  k_gemm_big<BIG_BM, BN><<<grid, BIG_THREADS, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot,
+                                                        y_slot_stride);
 }
 
-// A tile height pays off once there are enough of its blocks to fill the
-// GPU twice over (two blocks fit per SM) and its row tiles are nearly full.
-// Measured on B200:
-// - the 128-row tile reaches 0.70-0.81 of the FP32 pipe on the 3,072- and
-//   6,144-wide products of 4,096 and 8,192 rows, against 0.62-0.64 for the
-//   64 x 32 tile of k_gemm_t;
-// - the 64-row tile wins only on vocabulary-wide products (0.66 vs 0.59 on
-//   300 x 32,000);
-// - both lose on the narrow (576-960 wide) projections.
-// Returns the row tile, 0 for k_gemm_t.
+// Block tile choice for the sequential prompt-pass product, from 64 rows on.
+// Measured on B200, the 128 x 128, 128 x 64, 64 x 128 and 64 x 64 tiles run
+// their blocks at nearly the same rate per output (the 64-row ones about 5 %
+// slower), two blocks per SM, so the time is set by how many waves of
+// 2 x 148 blocks a tile needs: cost = waves x tile area / rate.  128 x 128
+// and 64 x 128 never beat the narrower tile of the same height by that
+// measure (at best they tie), so the choice is between:
+// - 128 x 64: e.g. the 576-wide projections of 4,096 rows (0.71-0.75 of the
+//   FP32 pipe, against 0.57-0.60 for k_gemm_t and 0.37 for 128 x 128), and
+//   the 2,304- to 6,144-wide ones (0.79, as fast as 128 x 128);
+// - 64 x 64: e.g. lm_head over 64 or 300 rows (0.63 and 0.71, against 0.55
+//   and 0.40 for the decode kernel).
+// Returns the tile height.
 int gemm_big_rows(int M, int N) {
-  const long nt = (N + BIG_BN - 1) / BIG_BN;
-  for (int bm : {128, 64}) {
-    if (bm == 64 && N < 16384) continue;
-    const long mt = (M + bm - 1) / bm;
-    if (mt * nt >= 2 * 148 && (long)M * 10 >= mt * bm * 9) return bm;
-  }
-  return 0;
+  const long w128 = ((long)((M + 127) / 128) * ((N + 63) / 64) + 2 * 148 - 1) / (2 * 148);
+  const long w64 = ((long)((M + 63) / 64) * ((N + 63) / 64) + 2 * 148 - 1) / (2 * 148);
+  return (double)w128 * 128 * 64 < (double)w64 * 64 * 64 / 0.95 ? 128 : 64;
 }
 
 void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                  const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
-  if (!tree) {
-    const int bm = gemm_big_rows(M, N);
-    if (bm == 128) { run_gemm_big<128>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s); return; }
-    if (bm == 64) { run_gemm_big<64>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s); return; }
+  if (!tree && M >= 64) {
+    if (gemm_big_rows(M, N) == 128)
+      run_gemm_big<128, 64>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s);
+    else
+      run_gemm_big<64, 64>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s);
+    return;
   }
+  // Fewer rows, or tree mode: SIMT register tiles (tree mode with the
+  // streaming 32-leaf tree per k tile).
 #define CIS2B_GEMM(BM_, BP_, TM_, TN_)                                                           \
   do {                                                                                           \
     if (tree)                                                                                    \

@@ -84,8 +84,8 @@ def test_pinned_math_bit_exact(fn, pkg, oracle):
 
 SHAPES = [(1, 576, 576), (3, 192, 576), (4, 100, 96), (7, 1536, 576), (16, 64, 1536), (33, 200, 40),
           (64, 576, 1536), (64, 960, 576), (5, 4099, 64), (128, 1024, 3072), (65, 300, 8), (2, 49152, 576),
-          (2048, 2560, 96), (1970, 2500, 40),   # the 128 x 128 prompt-pass tile
-          (300, 20000, 32)]                     # the 64 x 128 tile (vocabulary-wide)
+          (2048, 2560, 96), (1970, 2500, 40), (300, 20000, 32),   # the 64 x 64 prompt-pass tile
+          (4096, 576, 96), (700, 9000, 16)]                       # the 128 x 64 tile
 
 
 @pytest.mark.parametrize("form", ["sequential", "tree", "decode"])
