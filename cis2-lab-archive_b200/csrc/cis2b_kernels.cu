@@ -793,17 +793,23 @@ __device__ __forceinline__ float4 widen4(uint2 u) {
                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
 }
 
-template <int TM, int RW>
+// XS = false: the block's activation rows stay resident in shared memory
+// for the whole K (one copy up front).  XS = true: they stream through the
+// same ring as the weights, DEC_KC columns per stage, which keeps shared
+// memory small when ROWS x K is large (several blocks per SM instead of one).
+template <int TM, int RW, bool XS>
 __global__ void __launch_bounds__(32 * RW, 1)
 k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt, int K, int N, int M,
            float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
            size_t y_slot_stride, int glu) {
   constexpr int ROWS = TM * RW, NT = 32 * RW;
   constexpr int WST = DEC_KC * 32;  // bf16 per weight stage
+  constexpr int XST = ROWS * DEC_KC;  // floats per streamed activation stage
   constexpr int PF = 2;             // register prefetch distance in groups of four k
   extern __shared__ __align__(16) float smem[];
-  float *Xs = smem;                                                   // [ROWS][K]
-  uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + (size_t)ROWS * K);  // [STAGES][KC/4][32][4]
+  // XS: [STAGES][ROWS][KC] floats, then the weight ring; else [ROWS][K].
+  float *Xs = smem;
+  uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + (XS ? (size_t)DEC_STAGES * XST : (size_t)ROWS * K));
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int n32 = blockIdx.x, m0 = blockIdx.y * ROWS;
   const uint16_t *Wtile = Wt + (size_t)n32 * K * 32;
@@ -812,17 +818,29 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
   const int nc = (K + DEC_KC - 1) / DEC_KC;
   const int KQ = K / 4;
 
-  // The block's rows, whole K (rows past M are zero-filled), in group 0.
-  for (int i = tid; i < ROWS * KQ; i += NT) {
-    const int r = i / KQ, q = i - r * KQ;
-    const bool ok = m0 + r < M;
-    cp_async16_zfill(xs_b + (uint32_t)((r * K + 4 * q) * 4), ok ? X + (size_t)(m0 + r) * ldx + 4 * q : X, ok);
+  if (!XS) {
+    // The block's rows, whole K (rows past M are zero-filled), in group 0.
+    for (int i = tid; i < ROWS * KQ; i += NT) {
+      const int r = i / KQ, q = i - r * KQ;
+      const bool ok = m0 + r < M;
+      cp_async16_zfill(xs_b + (uint32_t)((r * K + 4 * q) * 4), ok ? X + (size_t)(m0 + r) * ldx + 4 * q : X, ok);
+    }
   }
   auto issue_w = [&](int c) {
     const int slot = c % DEC_STAGES, k0 = c * DEC_KC;
-    const int nchunk = min(DEC_KC, K - k0) * 4;  // 16-byte pieces: kn * 32 bf16 * 2 B / 16
+    const int kn = min(DEC_KC, K - k0);
+    const int nchunk = kn * 4;  // 16-byte pieces: kn * 32 bf16 * 2 B / 16
     for (int i = tid; i < nchunk; i += NT)
       cp_async16(ws_b + (uint32_t)(slot * WST * 2 + i * 16), Wtile + (size_t)k0 * 32 + (size_t)i * 8);
+    if (XS) {  // the rows' k0 .. k0 + kn columns, row stride DEC_KC in the stage
+      const int nq = kn / 4;
+      for (int i = tid; i < ROWS * nq; i += NT) {
+        const int r = i / nq, q = i - r * nq;
+        const bool ok = m0 + r < M;
+        cp_async16_zfill(xs_b + (uint32_t)((slot * XST + r * DEC_KC + 4 * q) * 4),
+                         ok ? X + (size_t)(m0 + r) * ldx + k0 + 4 * q : X, ok);
+      }
+    }
   };
 #pragma unroll
   for (int s = 0; s < DEC_STAGES - 1; ++s) {
@@ -833,14 +851,15 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
   float acc[TM];
 #pragma unroll
   for (int i = 0; i < TM; ++i) acc[i] = 0.0f;
-  const float *xw = Xs + (size_t)(w * TM) * K;
+  const int xstride = XS ? DEC_KC : K;  // row stride of the activations read below
   for (int c = 0; c < nc; ++c) {
     cp_async_wait<DEC_STAGES - 2>();
     __syncthreads();
     if (c + DEC_STAGES - 1 < nc) issue_w(c + DEC_STAGES - 1);
     cp_async_commit();
     const uint2 *wsl = reinterpret_cast<const uint2 *>(Ws + (c % DEC_STAGES) * WST) + lane;
-    const float *xc = xw + c * DEC_KC;
+    const float *xc = XS ? Xs + (size_t)(c % DEC_STAGES) * XST + (size_t)(w * TM) * DEC_KC
+                         : Xs + (size_t)(w * TM) * K + c * DEC_KC;
     const int kn = min(DEC_KC, K - c * DEC_KC);
     if (kn == DEC_KC) {
       constexpr int NQ = DEC_KC / 4;
@@ -848,7 +867,7 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
       auto ld = [&](int sl, int kq) {
         wb[sl] = widen4(wsl[kq * 32]);
 #pragma unroll
-        for (int i = 0; i < TM; ++i) xb[sl][i] = *reinterpret_cast<const float4 *>(xc + (size_t)i * K + 4 * kq);
+        for (int i = 0; i < TM; ++i) xb[sl][i] = *reinterpret_cast<const float4 *>(xc + (size_t)i * xstride + 4 * kq);
       };
 #pragma unroll
       for (int q = 0; q < PF; ++q) ld(q, q);
@@ -880,7 +899,7 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
         const float4 wv = widen4(wsl[kq * 32]);
 #pragma unroll
         for (int i = 0; i < TM; ++i) {
-          const float4 xv = *reinterpret_cast<const float4 *>(xc + (size_t)i * K + 4 * kq);
+          const float4 xv = *reinterpret_cast<const float4 *>(xc + (size_t)i * xstride + 4 * kq);
           acc[i] = fadd(acc[i], fmul(wv.x, xv.x));
           acc[i] = fadd(acc[i], fmul(wv.y, xv.y));
           acc[i] = fadd(acc[i], fmul(wv.z, xv.z));
@@ -916,19 +935,21 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
   }
 }
 
-template <int TM, int RW>
+template <int TM, int RW, bool XS>
 static void run_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, int M, float *Y, int ldy,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
                          cudaStream_t s) {
   constexpr int ROWS = TM * RW;
-  const size_t smem = (size_t)ROWS * K * 4 + (size_t)DEC_STAGES * DEC_KC * 32 * 2;
+  const size_t smem = (XS ? (size_t)DEC_STAGES * ROWS * DEC_KC * 4 : (size_t)ROWS * K * 4) +
+                      (size_t)DEC_STAGES * DEC_KC * 32 * 2;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_dec<TM, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_gemm_dec<TM, RW, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     attr_set = true;
   }
   dim3 grid((N + 31) / 32, (M + ROWS - 1) / ROWS);
-  k_gemm_dec<TM, RW><<<grid, 32 * RW, smem, s>>>(X, ldx, Wt, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride, glu);
+  k_gemm_dec<TM, RW, XS><<<grid, 32 * RW, smem, s>>>(X, ldx, Wt, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride,
+                                                      glu);
 }
 
 // Rows per block: the largest candidate that still gives at least two
@@ -936,15 +957,20 @@ static void run_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int
 struct DecCfg { int tm, rw; };
 static const DecCfg kDecTiles[] = {{8, 4}, {4, 4}, {2, 4}, {2, 2}};
 constexpr int kNumDecTiles = 4;
+// Resident activation rows above this many bytes stream instead.  Measured
+// on B200: 300 x 768 x 3,072 takes 102 us streamed against 143 us with
+// 16 x 3,072 rows resident (one block per SM), and 32 x 6,144 x 1,024 takes
+// 31.7 against 35.7 us; at 48 KB and below, resident rows are as fast or
+// faster (4 x 3,072 rows: 30.7 us resident, 34.9 streamed).
+constexpr size_t DEC_RESIDENT_MAX = 48 * 1024;
 
-bool gemm_dec_ok(int K) { return K > 0 && K % 4 == 0 && (size_t)4 * K * 4 + DEC_STAGES * DEC_KC * 64 <= 227 * 1024; }
+bool gemm_dec_ok(int K) { return K > 0 && K % 4 == 0; }
 
 int gemm_dec_choice(int M, int N, int K) {
   const long n32 = (N + 31) / 32;
   int pick = -1;
   for (int i = 0; i < kNumDecTiles; ++i) {
     const int rows = kDecTiles[i].tm * kDecTiles[i].rw;
-    if ((size_t)rows * K * 4 + (size_t)DEC_STAGES * DEC_KC * 64 > 227 * 1024) continue;
     // Eight rows per lane pay off only on very wide products (lm_head):
     // measured on B200, 4 x 4 is faster for the layer projections at 64 and 300 rows.
     if (kDecTiles[i].tm == 8 && N < 16384) continue;
@@ -958,12 +984,20 @@ void launch_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, 
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s,
                      int glu) {
   if (M <= 0 || N <= 0) return;
-  switch (gemm_dec_choice(M, N, K)) {
-    case 0: run_gemm_dec<8, 4>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
-    case 1: run_gemm_dec<4, 4>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
-    case 2: run_gemm_dec<2, 4>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
-    default: run_gemm_dec<2, 2>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); break;
+  const int pick = gemm_dec_choice(M, N, K);
+  const bool xs = (size_t)kDecTiles[pick].tm * kDecTiles[pick].rw * K * 4 > DEC_RESIDENT_MAX;
+#define CIS2B_DEC(TM_, RW_)                                                                                    \
+  do {                                                                                                         \
+    if (xs) run_gemm_dec<TM_, RW_, true>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); \
+    else run_gemm_dec<TM_, RW_, false>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s);   \
+  } while (0)
+  switch (pick) {
+    case 0: CIS2B_DEC(8, 4); break;
+    case 1: CIS2B_DEC(4, 4); break;
+    case 2: CIS2B_DEC(2, 4); break;
+    default: CIS2B_DEC(2, 2); break;
   }
+#undef CIS2B_DEC
 }
 
 // ============================================================ attention

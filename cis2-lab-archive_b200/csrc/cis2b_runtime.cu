@@ -1140,7 +1140,7 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
   if (rows <= 0 || n_out <= 0 || k <= 0 || k % 8) return fail(CIS2B_ERR_ARG, "bad shape (k must be a multiple of 8)");
   if (reduction < 0 || reduction > CIS2B_OP_MATMUL_DECODE) return fail(CIS2B_ERR_ARG, "bad reduction");
   if (reduction == CIS2B_OP_MATMUL_DECODE && (rows > 1024 || !gemm_dec_ok(k)))
-    return fail(CIS2B_ERR_ARG, "decode form: rows <= 1024 and k within shared memory");
+    return fail(CIS2B_ERR_ARG, "decode form: rows <= 1024 and k a multiple of 4");
   CU(cudaSetDevice(device));
   if (reduction == CIS2B_OP_MATMUL_DECODE) {
     Scoped<uint16_t> dw, dt;
