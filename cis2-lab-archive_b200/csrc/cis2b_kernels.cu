@@ -1201,10 +1201,10 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
     if (lane == 0) red[g] = is_nan(sg[0]) ? sg[0] : m;
   }
   __syncthreads();
-  for (int i = tid; i < G * len; i += nt) {
-    const int g = i / len, j = i - g * len;
-    float *p = sc + (size_t)g * scs + j;
-    *p = exp_pinned(fsub(*p, red[g]));
+  for (int g = 0; g < G; ++g) {
+    float *sg = sc + (size_t)g * scs;
+    const float mg = red[g];
+    for (int j = tid; j < len; j += nt) sg[j] = exp_pinned(fsub(sg[j], mg));
   }
   __syncthreads();
   // ---- denominators
@@ -1225,18 +1225,19 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * len; i += nt) {
-    const int g = i / len, j = i - g * len;
-    float *p = sc + (size_t)g * scs + j;
-    *p = fdiv(*p, red[32 + g]);
+  for (int g = 0; g < G; ++g) {
+    float *sg = sc + (size_t)g * scs;
+    const float den = red[32 + g];
+    for (int j = tid; j < len; j += nt) sg[j] = fdiv(sg[j], den);
   }
-  // ---- V-mix, V streamed through the two tile buffers.  A thread owns the
-  // four chains (g, d..d+3): one 16-byte load of V per position feeds four
-  // multiply-adds, and the weights come four positions per broadcast load.
-  const int hd4 = hd / 4;
-  const int g = tid / hd4, d = 4 * (tid - (tid / hd4) * hd4);
-  const bool owns = tid < G * hd4;
-  float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+  // ---- V-mix, V streamed through the two tile buffers.  Thread t owns the
+  // chain (g, d) = (t / hd, t % hd): the block's G*hd threads all work on
+  // every chunk, the lanes of a warp read consecutive d of one V row
+  // (conflict-free) and share the weights of one head (four positions per
+  // broadcast load).
+  const int g = tid / hd, d = tid - (tid / hd) * hd;
+  const bool owns = tid < G * hd;
+  float acc = 0.0f;
   for (int c = 0; c < nch; ++c) {
     if (c + 1 < nch) stage(vbase, c + 1, (c + 1) & 1);
     else cp_async_commit();
@@ -1249,37 +1250,18 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
       int jj = 0;
       for (; jj + 4 <= jc; jj += 4) {
         const float4 pw = *reinterpret_cast<const float4 *>(pg + jj);
-        float4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4 *>(tile + (jj + u) * ts);
-        const float pu[4] = {pw.x, pw.y, pw.z, pw.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          acc0 = fadd(acc0, fmul(pu[u], v[u].x));
-          acc1 = fadd(acc1, fmul(pu[u], v[u].y));
-          acc2 = fadd(acc2, fmul(pu[u], v[u].z));
-          acc3 = fadd(acc3, fmul(pu[u], v[u].w));
-        }
+        const float v0 = tile[jj * ts], v1 = tile[(jj + 1) * ts], v2 = tile[(jj + 2) * ts], v3 = tile[(jj + 3) * ts];
+        acc = fadd(acc, fmul(pw.x, v0));
+        acc = fadd(acc, fmul(pw.y, v1));
+        acc = fadd(acc, fmul(pw.z, v2));
+        acc = fadd(acc, fmul(pw.w, v3));
       }
-      for (; jj < jc; ++jj) {
-        const float pj = pg[jj];
-        const float4 v = *reinterpret_cast<const float4 *>(tile + jj * ts);
-        acc0 = fadd(acc0, fmul(pj, v.x));
-        acc1 = fadd(acc1, fmul(pj, v.y));
-        acc2 = fadd(acc2, fmul(pj, v.z));
-        acc3 = fadd(acc3, fmul(pj, v.w));
-      }
+      for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * ts]));
     }
     __syncthreads();
   }
   cp_async_wait<0>();
-  if (owns) {
-    float *o = att + (size_t)r * ars + ((size_t)kvh * G + g) * hd * acs + (size_t)d * acs;
-    o[0] = acc0;
-    o[acs] = acc1;
-    o[2 * (size_t)acs] = acc2;
-    o[3 * (size_t)acs] = acc3;
-  }
+  if (owns) att[(size_t)r * ars + ((size_t)kvh * G + g) * hd * acs + (size_t)d * acs] = acc;
 }
 
 void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
