@@ -156,7 +156,13 @@ int main(int argc, char **argv) {
   for (auto &p : prompts) maxp = p.size() > maxp ? p.size() : maxp;
   o.max_positions = (int32_t)(maxp + (size_t)gen > 4096 ? maxp + (size_t)gen : 4096);
   cis2b_model *m = nullptr;
-  if (cis2b_load(weights_dir.c_str(), &o, &m) != CIS2B_OK) {
+  const int lrc = cis2b_load(weights_dir.c_str(), &o, &m);
+  if (lrc == CIS2B_ERR_CONFIG) {  // the reference's refusal lines (code/cis2-fp/src/main.rs:818-822)
+    fprintf(stderr, "CIS2_REF_UNSUPPORTED reason=%s\n", cis2b_last_error());
+    fprintf(stderr, "This checkpoint is outside the CIS-2 specified subset; no digest emitted.\n");
+    return 2;
+  }
+  if (lrc != CIS2B_OK) {
     fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
     return 2;
   }

@@ -185,6 +185,72 @@ struct TensorRef {
 };
 
 // ------------------------------------------------------------------ loading
+
+// The architecture gate: the checkpoints whose arithmetic this decoder
+// reproduces, and a refusal by name for the rest (code/cis2-fp/src/main.rs:
+// 545-644, which refuses with CIS2_REF_UNSUPPORTED and exit status 2).  The
+// keys and reasons follow that gate; model_type "qwen3" is admitted as well,
+// because the lab's Qwen3 port of the C++ path decodes it
+// (labs/w1x-qwen3/scripts/qwen3-port.diff), and for it an explicit head_dim
+// is the one used (Qwen3-0.6B declares 128 against a derived 64).
+bool gate_architecture(const Json &cfg, std::string &why) {
+  auto present = [&](const char *k) {
+    const Json *j = cfg.get(k);
+    return j && j->kind != Json::NUL;
+  };
+  std::string mt;
+  if (const Json *j = cfg.get("model_type"); j && j->kind == Json::STR) {
+    mt = j->str;
+    if (mt != "llama" && mt != "qwen2" && mt != "qwen3") {
+      why = "model_type=\"" + mt + "\" is not in the CIS-2 specified subset [\"llama\", \"qwen2\", \"qwen3\"]";
+      return false;
+    }
+  }
+  if (const Json *j = cfg.get("torch_dtype"); j && j->kind == Json::STR && j->str != "bfloat16") {
+    why = "torch_dtype=\"" + j->str + "\"; CIS-2 pins bf16-on-disk weights (\u00a73.5)";
+    return false;
+  }
+  const Json *h = cfg.get("hidden_size"), *nh = cfg.get("num_attention_heads");
+  if (h && nh && h->kind == Json::NUM && nh->kind == Json::NUM) {
+    if (nh->num == 0) { why = "num_attention_heads=0"; return false; }
+    const long derived = (long)h->num / (long)nh->num;
+    long used = derived;
+    if (const Json *j = cfg.get("head_dim"); j && j->kind == Json::NUM) {
+      if ((long)j->num != derived && mt != "qwen3") {
+        why = "config declares head_dim=" + std::to_string((long)j->num) +
+              " but hidden_size/num_attention_heads=" + std::to_string(derived) +
+              "; only the qwen3 port uses an explicit head_dim";
+        return false;
+      }
+      used = (long)j->num;
+    }
+    if (used % 2 != 0) { why = "head_dim=" + std::to_string(used) + " is odd; RoPE pairs require even"; return false; }
+  }
+  if (const Json *j = cfg.get("partial_rotary_factor"); j && j->kind == Json::NUM && j->num != 1.0) {
+    why = "partial_rotary_factor is not 1; only full rotary is specified";
+    return false;
+  }
+  if (present("rope_scaling")) { why = "rope_scaling is set; only unscaled RoPE is specified"; return false; }
+  if (const Json *j = cfg.get("use_sliding_window"); j && j->kind == Json::BOOL && j->b) {
+    why = "use_sliding_window=true; only full causal attention is specified";
+    return false;
+  }
+  if (present("quantization_config")) {
+    why = "quantization_config is present; CIS-2 reads unquantized bf16 weights";
+    return false;
+  }
+  for (const char *k : {"attention_multiplier", "embedding_multiplier", "residual_multiplier", "logits_scaling",
+                        "attn_logit_softcapping", "final_logit_softcapping", "query_pre_attn_scalar"})
+    if (present(k)) {
+      why = std::string(k) + " is set; this decoder uses rsqrt(head_dim) attention scaling and no logit scaling, "
+            "so the result would be silently wrong";
+      return false;
+    }
+  for (const char *k : {"num_local_experts", "num_experts", "n_routed_experts", "moe_intermediate_size"})
+    if (present(k)) { why = std::string(k) + " is set; MoE routing is not specified"; return false; }
+  return true;
+}
+
 int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   if (!dir_c) return fail(CIS2B_ERR_ARG, "weights_dir is NULL");
   cis2b_opts o{};
@@ -199,13 +265,23 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   m->max_pos = o.max_positions ? o.max_positions : 4096;
 
   // Everything up to the upload is host work, so artifact and config errors
-  // are reported the same way with or without a device.
+  // are reported the same way with or without a device.  The config is read
+  // and gated first, so an unsupported checkpoint is refused by name even
+  // without its weights (code/cis2-fp/src/main.rs:812-823).
   const std::string dir(dir_c);
   std::string wbytes, tok, cfgtxt;
+  if (!read_file(dir + "/config.json", cfgtxt)) return fail(CIS2B_ERR_IO, "cannot read " + dir + "/config.json");
+  Json cfg;
+  std::string jerr;
+  if (!JsonParser(cfgtxt.data(), cfgtxt.data() + cfgtxt.size()).parse(cfg, jerr) || cfg.kind != Json::OBJ)
+    return fail(CIS2B_ERR_IO, "config.json: " + (jerr.empty() ? std::string("not an object") : jerr));
+  {
+    std::string why;
+    if (!gate_architecture(cfg, why)) return fail(CIS2B_ERR_CONFIG, why);
+  }
   if (!read_file(dir + "/model.safetensors", wbytes))
     return fail(CIS2B_ERR_IO, "cannot read " + dir + "/model.safetensors");
   if (!read_file(dir + "/tokenizer.json", tok)) return fail(CIS2B_ERR_IO, "cannot read " + dir + "/tokenizer.json");
-  if (!read_file(dir + "/config.json", cfgtxt)) return fail(CIS2B_ERR_IO, "cannot read " + dir + "/config.json");
   {
     Sha256 a, b, c;
     a.update(wbytes.data(), wbytes.size());
@@ -217,10 +293,6 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   }
 
   // ---- config (cis2_host.cpp:97-117, qwen3-port.diff:109-110)
-  Json cfg;
-  std::string jerr;
-  if (!JsonParser(cfgtxt.data(), cfgtxt.data() + cfgtxt.size()).parse(cfg, jerr) || cfg.kind != Json::OBJ)
-    return fail(CIS2B_ERR_IO, "config.json: " + (jerr.empty() ? std::string("not an object") : jerr));
   auto need = [&](const char *k, double &v) -> bool {
     const Json *j = cfg.get(k);
     if (!j || j->kind != Json::NUM) return false;
@@ -240,8 +312,6 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   if (const Json *j = cfg.get("head_dim"); j && j->kind == Json::NUM) m->HD = (int)j->num;
   bool tied = true;
   if (const Json *j = cfg.get("tie_word_embeddings")) tied = (j->kind == Json::BOOL) ? j->b : true;
-  if (const Json *j = cfg.get("rope_scaling"); j && j->kind != Json::NUL)
-    return fail(CIS2B_ERR_CONFIG, "rope_scaling is not part of the CIS-2 arithmetic");
   m->QD = m->NH * m->HD;
   m->KVD = m->NKV * m->HD;
   if (m->NH % m->NKV) return fail(CIS2B_ERR_CONFIG, "num_attention_heads % num_key_value_heads != 0");

@@ -73,6 +73,26 @@ def test_load_refuses_bad_configs(pkg, synth, synth_root, tmp_path):
         (d / "config.json").write_text(json.dumps(c))
         rc, msg, _ = _load_rc(pkg, str(d))
         assert rc == code and word in msg, (patch, rc, msg)
+    # The architecture gate (code/cis2-fp/src/main.rs:545-644).
+    for patch, word in [({"model_type": "mistral"}, "model_type"), ({"torch_dtype": "float16"}, "torch_dtype"),
+                        ({"head_dim": 32}, "head_dim"), ({"partial_rotary_factor": 0.5}, "partial_rotary_factor"),
+                        ({"use_sliding_window": True}, "use_sliding_window"),
+                        ({"quantization_config": {"bits": 4}}, "quantization_config"),
+                        ({"attention_multiplier": 0.5}, "attention_multiplier"),
+                        ({"final_logit_softcapping": 30.0}, "final_logit_softcapping"),
+                        ({"num_experts": 8}, "num_experts")]:
+        c = dict(cfg)
+        c.update(patch)
+        (d / "config.json").write_text(json.dumps(c))
+        rc, msg, _ = _load_rc(pkg, str(d))
+        assert rc == 3 and word in msg, (patch, rc, msg)
+    # Null-valued keys and the settings the gate allows pass it.
+    c = dict(cfg)
+    c.update({"rope_scaling": None, "quantization_config": None, "use_sliding_window": False,
+              "partial_rotary_factor": 1.0, "model_type": "qwen2"})
+    (d / "config.json").write_text(json.dumps(c))
+    rc, msg, _ = _load_rc(pkg, str(d))
+    assert rc != 3, msg
     c = dict(cfg)
     del c["vocab_size"]
     (d / "config.json").write_text(json.dumps(c))
@@ -81,6 +101,25 @@ def test_load_refuses_bad_configs(pkg, synth, synth_root, tmp_path):
     (d / "config.json").write_text("{not json")
     rc, msg, _ = _load_rc(pkg, str(d))
     assert rc == 2
+
+
+def test_gate_runs_before_the_weights_are_read(pkg, synth, synth_root, tmp_path):
+    """An unsupported checkpoint is refused by name even without its weights
+    (code/cis2-fp/src/main.rs:812-823); the CLI prints the reference's
+    CIS2_REF_UNSUPPORTED line and exits 2."""
+    d = _copy_model(synth, synth_root, tmp_path)
+    cfg = json.loads((d / "config.json").read_text())
+    cfg["model_type"] = "gemma"
+    (d / "config.json").write_text(json.dumps(cfg))
+    (d / "model.safetensors").unlink()
+    rc, msg, _ = _load_rc(pkg, str(d))
+    assert rc == 3 and "model_type" in msg
+    ids = tmp_path / "ids.txt"
+    ids.write_text("1 2 3\n")
+    p = subprocess.run([pkg.CLI_PATH, "--weights-dir", str(d), "--ids", str(ids), "--gen-toks", "2"],
+                       capture_output=True, text=True, timeout=60)
+    assert p.returncode == 2
+    assert p.stderr.startswith("CIS2_REF_UNSUPPORTED reason=model_type="), p.stderr
 
 
 def test_load_detects_corrupt_weights(pkg, synth, synth_root, tmp_path):
