@@ -1285,6 +1285,207 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
                                      k_norm, eps, cos_t, sin_t);
 }
 
+// ---- Prompt-pass attention, several rows per CTA.  In the prompt pass the
+// rows of one sequence are consecutive positions, and row p reads keys and
+// values 0..p, so one CTA takes a tile of up to `rt` such rows for one KV
+// head and streams each K/V chunk through shared memory once for all of
+// them (the one-row kernel above waits for each chunk once per row).  Per
+// (row, head) the arithmetic is the one-row kernel's, in the same order: the
+// scaled dot of every key, the serial-scan max, pinned exp, the pinned-order
+// denominator (one thread per (row, head) chain, or the 32-leaf blocks in
+// tree mode), the division, and the V-mix chain per (row, head, d) over keys
+// ascending.  tiles[t] = (first row, rows) of the pass's row list.
+constexpr int ATTR_NT = 256;
+constexpr int ATTR_CHAINS = 16;  // V-mix chains per thread at most
+
+int attention_rows_rt(int G, int hd, int max_len) {
+  const size_t row_bytes = (size_t)G * (((size_t)max_len + 3) / 4 * 4 + 4) * 4;  // one row's scores
+  int rt = (int)((64 * 1024) / row_bytes);
+  const int by_chains = ATTR_CHAINS * (ATTR_NT / hd) / G;
+  if (rt > by_chains) rt = by_chains;
+  if (rt > 16) rt = 16;
+  return rt < 1 ? 1 : rt;
+}
+size_t attention_rows_smem_floats(int rt, int G, int hd, int max_len) {
+  const size_t scs = (((size_t)max_len + 3) & ~(size_t)3) + 4;  // +4: rows start on different banks
+  const size_t P = (size_t)rt * G;
+  size_t f = P * hd + P * scs + P * ((size_t)max_len / 32 + 1) + 3 * P + 8;
+  f = (f + 3) & ~(size_t)3;
+  return f + (size_t)2 * ATT_JC * (hd + 4);
+}
+
+__global__ void __launch_bounds__(ATTR_NT)
+k_attention_rows(const float *qkv, int ld, const int2 *tiles, const int32_t *rseq, const int32_t *rpos, int rt,
+                 int nh, int nkv, int hd, const float *kc, const float *vc, int max_pos, int tree, float *att,
+                 int ars, int acs, int max_len) {
+  extern __shared__ __align__(16) float sm[];
+  const int kvh = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+  const int G = nh / nkv, KV = nkv * hd;
+  const int2 tl = tiles[blockIdx.x];
+  const int r0 = tl.x, nr = tl.y, P = nr * G;
+  const int seq = rseq[r0], p0 = rpos[r0];
+  const int lenmax = p0 + nr;                        // keys 0 .. p0 + nr - 1
+  const int scs = ((max_len + 3) & ~3) + 4;
+  const int npb = max_len / 32 + 1;
+  const int PR = rt * G;                             // pair slots the layout reserves
+  float *q = sm;                                     // [pair][hd], pair = i * G + g
+  float *sc = q + (size_t)PR * hd;                   // [pair][scs]
+  float *part = sc + (size_t)PR * scs;               // [pair][npb] (tree mode)
+  float *red = part + (size_t)PR * npb;              // [2][pair]: max, denominator
+  int *lim = reinterpret_cast<int *>(red + 2 * PR);  // [pair]: last key position the row reads
+  size_t toff = (size_t)(red + 3 * PR + 8 - sm);
+  toff = (toff + 3) & ~(size_t)3;
+  float *tiles_s = sm + toff;                        // [2][ATT_JC][hd + 4]
+  const int ts = hd + 4;
+  for (int x = tid; x < P * hd; x += nt) {
+    const int pr = x / hd, d = x - pr * hd, i = pr / G, g = pr - i * G;
+    q[x] = qkv[(size_t)(r0 + i) * ld + ((size_t)kvh * G + g) * hd + d];
+  }
+  for (int pr = tid; pr < P; pr += nt) lim[pr] = p0 + pr / G;
+  const float scale = rsqrt_cr(__int2float_rn(hd));
+  const float *kbase = kc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
+  const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * hd;
+  const int nch = (lenmax + ATT_JC - 1) / ATT_JC;
+  const uint32_t tbase = (uint32_t)__cvta_generic_to_shared(tiles_s);
+  auto stage = [&](const float *base, int c, int buf) {
+    const int j0 = c * ATT_JC, jc = min(ATT_JC, lenmax - j0), nq = hd / 4;
+    for (int x = tid; x < jc * nq; x += nt) {
+      const int jj = x / nq, q4 = x - jj * nq;
+      cp_async16(tbase + (uint32_t)(((buf * ATT_JC + jj) * ts + 4 * q4) * 4), base + (size_t)(j0 + jj) * KV + 4 * q4);
+    }
+    cp_async_commit();
+  };
+
+  // ---- scores
+  stage(kbase, 0, 0);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) stage(kbase, c + 1, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int j0 = c * ATT_JC;
+    const float *tile = tiles_s + (size_t)(c & 1) * ATT_JC * ts;
+    for (int x = tid; x < P * ATT_JC; x += nt) {
+      const int pr = x / ATT_JC, jj = x % ATT_JC;
+      if (j0 + jj > lim[pr]) continue;  // past this row's position (and past the chunk)
+      const float *qg = q + (size_t)pr * hd, *kj = tile + jj * ts;
+      float d;
+      if (!tree) {
+        const float4 *q4 = reinterpret_cast<const float4 *>(qg), *k4 = reinterpret_cast<const float4 *>(kj);
+        d = 0.0f;
+        for (int u = 0; u < hd / 4; ++u) {
+          const float4 a = q4[u], b = k4[u];
+          d = fadd(d, fmul(a.x, b.x));
+          d = fadd(d, fmul(a.y, b.y));
+          d = fadd(d, fmul(a.z, b.z));
+          d = fadd(d, fmul(a.w, b.w));
+        }
+      } else {
+        d = dot_tree(qg, kj, hd);
+      }
+      sc[(size_t)pr * scs + j0 + jj] = fmul(d, scale);
+    }
+    __syncthreads();
+  }
+  stage(vbase, 0, 0);  // V chunk 0 loads while the softmax runs
+  // ---- max per (row, head), serial-scan semantics
+  for (int pr = warp; pr < P; pr += nw) {
+    const float *sg = sc + (size_t)pr * scs;
+    const int len = lim[pr] + 1;
+    float mx = bitsf(0x7fc00000u);
+    for (int j = lane; j < len; j += 32) mx = max_comb(mx, sg[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max_comb(mx, __shfl_xor_sync(FULL, mx, o));
+    if (lane == 0) red[pr] = is_nan(sg[0]) ? sg[0] : mx;
+  }
+  __syncthreads();
+  for (int pr = 0; pr < P; ++pr) {
+    float *sg = sc + (size_t)pr * scs;
+    const int len = lim[pr] + 1;
+    const float mg = red[pr];
+    for (int j = tid; j < len; j += nt) sg[j] = exp_pinned(fsub(sg[j], mg));
+  }
+  __syncthreads();
+  // ---- denominators: one thread per (row, head) chain
+  if (tree) {
+    for (int pr = 0; pr < P; ++pr) {
+      const int len = lim[pr] + 1, nb = (len + 31) / 32;
+      for (int b = warp; b < nb; b += nw) {
+        const int j = b * 32 + lane;
+        const float v = warp_tree32(j < len ? sc[(size_t)pr * scs + j] : 0.0f);
+        if (lane == 0) part[(size_t)pr * npb + b] = v;
+      }
+    }
+    __syncthreads();
+  }
+  for (int pr = tid; pr < P; pr += nt) {
+    const int len = lim[pr] + 1;
+    red[PR + pr] = tree ? serial_sum(part + (size_t)pr * npb, (len + 31) / 32) : serial_sum4(sc + (size_t)pr * scs, len);
+  }
+  __syncthreads();
+  for (int pr = 0; pr < P; ++pr) {
+    float *sg = sc + (size_t)pr * scs;
+    const int len = lim[pr] + 1;
+    const float den = red[PR + pr];
+    for (int j = tid; j < len; j += nt) sg[j] = fdiv(sg[j], den);
+  }
+  // ---- V-mix: thread owns d = tid % hd of pairs tid / hd + k * (nt / hd)
+  const int d = tid % hd, slot0 = tid / hd, slots = nt / hd;
+  float acc[ATTR_CHAINS];
+#pragma unroll
+  for (int k = 0; k < ATTR_CHAINS; ++k) acc[k] = 0.0f;
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) stage(vbase, c + 1, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int j0 = c * ATT_JC;
+    const float *tile = tiles_s + (size_t)(c & 1) * ATT_JC * ts + d;
+    if (slot0 < slots) {
+#pragma unroll
+      for (int k = 0; k < ATTR_CHAINS; ++k) {
+        const int pr = slot0 + k * slots;
+        if (pr < P) {
+          const int je = min(ATT_JC, lim[pr] + 1 - j0);  // keys of this chunk the row reads
+          const float *pg = sc + (size_t)pr * scs + j0;
+          float a = acc[k];
+          for (int jj = 0; jj < je; ++jj) a = fadd(a, fmul(pg[jj], tile[jj * ts]));
+          acc[k] = a;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  if (slot0 < slots) {
+#pragma unroll
+    for (int k = 0; k < ATTR_CHAINS; ++k) {
+      const int pr = slot0 + k * slots;
+      if (pr < P) {
+        const int i = pr / G, g = pr - i * G;
+        att[(size_t)(r0 + i) * ars + (((size_t)kvh * G + g) * hd + d) * acs] = acc[k];
+      }
+    }
+  }
+}
+
+void launch_attention_rows(const float *qkv, int ld, const int2 *tiles, int n_tiles, int rt, RowMap rm, int n_heads,
+                           int n_kv, int hd, const float *kcache, const float *vcache, int max_pos, bool tree,
+                           float *att, int ars, int acs, int max_len, cudaStream_t s) {
+  if (n_tiles <= 0) return;
+  const int G = n_heads / n_kv;
+  const size_t smem = attention_rows_smem_floats(rt, G, hd, max_len) * sizeof(float);
+  static size_t attr = 48 * 1024;
+  if (smem > attr) {
+    cudaFuncSetAttribute(k_attention_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = smem;
+  }
+  k_attention_rows<<<dim3(n_tiles, n_kv), ATTR_NT, smem, s>>>(qkv, ld, tiles, rm.seq, rm.pos, rt, n_heads, n_kv, hd,
+                                                             kcache, vcache, max_pos, tree ? 1 : 0, att, ars, acs,
+                                                             max_len);
+}
+
 // ============================================================ token selection
 
 struct ArgBest { float v; int i; };

@@ -71,6 +71,16 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
                       cudaStream_t s);
 // Shared memory (floats) the attention kernel needs; G = n_heads / n_kv.
 size_t attention_smem_floats(int G, int hd, int max_len);
+// Prompt-pass attention over tiles of consecutive rows of one sequence
+// (consecutive positions): tiles[t] = (first row, rows <= rt).  Each K/V
+// chunk is staged once per tile instead of once per row.  rt from
+// attention_rows_rt (scores of rt rows fit the shared-memory budget);
+// max_len >= the largest position + 1 of the pass; hd <= 256.
+int attention_rows_rt(int G, int hd, int max_len);
+size_t attention_rows_smem_floats(int rt, int G, int hd, int max_len);
+void launch_attention_rows(const float *qkv, int ld, const int2 *tiles, int n_tiles, int rt, RowMap rm, int n_heads,
+                           int n_kv, int hd, const float *kcache, const float *vcache, int max_pos, bool tree,
+                           float *att, int ars, int acs, int max_len, cudaStream_t s);
 // Index of the GEMM tile the dispatcher picks for (M, N, K).
 int gemm_tile_choice(int M, int N, int K, bool tree);
 void launch_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs, cudaStream_t s);

@@ -116,7 +116,7 @@ struct cis2b_model {
   // workspace
   DevBuf h, ln, qkv, att, gu, hid, hlast, lnlast, kc, vc, ring, scratch;
   int act_ldm = 0;  // column count of the k-major activation buffers
-  DevBuf rows_seq, rows_pos, rows_tok, gsrc, gdst;
+  DevBuf rows_seq, rows_pos, rows_tok, gsrc, gdst, att_tiles;
   DevBuf d_next, d_pos, d_spos, d_seq, d_ctl, d_tokens, d_ids_hist;
   DevBuf sha_state, sha_wk, sha_c0, step_dig, d_witness, d_argmax;
   DevBuf hdr_bytes, hdr_off, p_flat, p_off, p_len;
@@ -571,8 +571,14 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
 // state in m->h.  kv caches are [layer][seq][maxP][kvd].  `decode`: every
 // row is a different sequence's newest position, so the q/k post-processing
 // and the cache append run inside the attention kernel.
+// Row tiles for the prompt-pass attention (launch_attention_rows).
+struct AttTiles {
+  const int2 *tiles = nullptr;
+  int n = 0, rt = 0, max_len = 0;
+};
+
 int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *seq,
-                 const int32_t *pos, int n_seq_cache, int maxP, bool decode) {
+                 const int32_t *pos, int n_seq_cache, int maxP, bool decode, const AttTiles *at = nullptr) {
   cudaStream_t s = m->s_main;
   const int H = m->H, I = m->I, QD = m->QD, KVD = m->KVD, NQKV = QD + 2 * KVD;
   float *h = m->h.as<float>(), *ln = m->ln.as<float>(), *qkv = m->qkv.as<float>();
@@ -609,9 +615,13 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
       m->launches++;
     }
     { ProfScope p(m, CIS2B_PROF_ATTENTION, s);
-      launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, atr,
-                       dec ? 1 : ldm, maxP, decode, w.q_norm, w.k_norm, m->eps, m->cos_t.as<float>(),
-                       m->sin_t.as<float>(), s); }
+      if (!decode && at && at->n > 0)
+        launch_attention_rows(qkv, NQKV, at->tiles, at->n, at->rt, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree,
+                              att, atr, ldm, at->max_len, s);
+      else
+        launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, atr,
+                         dec ? 1 : ldm, maxP, decode, w.q_norm, w.k_norm, m->eps, m->cos_t.as<float>(),
+                         m->sin_t.as<float>(), s); }
     gemm(att, w.po, w.to, QD, H, h, H, h, H);
     launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, lnr, lnc, s);
     if (dec) {  // SwiGLU in the gate/up GEMM's epilogue
@@ -699,11 +709,45 @@ int prefill(cis2b_model *m, const std::vector<uint32_t> &tok, const std::vector<
     CU(cudaMemcpyAsync(m->gsrc.p, gs.data(), 4 * gs.size(), cudaMemcpyHostToDevice, s));
     CU(cudaMemcpyAsync(m->gdst.p, gd.data(), 4 * gd.size(), cudaMemcpyHostToDevice, s));
   }
+  // Attention row tiles per chunk: runs of rows of one sequence at
+  // consecutive positions, at most rt long (rt from the chunk's longest row).
+  std::vector<int2> tl;
+  std::vector<AttTiles> ats;
+  const bool tiled = m->HD <= 256;
+  for (int c0 = 0; c0 < total && tiled; c0 += chunk) {
+    const int n = std::min(chunk, total - c0);
+    int maxpos = 0;
+    for (int i = c0; i < c0 + n; ++i) maxpos = std::max(maxpos, (int)pos[(size_t)i]);
+    AttTiles a;
+    a.max_len = maxpos + 1;
+    a.rt = attention_rows_rt(m->NH / m->NKV, m->HD, a.max_len);
+    a.n = (int)tl.size();  // index of the chunk's first tile until the pointers are known
+    for (int i = c0; i < c0 + n;) {
+      int k = 1;
+      while (k < a.rt && i + k < c0 + n && seq[(size_t)(i + k)] == seq[(size_t)i] &&
+             pos[(size_t)(i + k)] == pos[(size_t)i] + k)
+        ++k;
+      tl.push_back(make_int2(i - c0, k));
+      i += k;
+    }
+    ats.push_back(a);
+  }
+  if (!tl.empty()) {
+    if (m->att_tiles.ensure(sizeof(int2) * tl.size()))
+      return fail(CIS2B_ERR_NOMEM, "device allocation of attention tiles failed");
+    CU(cudaMemcpyAsync(m->att_tiles.p, tl.data(), sizeof(int2) * tl.size(), cudaMemcpyHostToDevice, s));
+    for (size_t c = 0; c < ats.size(); ++c) {
+      const int first = ats[c].n, last = c + 1 < ats.size() ? ats[c + 1].n : (int)tl.size();
+      ats[c].tiles = m->att_tiles.as<int2>() + first;
+      ats[c].n = last - first;
+    }
+  }
   int ci = 0;
   for (int c0 = 0; c0 < total; c0 += chunk, ++ci) {
     const int n = std::min(chunk, total - c0);
     rc = forward_rows(m, n, m->rows_tok.as<uint32_t>() + c0, m->rows_seq.as<int32_t>() + c0,
-                      m->rows_pos.as<int32_t>() + c0, n_seq_cache, maxP, false);
+                      m->rows_pos.as<int32_t>() + c0, n_seq_cache, maxP, false,
+                      tiled ? &ats[(size_t)ci] : nullptr);
     if (rc) return rc;
     const auto &rg = ranges[(size_t)ci];
     if (rg.second) {
