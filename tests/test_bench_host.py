@@ -1,0 +1,63 @@
+"""The arithmetic behind bench.py's roofline fields, on CPU: the witness
+chain's issue-bound fraction, the per-launch achieved rates from event
+timings, and the step bound's label."""
+from __future__ import annotations
+
+import pytest
+
+import bench
+
+synth = bench.synth
+
+
+def _prof(witness_ms_per_launch=None, lm_ms_per_launch=None, launches=256):
+    p = {}
+    if witness_ms_per_launch is not None:
+        p["witness"] = {"launches": launches, "total_ms": witness_ms_per_launch * launches}
+    if lm_ms_per_launch is not None:
+        p["lm_head"] = {"launches": launches, "total_ms": lm_ms_per_launch * launches}
+    return p
+
+
+def test_witness_roofline_fields():
+    m, w = synth.MODELS["smollm2"], synth.WORKLOADS["c2"]
+    # 3,073 blocks per chain at 1,408 cycles each, at 1,965 MHz: the issue bound.
+    blocks = (4 * m.vocab + 4) / 64.0
+    t_ms = blocks * bench.CHAIN_FLOOR_CYCLES_PER_BLOCK / 1965e6 * 1e3
+    r = bench.kernel_rooflines(m, w, 64, _prof(witness_ms_per_launch=t_ms), 1965.0)["witness"]
+    assert r["chain_frac"] == pytest.approx(1.0, rel=1e-9)
+    assert r["cycles_per_block_per_chain"] == pytest.approx(bench.CHAIN_FLOOR_CYCLES_PER_BLOCK, rel=1e-9)
+    assert r["algorithmic_bytes"] == 64 * (4 * m.vocab + 4)
+    assert r["achieved"] == pytest.approx(r["algorithmic_bytes"] / (t_ms / 1e3) / 1e9)
+    assert r["frac"] == pytest.approx(r["achieved"] / r["peak"])
+    assert r["traffic"] == bench.WITNESS_TRAFFIC_C2  # the captured shape
+    # Twice as slow: half the fraction.
+    r2 = bench.kernel_rooflines(m, w, 64, _prof(witness_ms_per_launch=2 * t_ms), 1965.0)["witness"]
+    assert r2["chain_frac"] == pytest.approx(0.5, rel=1e-9)
+    # Another shape has no captured traffic figure.
+    r3 = bench.kernel_rooflines(m, w, 32, _prof(witness_ms_per_launch=t_ms), 1965.0)["witness"]
+    assert r3["traffic"] is None
+
+
+def test_lm_head_roofline_fields():
+    m, w = synth.MODELS["smollm2"], synth.WORKLOADS["c2"]
+    r = bench.kernel_rooflines(m, w, 64, _prof(lm_ms_per_launch=0.2), 1965.0)["lm_head"]
+    byts = m.vocab * m.hidden * 2 + 64 * m.hidden * 4 + 64 * m.vocab * 4
+    assert r["algorithmic_bytes"] == byts
+    assert r["achieved"] == pytest.approx(byts / 0.2e-3 / 1e9)
+    fp32 = 148 * 128 * 1965e6
+    assert r["fp32_alu_frac"] == pytest.approx(2 * 64 * m.vocab * m.hidden / 0.2e-3 / fp32)
+
+
+def test_step_bound_label_follows_the_longer_path():
+    m, w = synth.MODELS["smollm2"], synth.WORKLOADS["c2"]
+    peak, src = bench.measured_peaks()
+    a = bench.step_roofline(m, w, 64, 2.8e-3, peak, src, forward_ms=2.6, witness_ms=2.76)
+    b = bench.step_roofline(m, w, 64, 2.8e-3, peak, src, forward_ms=3.0, witness_ms=2.76)
+    assert a["bound_actual"].startswith("witness chain")
+    assert b["bound_actual"].startswith("decode forward pass")
+    # The HBM side does not depend on the label: bf16 weights once, KV and logits.
+    assert a["algorithmic_bytes_per_step"] == b["algorithmic_bytes_per_step"]
+    assert a["weights_bytes"] == 2 * (m.layers * (m.hidden * (m.q_dim + 2 * m.kv_dim) + m.q_dim * m.hidden
+                                                 + 3 * m.inter * m.hidden) + m.vocab * m.hidden)
+    assert a["frac"] == pytest.approx(a["achieved"] / peak)
