@@ -24,6 +24,27 @@ namespace cis2b {
 
 static constexpr unsigned FULL = 0xffffffffu;
 
+// A kernel's dynamic shared-memory limit.  cudaFuncSetAttribute acts on the
+// current device only, and one process may drive several devices (one model
+// handle each, possibly from several threads), so each launcher keeps one of
+// these per kernel and raises the limit once per device, never lowering it.
+struct SmemLimit {
+  static constexpr int kMaxDevices = 64;
+  std::mutex mu;
+  size_t bytes[kMaxDevices] = {};
+  template <class F>
+  void ensure(F fn, size_t need) {
+    int d = -1;
+    cudaGetDevice(&d);
+    std::lock_guard<std::mutex> lk(mu);
+    if (d >= 0 && d < kMaxDevices) {
+      if (bytes[d] >= need) return;
+      bytes[d] = need;
+    }
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need);
+  }
+};
+
 // ============================================================ reductions
 
 // Pairwise 32-leaf tree across a warp: after round s every lane holds the
@@ -261,11 +282,8 @@ void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n
   if (rows <= 0) return;
   const size_t rsm = ((size_t)RMS_ROWS * (n + 4) + RMS_ROWS) * sizeof(float);
   if (!tree && n % 4 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && rsm <= 227 * 1024) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(k_rmsnorm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
+    static SmemLimit lim;
+    lim.ensure(k_rmsnorm_rows, 227 * 1024);
     k_rmsnorm_rows<<<(rows + RMS_ROWS - 1) / RMS_ROWS, RMS_THREADS, rsm, s>>>(x, ldx, w, eps, n, rows, out, ors,
                                                                               ocs);
     return;
@@ -484,12 +502,8 @@ static void run_gemm_t(const float *XT, int ldm, const uint16_t *Wp, int K, int 
                        const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s) {
   constexpr int NT = (BM / TM) * (8 * BP / TN);
   const size_t smem = (size_t)GEMM_STAGES * (GEMM_KT * BM * 4 + GEMM_KT * 8 * BP * 2);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_t<BM, BP, TM, TN, TREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr_set = true;
-  }
+  static SmemLimit lim;
+  lim.ensure(k_gemm_t<BM, BP, TM, TN, TREE>, smem);
   dim3 grid((N + 8 * BP - 1) / (8 * BP), (M + BM - 1) / BM);
   k_gemm_t<BM, BP, TM, TN, TREE><<<grid, NT, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot,
                                                           y_slot_stride);
@@ -658,11 +672,8 @@ template <int BIG_BM, int BN>
 static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s) {
   const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BIG_BM * 4 + BIG_KT * BN * 2);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_big<BIG_BM, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
+  static SmemLimit lim;
+  lim.ensure(k_gemm_big<BIG_BM, BN>, smem);
   dim3 grid((N + BN - 1) / BN, (M + BIG_BM - 1) / BIG_BM);
   k_gemm_big<BIG_BM, BN><<<grid, BIG_THREADS, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot,
                                                         y_slot_stride);
@@ -942,11 +953,8 @@ static void run_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int
   constexpr int ROWS = TM * RW;
   const size_t smem = (XS ? (size_t)DEC_STAGES * ROWS * DEC_KC * 4 : (size_t)ROWS * K * 4) +
                       (size_t)DEC_STAGES * DEC_KC * 32 * 2;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(k_gemm_dec<TM, RW, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr_set = true;
-  }
+  static SmemLimit lim;
+  lim.ensure(k_gemm_dec<TM, RW, XS>, 227 * 1024);
   dim3 grid((N + 31) / 32, (M + ROWS - 1) / ROWS);
   k_gemm_dec<TM, RW, XS><<<grid, 32 * RW, smem, s>>>(X, ldx, Wt, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride,
                                                       glu);
@@ -1274,11 +1282,8 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
   int nt = ((G * hd + 31) / 32) * 32;
   if (nt < 128) nt = 128;
   size_t smem = attention_smem_floats(G, hd, max_len) * sizeof(float);
-  static size_t attr = 48 * 1024;
-  if (smem > attr) {
-    cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = smem;
-  }
+  static SmemLimit lim;
+  if (smem > 48 * 1024) lim.ensure(k_attention, smem);
   dim3 grid(rows, n_kv);
   k_attention<<<grid, nt, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache, max_pos,
                                      tree ? 1 : 0, att, ars, acs, max_len, fuse_post ? 1 : 0, q_norm,
@@ -1476,11 +1481,8 @@ void launch_attention_rows(const float *qkv, int ld, const int2 *tiles, int n_ti
   if (n_tiles <= 0) return;
   const int G = n_heads / n_kv;
   const size_t smem = attention_rows_smem_floats(rt, G, hd, max_len) * sizeof(float);
-  static size_t attr = 48 * 1024;
-  if (smem > attr) {
-    cudaFuncSetAttribute(k_attention_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = smem;
-  }
+  static SmemLimit lim;
+  if (smem > 48 * 1024) lim.ensure(k_attention_rows, smem);
   k_attention_rows<<<dim3(n_tiles, n_kv), ATTR_NT, smem, s>>>(qkv, ld, tiles, rm.seq, rm.pos, rt, n_heads, n_kv, hd,
                                                              kcache, vcache, max_pos, tree ? 1 : 0, att, ars, acs,
                                                              max_len);
@@ -2268,13 +2270,9 @@ void launch_sha_compress(ShaState *st, int n_seq, const float *logits, int V, si
                          const uint32_t *next_ids, const uint32_t *wk_scratch, uint8_t *step_digest_out,
                          size_t digest_stride, cudaStream_t s) {
   if (n_seq <= 0) return;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_sha_compress<SHA_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SHA_SMEM);
-    cudaFuncSetAttribute(k_sha_compress<SHA_SOLO_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)SHA_SMEM);
-    attr = true;
-  }
+  static SmemLimit lim_shared, lim_solo;
+  lim_shared.ensure(k_sha_compress<SHA_STAGES>, SHA_SMEM);
+  lim_solo.ensure(k_sha_compress<SHA_SOLO_STAGES>, SHA_SMEM);
   const int warps = (n_seq + 31) / 32;
   if (warps <= SHA_SOLO_WARPS) {
     k_sha_compress<SHA_SOLO_STAGES><<<warps, 32, SHA_SMEM, s>>>(st, n_seq, logits, V, row_stride, next_ids,
