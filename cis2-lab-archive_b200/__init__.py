@@ -39,7 +39,14 @@ class Cis2Error(RuntimeError):
 
 class _Opts(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("reduction", ctypes.c_int32),
-                ("max_positions", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5)]
+                ("max_positions", ctypes.c_int32), ("arch_gate", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 4)]
+
+
+# CIS2B_GATE_*: "reference" is the Rust reference's architecture gate
+# (model_type llama or qwen2); "qwen3-port" also admits model_type qwen3, as
+# the lab's Qwen3 port of the C++ path does.
+ARCH_GATES = {"reference": 0, "qwen3-port": 1}
 
 
 class _Sample(ctypes.Structure):
@@ -110,6 +117,7 @@ def lib() -> ctypes.CDLL:
     L.cis2b_op_pinned_map.argtypes = [I32, I32, P, P, SZ]
     L.cis2b_op_matmul.argtypes = [I32, P, P, I32, I32, I32, I32, P]
     L.cis2b_op_sha256_stream.argtypes = [I32, P, SZ, P, U32, U32, P]
+    L.cis2b_op_argmax.argtypes = [I32, P, I32, I32, P]
     L.cis2b_op_sample.argtypes = [I32, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
                                   ctypes.c_uint64, ctypes.POINTER(U32)]
     L.cis2b_op_sample_gumbel.argtypes = [I32, P, I32, ctypes.c_float, U32, ctypes.c_float, ctypes.c_uint64, U32,
@@ -140,9 +148,10 @@ class Model:
     """One loaded model on one device (reference: verify3 cis2_model_load)."""
 
     def __init__(self, weights_dir: str, device: int = 0, reduction: str | int = "sequential",
-                 max_positions: int = 0):
+                 max_positions: int = 0, arch_gate: str | int = "reference"):
         red = {"sequential": SEQUENTIAL, "tree": TREE}.get(reduction, reduction)
-        o = _Opts(device=device, reduction=int(red), max_positions=max_positions)
+        o = _Opts(device=device, reduction=int(red), max_positions=max_positions,
+                  arch_gate=int(ARCH_GATES.get(arch_gate, arch_gate)))
         h = ctypes.c_void_p()
         _check(lib().cis2b_load(weights_dir.encode(), ctypes.byref(o), ctypes.byref(h)))
         self._h = h
@@ -250,6 +259,14 @@ def sha256_stream(prefix: bytes, words: np.ndarray, chunk_words: int, device: in
     out = np.zeros((max(n_chunks, 1), 32), dtype=np.uint8)
     _check(lib().cis2b_op_sha256_stream(device, _ptr(pre), len(prefix), _ptr(words), chunk_words, n_chunks,
                                         _ptr(out)))
+    return out
+
+
+def argmax(logits: np.ndarray, device: int = 0) -> np.ndarray:
+    """First index of the strict maximum of each row (the decode steps' kernel)."""
+    x = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.float32)
+    out = np.zeros(x.shape[0], dtype=np.uint32)
+    _check(lib().cis2b_op_argmax(device, _ptr(x), x.shape[0], x.shape[1], _ptr(out)))
     return out
 
 

@@ -15,8 +15,14 @@
 //
 //   cis2b_ref --weights-dir D --ids F [--gen-toks N] [--reduction sequential|tree]
 //             [--mode greedy|sampled --seed S --temperature T --top-p P]
-//             [--sample SEED,T,K,P] [--receipt F]
+//             [--sample SEED,T,K,P] [--receipt F] [--arch-gate reference|qwen3-port]
 //             [--device I] [--prompt-idx I] [--step-digests]
+// The architecture gate runs on config.json first, as in the reference
+// (code/cis2-fp/src/main.rs:812-823): a refused checkpoint prints the two
+// CIS2_REF_UNSUPPORTED lines and exits 2 whatever else is missing; a failure
+// after the gate admitted the checkpoint (say, absent weights) exits 101, the
+// status the reference's panic gives, so refusal suites
+// (code/cis2-fp/tests/fixtures/run_refusal_suite.sh) tell the two apart.
 // With --receipt F (one line of claimed generated ids per prompt, all the
 // same length) the prompts are VERIFIED instead of decoded: one
 // teacher-forced pass (cis2b_verify), and per prompt the lines
@@ -88,6 +94,7 @@ int main(int argc, char **argv) {
   std::string weights_dir = "weights", ids_path, receipt_path;
   int gen = 16, device = 0, prompt_idx = 0;
   bool tree = false, sampled = false, gumbel = false, step_digests = false;
+  int arch_gate = CIS2B_GATE_REFERENCE;
   cis2b_sample smp{0, 0.8f, 0.95f, CIS2B_SAMPLE_E23, 0};
   for (int i = 1; i < argc; ++i) {
     std::string a = argv[i];
@@ -125,17 +132,23 @@ int main(int argc, char **argv) {
       smp.top_p = strtof(pbuf, nullptr);
       smp.scheme = CIS2B_SAMPLE_GUMBEL;
       gumbel = true;
+    } else if (a == "--arch-gate") {
+      std::string v = next();
+      if (v == "qwen3-port") arch_gate = CIS2B_GATE_QWEN3_PORT;
+      else if (v != "reference") { fprintf(stderr, "FATAL: --arch-gate reference|qwen3-port\n"); return 2; }
     } else if (a == "--receipt") receipt_path = next();
     else if (a == "--seed") smp.seed = strtoull(next(), nullptr, 10);
     else if (a == "--temperature") smp.temperature = strtof(next(), nullptr);
     else if (a == "--top-p") smp.top_p = strtof(next(), nullptr);
     else { fprintf(stderr, "FATAL: unknown CLI argument: %s\n", a.c_str()); return 2; }
   }
-  if (ids_path.empty() || gen < 0) { fprintf(stderr, "FATAL: --ids FILE is required\n"); return 2; }
+  if (gen < 0) { fprintf(stderr, "FATAL: --gen-toks must be >= 0\n"); return 2; }
 
   std::vector<std::vector<uint32_t>> prompts, claims;
-  if (!read_id_lines(ids_path, prompts)) return 2;
-  if (prompts.empty()) { fprintf(stderr, "FATAL: %s: no token ids\n", ids_path.c_str()); return 2; }
+  if (!ids_path.empty()) {
+    if (!read_id_lines(ids_path, prompts)) return 2;
+    if (prompts.empty()) { fprintf(stderr, "FATAL: %s: no token ids\n", ids_path.c_str()); return 2; }
+  }
   const bool verify = !receipt_path.empty();
   if (verify) {
     if (!read_id_lines(receipt_path, claims)) return 2;
@@ -144,13 +157,14 @@ int main(int argc, char **argv) {
               prompts.size());
       return 2;
     }
-    gen = (int)claims[0].size();
+    gen = claims.empty() ? 0 : (int)claims[0].size();
     for (auto &c : claims)
       if ((int)c.size() != gen) { fprintf(stderr, "FATAL: %s: claim lines differ in length\n", receipt_path.c_str()); return 2; }
   }
 
   cis2b_opts o{};
   o.device = device;
+  o.arch_gate = arch_gate;
   o.reduction = tree ? CIS2B_REDUCTION_TREE : CIS2B_REDUCTION_SEQUENTIAL;
   size_t maxp = 0;
   for (auto &p : prompts) maxp = p.size() > maxp ? p.size() : maxp;
@@ -164,6 +178,11 @@ int main(int argc, char **argv) {
   }
   if (lrc != CIS2B_OK) {
     fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
+    return 101;
+  }
+  if (prompts.empty()) {
+    fprintf(stderr, "FATAL: --ids FILE is required\n");
+    cis2b_free(m);
     return 2;
   }
   cis2b_info info;

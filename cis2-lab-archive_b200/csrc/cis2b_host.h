@@ -14,131 +14,245 @@
 namespace cis2b {
 
 // ------------------------------------------------------------------ JSON
-struct Json {
-  enum Kind { NUL, BOOL, NUM, STR, ARR, OBJ } kind = NUL;
-  bool b = false;
-  double num = 0.0;  // strtod: correctly rounded decimal -> f64
-  std::string str;
-  std::vector<Json> arr;
-  std::vector<std::pair<std::string, Json>> obj;
-  const Json *get(const char *k) const {
-    if (kind != OBJ) return nullptr;
-    for (auto &kv : obj)
-      if (kv.first == k) return &kv.second;
-    return nullptr;
-  }
-};
+// A parsed JSON text held as one flat array of nodes.  Containers list
+// their children by node index; an object's children alternate key, value.
+// Strings are decoded to UTF-8 (\uXXXX escapes included, surrogate pairs
+// joined), numbers are checked against the JSON grammar and converted once
+// with strtod (correctly rounded decimal -> f64; the loader narrows eps to
+// f32 from that f64 afterwards).  Access goes through JsonRef, a (document,
+// node) pair that is empty when a lookup misses, so chained lookups need no
+// null checks.
+class JsonDoc;
 
-class JsonParser {
+class JsonRef {
  public:
-  JsonParser(const char *p, const char *e) : p_(p), e_(e) {}
-  bool parse(Json &out, std::string &err) {
-    ok_ = true;
-    value(out, 0);
-    ws();
-    if (ok_ && p_ != e_) fail("trailing characters");
-    err = err_;
-    return ok_;
-  }
+  enum Type { None, Null, Bool, Number, String, Array, Object };
+  JsonRef() = default;
+  JsonRef(const JsonDoc *d, int n) : doc_(d), node_(n) {}
+  explicit operator bool() const { return doc_ && node_ >= 0; }
+  inline Type type() const;
+  bool is(Type t) const { return type() == t; }
+  inline bool boolean() const;        // Bool's value (false otherwise)
+  inline double number() const;       // Number's value (0 otherwise)
+  inline const std::string &text() const;  // String's value ("" otherwise)
+  inline size_t size() const;         // Array items / Object members
+  inline JsonRef item(size_t i) const;           // i-th Array item
+  inline JsonRef operator[](const char *key) const;  // Object member (first match)
 
  private:
-  const char *p_, *e_;
-  bool ok_ = true;
+  const JsonDoc *doc_ = nullptr;
+  int node_ = -1;
+};
+
+class JsonDoc {
+ public:
+  // Parses [b, e); on failure returns false with a message in `err`.
+  bool parse(const char *b, const char *e, std::string &err) {
+    nodes_.clear();
+    cur_ = b;
+    end_ = e;
+    err_.clear();
+    int root = parse_value(0);
+    skip_space();
+    if (root >= 0 && cur_ != end_) root = error("trailing characters after the top-level value");
+    err = err_;
+    return root >= 0;
+  }
+  JsonRef root() const { return nodes_.empty() ? JsonRef() : JsonRef(this, 0); }
+
+ private:
+  friend class JsonRef;
+  struct Node {
+    JsonRef::Type type = JsonRef::Null;
+    bool flag = false;
+    double value = 0.0;
+    std::string text;
+    std::vector<int> kids;
+  };
+  std::vector<Node> nodes_;
+  const char *cur_ = nullptr, *end_ = nullptr;
   std::string err_;
-  void fail(const char *m) {
-    if (ok_) err_ = m;
-    ok_ = false;
-    p_ = e_;
+  static const std::string &empty() {
+    static const std::string e;
+    return e;
   }
-  void ws() {
-    while (p_ < e_ && (*p_ == ' ' || *p_ == '\t' || *p_ == '\n' || *p_ == '\r')) ++p_;
+
+  int error(const char *what) {
+    if (err_.empty()) err_ = what;
+    cur_ = end_;
+    return -1;
   }
-  void str(std::string &s) {
-    if (p_ >= e_ || *p_ != '"') return fail("expected string");
-    ++p_;
-    while (p_ < e_ && *p_ != '"') {
-      char c = *p_++;
-      if (c != '\\') { s.push_back(c); continue; }
-      if (p_ >= e_) return fail("bad escape");
-      char x = *p_++;
-      switch (x) {
-        case 'n': s.push_back('\n'); break;
-        case 't': s.push_back('\t'); break;
-        case 'r': s.push_back('\r'); break;
-        case 'b': s.push_back('\b'); break;
-        case 'f': s.push_back('\f'); break;
+  void skip_space() {
+    while (cur_ < end_ && (*cur_ == ' ' || *cur_ == '\n' || *cur_ == '\r' || *cur_ == '\t')) ++cur_;
+  }
+  int add(JsonRef::Type t) {
+    nodes_.emplace_back();
+    nodes_.back().type = t;
+    return (int)nodes_.size() - 1;
+  }
+  bool literal(const char *word) {
+    size_t n = strlen(word);
+    if ((size_t)(end_ - cur_) < n || memcmp(cur_, word, n) != 0) return false;
+    cur_ += n;
+    return true;
+  }
+  static void put_utf8(std::string &out, uint32_t cp) {
+    if (cp < 0x80) {
+      out.push_back((char)cp);
+    } else if (cp < 0x800) {
+      out.push_back((char)(0xC0 | (cp >> 6)));
+      out.push_back((char)(0x80 | (cp & 0x3F)));
+    } else if (cp < 0x10000) {
+      out.push_back((char)(0xE0 | (cp >> 12)));
+      out.push_back((char)(0x80 | ((cp >> 6) & 0x3F)));
+      out.push_back((char)(0x80 | (cp & 0x3F)));
+    } else {
+      out.push_back((char)(0xF0 | (cp >> 18)));
+      out.push_back((char)(0x80 | ((cp >> 12) & 0x3F)));
+      out.push_back((char)(0x80 | ((cp >> 6) & 0x3F)));
+      out.push_back((char)(0x80 | (cp & 0x3F)));
+    }
+  }
+  bool hex4(uint32_t &cp) {
+    if (end_ - cur_ < 4) return false;
+    cp = 0;
+    for (int i = 0; i < 4; ++i) {
+      char c = *cur_++;
+      int d = (c >= '0' && c <= '9') ? c - '0' : (c >= 'a' && c <= 'f') ? c - 'a' + 10
+                                                : (c >= 'A' && c <= 'F') ? c - 'A' + 10 : -1;
+      if (d < 0) return false;
+      cp = cp * 16 + (uint32_t)d;
+    }
+    return true;
+  }
+  // Reads a string token (cur_ at the opening quote) into `out`.
+  bool read_string(std::string &out) {
+    ++cur_;
+    while (cur_ < end_) {
+      unsigned char c = (unsigned char)*cur_++;
+      if (c == '"') return true;
+      if (c < 0x20) return false;  // raw control characters are not allowed
+      if (c != '\\') { out.push_back((char)c); continue; }
+      if (cur_ >= end_) return false;
+      char esc = *cur_++;
+      switch (esc) {
+        case '"': case '\\': case '/': out.push_back(esc); break;
+        case 'b': out.push_back('\b'); break;
+        case 'f': out.push_back('\f'); break;
+        case 'n': out.push_back('\n'); break;
+        case 'r': out.push_back('\r'); break;
+        case 't': out.push_back('\t'); break;
         case 'u': {
-          if (e_ - p_ < 4) return fail("bad \\u");
-          unsigned v = (unsigned)strtoul(std::string(p_, 4).c_str(), nullptr, 16);
-          p_ += 4;
-          s.push_back(v < 0x80 ? (char)v : '?');
+          uint32_t cp;
+          if (!hex4(cp)) return false;
+          if (cp >= 0xD800 && cp < 0xDC00) {  // high surrogate: a low one must follow
+            uint32_t lo;
+            if (end_ - cur_ < 2 || cur_[0] != '\\' || cur_[1] != 'u') return false;
+            cur_ += 2;
+            if (!hex4(lo) || lo < 0xDC00 || lo >= 0xE000) return false;
+            cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+          } else if (cp >= 0xDC00 && cp < 0xE000) {
+            return false;
+          }
+          put_utf8(out, cp);
           break;
         }
-        default: s.push_back(x);
+        default: return false;
       }
     }
-    if (p_ >= e_) return fail("unterminated string");
-    ++p_;
+    return false;
   }
-  void value(Json &v, int depth) {
-    if (depth > 64) return fail("nesting too deep");
-    ws();
-    if (p_ >= e_) return fail("unexpected end");
-    char c = *p_;
-    if (c == '{') {
-      v.kind = Json::OBJ;
-      ++p_;
-      ws();
-      if (p_ < e_ && *p_ == '}') { ++p_; return; }
-      while (ok_) {
-        ws();
-        std::string k;
-        str(k);
-        ws();
-        if (p_ >= e_ || *p_ != ':') return fail("expected ':'");
-        ++p_;
-        Json child;
-        value(child, depth + 1);
-        v.obj.emplace_back(std::move(k), std::move(child));
-        ws();
-        if (p_ < e_ && *p_ == ',') { ++p_; continue; }
-        if (p_ < e_ && *p_ == '}') { ++p_; return; }
-        return fail("expected ',' or '}'");
-      }
-      return;
+  // Number per the JSON grammar: -? (0 | [1-9][0-9]*) (.[0-9]+)? ([eE][+-]?[0-9]+)?
+  int parse_number() {
+    const char *s = cur_;
+    auto digits = [&]() {
+      const char *d = cur_;
+      while (cur_ < end_ && *cur_ >= '0' && *cur_ <= '9') ++cur_;
+      return cur_ > d;
+    };
+    if (cur_ < end_ && *cur_ == '-') ++cur_;
+    if (cur_ < end_ && *cur_ == '0') ++cur_;
+    else if (!digits()) return error("malformed number");
+    if (cur_ < end_ && *cur_ == '.') { ++cur_; if (!digits()) return error("malformed number"); }
+    if (cur_ < end_ && (*cur_ == 'e' || *cur_ == 'E')) {
+      ++cur_;
+      if (cur_ < end_ && (*cur_ == '+' || *cur_ == '-')) ++cur_;
+      if (!digits()) return error("malformed number");
     }
-    if (c == '[') {
-      v.kind = Json::ARR;
-      ++p_;
-      ws();
-      if (p_ < e_ && *p_ == ']') { ++p_; return; }
-      while (ok_) {
-        Json child;
-        value(child, depth + 1);
-        v.arr.push_back(std::move(child));
-        ws();
-        if (p_ < e_ && *p_ == ',') { ++p_; continue; }
-        if (p_ < e_ && *p_ == ']') { ++p_; return; }
-        return fail("expected ',' or ']'");
-      }
-      return;
+    const std::string lexeme(s, cur_);  // strtod must not read past the token
+    int n = add(JsonRef::Number);
+    nodes_[(size_t)n].value = strtod(lexeme.c_str(), nullptr);
+    return n;
+  }
+  int parse_value(int depth) {
+    if (depth > 64) return error("nesting deeper than 64 levels");
+    skip_space();
+    if (cur_ >= end_) return error("unexpected end of input");
+    const char c = *cur_;
+    if (c == '"') {
+      std::string t;
+      if (!read_string(t)) return error("malformed string");
+      int n = add(JsonRef::String);
+      nodes_[(size_t)n].text = std::move(t);
+      return n;
     }
-    if (c == '"') { v.kind = Json::STR; return str(v.str); }
-    if (e_ - p_ >= 4 && !memcmp(p_, "true", 4)) { v.kind = Json::BOOL; v.b = true; p_ += 4; return; }
-    if (e_ - p_ >= 5 && !memcmp(p_, "false", 5)) { v.kind = Json::BOOL; p_ += 5; return; }
-    if (e_ - p_ >= 4 && !memcmp(p_, "null", 4)) { p_ += 4; return; }
-    // number: copy the lexeme so strtod never reads past the buffer
-    const char *q = p_;
-    while (q < e_ && (strchr("+-0123456789.eE", *q) != nullptr)) ++q;
-    if (q == p_) return fail("expected value");
-    std::string lex(p_, q);
-    char *stop = nullptr;
-    v.num = strtod(lex.c_str(), &stop);
-    if (stop != lex.c_str() + lex.size()) return fail("bad number");
-    v.kind = Json::NUM;
-    p_ = q;
+    if (c == '{' || c == '[') {
+      const bool obj = c == '{';
+      const char close = obj ? '}' : ']';
+      int n = add(obj ? JsonRef::Object : JsonRef::Array);
+      ++cur_;
+      skip_space();
+      if (cur_ < end_ && *cur_ == close) { ++cur_; return n; }
+      for (;;) {
+        if (obj) {
+          skip_space();
+          if (cur_ >= end_ || *cur_ != '"') return error("object key must be a string");
+          std::string key;
+          if (!read_string(key)) return error("malformed object key");
+          int k = add(JsonRef::String);
+          nodes_[(size_t)k].text = std::move(key);
+          nodes_[(size_t)n].kids.push_back(k);
+          skip_space();
+          if (cur_ >= end_ || *cur_ != ':') return error("expected ':' after an object key");
+          ++cur_;
+        }
+        int v = parse_value(depth + 1);
+        if (v < 0) return -1;
+        nodes_[(size_t)n].kids.push_back(v);
+        skip_space();
+        if (cur_ < end_ && *cur_ == ',') { ++cur_; continue; }
+        if (cur_ < end_ && *cur_ == close) { ++cur_; return n; }
+        return error(obj ? "expected ',' or '}'" : "expected ',' or ']'");
+      }
+    }
+    if (literal("true")) { int n = add(JsonRef::Bool); nodes_[(size_t)n].flag = true; return n; }
+    if (literal("false")) return add(JsonRef::Bool);
+    if (literal("null")) return add(JsonRef::Null);
+    if (c == '-' || (c >= '0' && c <= '9')) return parse_number();
+    return error("unexpected character");
   }
 };
+
+JsonRef::Type JsonRef::type() const { return *this ? doc_->nodes_[(size_t)node_].type : None; }
+bool JsonRef::boolean() const { return is(Bool) && doc_->nodes_[(size_t)node_].flag; }
+double JsonRef::number() const { return is(Number) ? doc_->nodes_[(size_t)node_].value : 0.0; }
+const std::string &JsonRef::text() const { return is(String) ? doc_->nodes_[(size_t)node_].text : JsonDoc::empty(); }
+size_t JsonRef::size() const {
+  if (is(Array)) return doc_->nodes_[(size_t)node_].kids.size();
+  if (is(Object)) return doc_->nodes_[(size_t)node_].kids.size() / 2;
+  return 0;
+}
+JsonRef JsonRef::item(size_t i) const {
+  if (!is(Array) || i >= size()) return JsonRef();
+  return JsonRef(doc_, doc_->nodes_[(size_t)node_].kids[i]);
+}
+JsonRef JsonRef::operator[](const char *key) const {
+  if (!is(Object)) return JsonRef();
+  const std::vector<int> &k = doc_->nodes_[(size_t)node_].kids;
+  for (size_t i = 0; i + 1 < k.size(); i += 2)
+    if (doc_->nodes_[(size_t)k[i]].text == key) return JsonRef(doc_, k[i + 1]);
+  return JsonRef();
+}
 
 // ------------------------------------------------------------------ SHA-256 (host)
 class Sha256 {

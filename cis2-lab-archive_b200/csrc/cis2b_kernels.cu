@@ -12,6 +12,7 @@
 //   * order-free steps (max, argmax with lowest-index ties, element-wise
 //     maps) use parallel reductions with the reference's tie and NaN rules.
 // No tensor cores: their fp32 accumulation order is unspecified.
+#include "../../include/cis2b.h"
 #include "cis2b_kernels.h"
 #include "cis2b_pinned.cuh"
 #include "cis2b_sha256.cuh"
@@ -1918,11 +1919,14 @@ void launch_sample_gumbel(const float *logits, int V, int rows, const int32_t *s
 // that loads the library holds until the process exits.  Sized for rows of
 // up to CIS2B_STATIC_SAMPLE_MAX logits: the sampler needs 5 floats per logit
 // (probabilities, two key/index buffer pairs) plus one int for the position.
-constexpr int kStaticSampleMax = 262144;
+constexpr int kStaticSampleMax = CIS2B_STATIC_SAMPLE_MAX;
+static_assert(kStaticSampleMax == 262144, "the error text below and the header state 262144");
 static __device__ __align__(256) float g_sample_scratch[5 * kStaticSampleMax + 64];
 
 // The host-side name g_sample_scratch is not a device address; the address
-// is looked up once per device, with that device current.
+// is looked up once per device, with that device current, and kept for the
+// life of the process (a device reset that destroys the primary context
+// leaves it stale; the header says so).
 static float *g_scratch_addr[64];
 static std::mutex g_scratch_mu;
 

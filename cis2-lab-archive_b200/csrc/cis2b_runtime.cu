@@ -186,52 +186,71 @@ struct TensorRef {
 
 // ------------------------------------------------------------------ loading
 
+// Shortest decimal that reads back as the same f64, in positional notation
+// (how Rust's Display prints an f64 in the gate's reasons).
+std::string f64_display(double x) {
+  char buf[512];
+  for (int p = 1; p <= 17; ++p) {
+    snprintf(buf, sizeof buf, "%.*g", p, x);
+    if (strtod(buf, nullptr) == x) break;
+  }
+  if (!strchr(buf, 'e')) return buf;
+  for (int d = 0; d <= 340; ++d) {  // no exponent form: widen the fixed form until it round-trips
+    snprintf(buf, sizeof buf, "%.*f", d, x);
+    if (strtod(buf, nullptr) == x) break;
+  }
+  return buf;
+}
+
 // The architecture gate: the checkpoints whose arithmetic this decoder
-// reproduces, and a refusal by name for the rest (code/cis2-fp/src/main.rs:
-// 545-644, which refuses with CIS2_REF_UNSUPPORTED and exit status 2).  The
-// keys and reasons follow that gate; model_type "qwen3" is admitted as well,
-// because the lab's Qwen3 port of the C++ path decodes it
-// (labs/w1x-qwen3/scripts/qwen3-port.diff), and for it an explicit head_dim
-// is the one used (Qwen3-0.6B declares 128 against a derived 64).
-bool gate_architecture(const Json &cfg, std::string &why) {
-  auto present = [&](const char *k) {
-    const Json *j = cfg.get(k);
-    return j && j->kind != Json::NUL;
-  };
+// reproduces, and a refusal by name for the rest, with the reference's keys,
+// order and reason texts (code/cis2-fp/src/main.rs:545-644, which refuses
+// with CIS2_REF_UNSUPPORTED and exit status 2).  With CIS2B_GATE_QWEN3_PORT
+// model_type "qwen3" is admitted as well, because the lab's Qwen3 port of the
+// C++ path decodes it (labs/w1x-qwen3/scripts/qwen3-port.diff); for it the
+// explicit head_dim is the one used (Qwen3-0.6B declares 128 against a
+// derived 64).
+bool gate_architecture(JsonRef cfg, int gate, std::string &why) {
+  auto present = [&](const char *k) { return cfg[k] && !cfg[k].is(JsonRef::Null); };
+  const bool qwen3_port = gate == CIS2B_GATE_QWEN3_PORT;
   std::string mt;
-  if (const Json *j = cfg.get("model_type"); j && j->kind == Json::STR) {
-    mt = j->str;
-    if (mt != "llama" && mt != "qwen2" && mt != "qwen3") {
-      why = "model_type=\"" + mt + "\" is not in the CIS-2 specified subset [\"llama\", \"qwen2\", \"qwen3\"]";
+  if (cfg["model_type"].is(JsonRef::String)) {
+    mt = cfg["model_type"].text();
+    if (mt != "llama" && mt != "qwen2" && !(qwen3_port && mt == "qwen3")) {
+      why = "model_type=\"" + mt + "\" is not in the CIS-2 specified subset " +
+            (qwen3_port ? "[\"llama\", \"qwen2\", \"qwen3\"]" : "[\"llama\", \"qwen2\"]");
       return false;
     }
   }
-  if (const Json *j = cfg.get("torch_dtype"); j && j->kind == Json::STR && j->str != "bfloat16") {
-    why = "torch_dtype=\"" + j->str + "\"; CIS-2 pins bf16-on-disk weights (\u00a73.5)";
+  if (cfg["torch_dtype"].is(JsonRef::String) && cfg["torch_dtype"].text() != "bfloat16") {
+    why = "torch_dtype=\"" + cfg["torch_dtype"].text() + "\"; CIS-2 pins bf16-on-disk weights (\u00a73.5)";
     return false;
   }
-  const Json *h = cfg.get("hidden_size"), *nh = cfg.get("num_attention_heads");
-  if (h && nh && h->kind == Json::NUM && nh->kind == Json::NUM) {
-    if (nh->num == 0) { why = "num_attention_heads=0"; return false; }
-    const long derived = (long)h->num / (long)nh->num;
+  const JsonRef h = cfg["hidden_size"], nh = cfg["num_attention_heads"];
+  if (h.is(JsonRef::Number) && nh.is(JsonRef::Number)) {
+    if (nh.number() == 0) { why = "num_attention_heads=0"; return false; }
+    const long derived = (long)h.number() / (long)nh.number();
     long used = derived;
-    if (const Json *j = cfg.get("head_dim"); j && j->kind == Json::NUM) {
-      if ((long)j->num != derived && mt != "qwen3") {
-        why = "config declares head_dim=" + std::to_string((long)j->num) +
-              " but hidden_size/num_attention_heads=" + std::to_string(derived) +
-              "; only the qwen3 port uses an explicit head_dim";
+    if (const JsonRef j = cfg["head_dim"]; j.is(JsonRef::Number)) {
+      if ((long)j.number() != derived && !(qwen3_port && mt == "qwen3")) {
+        why = "config declares head_dim=" + std::to_string((long)j.number()) +
+              " but this implementation derives hidden_size/num_attention_heads=" + std::to_string(derived) +
+              "; the decode path uses the derived value, so the explicit one would be silently ignored";
         return false;
       }
-      used = (long)j->num;
+      used = (long)j.number();
     }
-    if (used % 2 != 0) { why = "head_dim=" + std::to_string(used) + " is odd; RoPE pairs require even"; return false; }
+    if (used % 2 != 0) {
+      why = "derived head_dim=" + std::to_string(used) + " is odd; RoPE pairs require even";
+      return false;
+    }
   }
-  if (const Json *j = cfg.get("partial_rotary_factor"); j && j->kind == Json::NUM && j->num != 1.0) {
-    why = "partial_rotary_factor is not 1; only full rotary is specified";
+  if (const JsonRef j = cfg["partial_rotary_factor"]; j.is(JsonRef::Number) && j.number() != 1.0) {
+    why = "partial_rotary_factor=" + f64_display(j.number()) + "; only full rotary is specified";
     return false;
   }
   if (present("rope_scaling")) { why = "rope_scaling is set; only unscaled RoPE is specified"; return false; }
-  if (const Json *j = cfg.get("use_sliding_window"); j && j->kind == Json::BOOL && j->b) {
+  if (cfg["use_sliding_window"].boolean()) {
     why = "use_sliding_window=true; only full causal attention is specified";
     return false;
   }
@@ -242,8 +261,8 @@ bool gate_architecture(const Json &cfg, std::string &why) {
   for (const char *k : {"attention_multiplier", "embedding_multiplier", "residual_multiplier", "logits_scaling",
                         "attn_logit_softcapping", "final_logit_softcapping", "query_pre_attn_scalar"})
     if (present(k)) {
-      why = std::string(k) + " is set; this decoder uses rsqrt(head_dim) attention scaling and no logit scaling, "
-            "so the result would be silently wrong";
+      why = std::string(k) + " is set; this implementation hardcodes rsqrt(head_dim) attention scaling and no "
+            "logit scaling, so the result would be silently wrong";
       return false;
     }
   for (const char *k : {"num_local_experts", "num_experts", "n_routed_experts", "moe_intermediate_size"})
@@ -255,8 +274,10 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   if (!dir_c) return fail(CIS2B_ERR_ARG, "weights_dir is NULL");
   cis2b_opts o{};
   if (opts) o = *opts;
-  for (int i = 0; i < 5; ++i)
+  for (int i = 0; i < 4; ++i)
     if (o.reserved[i] != 0) return fail(CIS2B_ERR_ARG, "cis2b_opts.reserved must be zero");
+  if (o.arch_gate != CIS2B_GATE_REFERENCE && o.arch_gate != CIS2B_GATE_QWEN3_PORT)
+    return fail(CIS2B_ERR_ARG, "unknown architecture gate");
   if (o.reduction != CIS2B_REDUCTION_SEQUENTIAL && o.reduction != CIS2B_REDUCTION_TREE)
     return fail(CIS2B_ERR_ARG, "unknown reduction mode");
   if (o.max_positions < 0) return fail(CIS2B_ERR_ARG, "max_positions < 0");
@@ -271,13 +292,14 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   const std::string dir(dir_c);
   std::string wbytes, tok, cfgtxt;
   if (!read_file(dir + "/config.json", cfgtxt)) return fail(CIS2B_ERR_IO, "cannot read " + dir + "/config.json");
-  Json cfg;
+  JsonDoc cfg_doc;
   std::string jerr;
-  if (!JsonParser(cfgtxt.data(), cfgtxt.data() + cfgtxt.size()).parse(cfg, jerr) || cfg.kind != Json::OBJ)
+  if (!cfg_doc.parse(cfgtxt.data(), cfgtxt.data() + cfgtxt.size(), jerr) || !cfg_doc.root().is(JsonRef::Object))
     return fail(CIS2B_ERR_IO, "config.json: " + (jerr.empty() ? std::string("not an object") : jerr));
+  const JsonRef cfg = cfg_doc.root();
   {
     std::string why;
-    if (!gate_architecture(cfg, why)) return fail(CIS2B_ERR_CONFIG, why);
+    if (!gate_architecture(cfg, o.arch_gate, why)) return fail(CIS2B_ERR_CONFIG, why);
   }
   if (!read_file(dir + "/model.safetensors", wbytes))
     return fail(CIS2B_ERR_IO, "cannot read " + dir + "/model.safetensors");
@@ -294,9 +316,8 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
 
   // ---- config (cis2_host.cpp:97-117, qwen3-port.diff:109-110)
   auto need = [&](const char *k, double &v) -> bool {
-    const Json *j = cfg.get(k);
-    if (!j || j->kind != Json::NUM) return false;
-    v = j->num;
+    if (!cfg[k].is(JsonRef::Number)) return false;
+    v = cfg[k].number();
     return true;
   };
   double hid, inter, nl, nh, nkv, voc, eps, theta;
@@ -309,9 +330,9 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   if (m->NH <= 0 || m->NKV <= 0 || m->H <= 0 || m->I <= 0 || m->L <= 0 || m->V <= 0)
     return fail(CIS2B_ERR_CONFIG, "non-positive model dimension");
   m->HD = m->H / m->NH;
-  if (const Json *j = cfg.get("head_dim"); j && j->kind == Json::NUM) m->HD = (int)j->num;
+  if (cfg["head_dim"].is(JsonRef::Number)) m->HD = (int)cfg["head_dim"].number();
   bool tied = true;
-  if (const Json *j = cfg.get("tie_word_embeddings")) tied = (j->kind == Json::BOOL) ? j->b : true;
+  if (cfg["tie_word_embeddings"].is(JsonRef::Bool)) tied = cfg["tie_word_embeddings"].boolean();
   m->QD = m->NH * m->HD;
   m->KVD = m->NKV * m->HD;
   if (m->NH % m->NKV) return fail(CIS2B_ERR_CONFIG, "num_attention_heads % num_key_value_heads != 0");
@@ -328,20 +349,21 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   uint64_t hlen = 0;
   for (int i = 0; i < 8; ++i) hlen |= (uint64_t)(uint8_t)wbytes[i] << (8 * i);
   if (8 + hlen > wbytes.size()) return fail(CIS2B_ERR_IO, "safetensors header length out of range");
-  Json hdr;
-  if (!JsonParser(wbytes.data() + 8, wbytes.data() + 8 + hlen).parse(hdr, jerr) || hdr.kind != Json::OBJ)
-    return fail(CIS2B_ERR_IO, "safetensors header: " + jerr);
+  JsonDoc hdr_doc;
+  if (!hdr_doc.parse(wbytes.data() + 8, wbytes.data() + 8 + hlen, jerr) || !hdr_doc.root().is(JsonRef::Object))
+    return fail(CIS2B_ERR_IO, "safetensors header: " + (jerr.empty() ? std::string("not an object") : jerr));
+  const JsonRef hdr = hdr_doc.root();
   const size_t data0 = 8 + hlen, data_len = wbytes.size() - data0;
   auto find = [&](const std::string &name, TensorRef &t) -> bool {
-    const Json *j = hdr.get(name.c_str());
-    if (!j) return false;
-    const Json *dt = j->get("dtype"), *sh = j->get("shape"), *of = j->get("data_offsets");
-    if (!dt || !sh || !of || of->arr.size() != 2) return false;
-    t.dtype = dt->str;
+    const JsonRef j = hdr[name.c_str()];
+    const JsonRef dt = j["dtype"], sh = j["shape"], of = j["data_offsets"];
+    if (!dt.is(JsonRef::String) || !sh.is(JsonRef::Array) || !of.is(JsonRef::Array) || of.size() != 2)
+      return false;
+    t.dtype = dt.text();
     t.shape.clear();
-    for (auto &x : sh->arr) t.shape.push_back((size_t)x.num);
-    t.begin = (size_t)of->arr[0].num;
-    t.end = (size_t)of->arr[1].num;
+    for (size_t i = 0; i < sh.size(); ++i) t.shape.push_back((size_t)sh.item(i).number());
+    t.begin = (size_t)of.item(0).number();
+    t.end = (size_t)of.item(1).number();
     return true;
   };
   struct Piece { size_t dst_off; const uint8_t *src; size_t bytes; };
@@ -1336,6 +1358,7 @@ int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temper
                     uint64_t position, uint32_t *out_index) {
   if (!logits || !out_index || n <= 0) return fail(CIS2B_ERR_ARG, "bad argument");
   if (!(temperature > 0.0f) || !(top_p > 0.0f && top_p <= 1.0f)) return fail(CIS2B_ERR_ARG, "bad sampler parameters");
+  if (position > 0x7fffffffull) return fail(CIS2B_ERR_ARG, "position must be below 2^31");
   CU(cudaSetDevice(device));
   Scoped<float> dl, scr;
   Scoped<uint32_t> nx;
@@ -1350,6 +1373,20 @@ int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temper
   launch_sample(dl.p, n, 1, nullptr, 0, temperature, top_p, seed, dp.p, scr.p, nx.p, 0);
   CU_LAUNCHED();
   CU(cudaMemcpy(out_index, nx.p, 4, cudaMemcpyDeviceToHost));
+  return CIS2B_OK;
+}
+
+int cis2b_op_argmax(int32_t device, const float *logits, int32_t rows, int32_t n, uint32_t *out_index) {
+  if (!logits || !out_index || rows <= 0 || n <= 0) return fail(CIS2B_ERR_ARG, "bad argument");
+  CU(cudaSetDevice(device));
+  Scoped<float> dl;
+  Scoped<uint32_t> nx;
+  CU(cudaMalloc(&dl.p, 4 * (size_t)rows * n));
+  CU(cudaMalloc(&nx.p, 4 * (size_t)rows));
+  CU(cudaMemcpy(dl.p, logits, 4 * (size_t)rows * n, cudaMemcpyHostToDevice));
+  launch_argmax(dl.p, n, rows, nullptr, 0, nx.p, 0);
+  CU_LAUNCHED();
+  CU(cudaMemcpy(out_index, nx.p, 4 * (size_t)rows, cudaMemcpyDeviceToHost));
   return CIS2B_OK;
 }
 

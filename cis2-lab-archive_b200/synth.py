@@ -51,6 +51,7 @@ class ModelShape:
     qk_norm: bool = False         # per-head q_norm/k_norm tensors (Qwen3)
     qkv_bias: bool = False        # q/k/v bias tensors (Qwen2 family)
     model_type: str = "llama"
+    coverage: bool = False        # lm_head rows rebuilt for the tie / subnormal clauses (below)
 
     @property
     def hd(self) -> int:
@@ -83,7 +84,22 @@ MODELS: dict[str, ModelShape] = {
     # Mid-size: SmolLM2 widths with fewer layers and a smaller vocab, so the
     # oracle finishes in seconds while the kernels see realistic K and N.
     "mid": ModelShape("mid", 576, 1536, 3, 9, 3, 4096, "1e-05", "100000", True, 11),
+    # Constructed coverage vector (labs/w1x-coverage/plans/2026-10-16-w1x-coverage-PLAN.md:8-16):
+    # hidden 64, 2 heads (head_dim 32), 2 layers, inter 128, vocab 32, untied.
+    "coverage": ModelShape("coverage", 64, 128, 2, 2, 2, 32, "1e-05", "10000", False, 20261016,
+                           coverage=True),
 }
+
+# The coverage model's clauses.  Rows TIE_A and TIE_B of lm_head are the
+# same +-2.0 row, so every step's logits tie exactly between them and the
+# strict-first argmax (code/cis2-fp/src/main.rs:1161-1169) must pick TIE_A.
+# Row SUB holds one non-zero weight, +-2^-126 (the smallest normal bf16), at
+# a column whose final-norm value at the last prompt position lies in
+# [0.25, 0.75] in magnitude: its step-0 logit is then a positive subnormal,
+# which the pinned FTZ/DAZ environment flushes to +0 before the witness
+# hashes it (spec §1.3, code/cis2-fp/gpu/cis2_fpenv.h:62-135).
+COVERAGE_TIE_A, COVERAGE_TIE_B, COVERAGE_SUB = 5, 17, 29
+COVERAGE_PROMPT_SEED, COVERAGE_PROMPT_LEN = 20261016, 4
 
 
 @dataclass(frozen=True)
@@ -222,6 +238,85 @@ def sha256_file(path: str) -> bytes:
     return h.digest()
 
 
+def _widen(a: np.ndarray) -> np.ndarray:
+    return (a.astype(np.uint32) << np.uint32(16)).view(np.float32).astype(np.float64)
+
+
+def _final_hidden_f64(m: ModelShape, t: dict[str, np.ndarray], ids: np.ndarray) -> np.ndarray:
+    """Final-norm output of the last of `ids` in float64: the plain Llama
+    forward (RMSNorm, rotate-half RoPE, causal GQA attention, SwiGLU) with no
+    pinned order.  Only its signs and rough magnitudes are used, to place the
+    coverage rows; nothing is checked against it."""
+    H, HD, NH, NKV = m.hidden, m.hd, m.heads, m.kv_heads
+    eps, theta = float(m.eps), float(m.theta)
+
+    def rms(x, w):
+        return x / np.sqrt((x * x).mean(-1, keepdims=True) + eps) * w
+
+    def W(name, rows, cols):
+        return _widen(t[name]).reshape(rows, cols)
+
+    P = len(ids)
+    h = W("model.embed_tokens.weight", m.vocab, H)[ids.astype(np.int64)]
+    half = HD // 2
+    ang = np.arange(P)[:, None] * theta ** (-np.arange(half) * 2.0 / HD)[None, :]
+    cos, sin = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+
+    def rope(x):  # [P, heads, HD]
+        x1, x2 = x[..., :half], x[..., half:]
+        return np.concatenate([x1 * cos - x2 * sin, x2 * cos + x1 * sin], axis=-1)
+
+    for li in range(m.layers):
+        p = f"model.layers.{li}."
+        x = rms(h, _widen(t[p + "input_layernorm.weight"]))
+        q = rope((x @ W(p + "self_attn.q_proj.weight", m.q_dim, H).T).reshape(P, NH, HD))
+        k = rope((x @ W(p + "self_attn.k_proj.weight", m.kv_dim, H).T).reshape(P, NKV, HD))
+        v = (x @ W(p + "self_attn.v_proj.weight", m.kv_dim, H).T).reshape(P, NKV, HD)
+        att = np.zeros((P, NH, HD))
+        for hh in range(NH):
+            g = hh // (NH // NKV)
+            s = q[:, hh, :] @ k[:, g, :].T / np.sqrt(HD)
+            s = np.where(np.tril(np.ones((P, P), bool)), s, -np.inf)
+            e = np.exp(s - s.max(-1, keepdims=True))
+            att[:, hh, :] = (e / e.sum(-1, keepdims=True)) @ v[:, g, :]
+        h = h + att.reshape(P, m.q_dim) @ W(p + "self_attn.o_proj.weight", H, m.q_dim).T
+        x = rms(h, _widen(t[p + "post_attention_layernorm.weight"]))
+        gt = x @ W(p + "mlp.gate_proj.weight", m.inter, H).T
+        up = x @ W(p + "mlp.up_proj.weight", m.inter, H).T
+        h = h + (gt / (1.0 + np.exp(-gt)) * up) @ W(p + "mlp.down_proj.weight", H, m.inter).T
+    return rms(h, _widen(t["model.norm.weight"]))[-1]
+
+
+def coverage_prompt() -> np.ndarray:
+    return random_prompts("coverage", 1, COVERAGE_PROMPT_LEN, COVERAGE_PROMPT_SEED)[0]
+
+
+def _apply_coverage_rows(m: ModelShape, tensors: list) -> None:
+    t = {name: arr for name, _, arr in tensors}
+    x = _final_hidden_f64(m, t, coverage_prompt())
+    lm = t["lm_head.weight"].reshape(m.vocab, m.hidden)
+    tie = np.where(x >= 0, 0x4000, 0xC000).astype(np.uint16)       # +-2.0 in bf16
+    lm[COVERAGE_TIE_A] = tie
+    lm[COVERAGE_TIE_B] = tie
+    mag = np.abs(x)
+    col = int(np.argmin(np.where((mag >= 0.25) & (mag <= 0.75), np.abs(mag - 0.5), np.inf)))
+    assert 0.25 <= mag[col] <= 0.75, "no column with |x| in [0.25, 0.75]"
+    lm[COVERAGE_SUB] = 0
+    lm[COVERAGE_SUB, col] = 0x0080 if x[col] > 0 else 0x8080        # +-2^-126, product sign +
+
+
+def coverage_column(weights_dir: str) -> int:
+    """Column of the coverage model's single non-zero weight in row SUB."""
+    with open(os.path.join(weights_dir, "model.safetensors"), "rb") as f:
+        (hl,) = struct.unpack("<Q", f.read(8))
+        hdr = json.loads(f.read(hl))
+        b, e = hdr["lm_head.weight"]["data_offsets"]
+        f.seek(8 + hl + b)
+        lm = np.frombuffer(f.read(e - b), dtype="<u2").reshape(hdr["lm_head.weight"]["shape"])
+    (nz,) = np.nonzero(lm[COVERAGE_SUB])
+    return int(nz[0])
+
+
 def ensure_model(m: ModelShape | str, root: str) -> str:
     """Write (once) the three artifacts of `m` under root/<name>/ and return the dir."""
     if isinstance(m, str):
@@ -233,6 +328,8 @@ def ensure_model(m: ModelShape | str, root: str) -> str:
     os.makedirs(d, exist_ok=True)
     specs = tensor_specs(m)
     tensors = [(name, shape, make_tensor(m, i, shape, kind)) for i, (name, shape, kind) in enumerate(specs)]
+    if m.coverage:
+        _apply_coverage_rows(m, tensors)
     write_safetensors(os.path.join(d, "model.safetensors"), tensors)
     with open(os.path.join(d, "config.json"), "w") as f:
         f.write(config_json_text(m))

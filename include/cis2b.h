@@ -46,11 +46,22 @@ extern "C" {
 
 typedef struct cis2b_model cis2b_model;
 
+/* Architecture gate run on config.json before the weights are read.
+ * CIS2B_GATE_REFERENCE (0, the default): the Rust reference's gate
+ *   (code/cis2-fp/src/main.rs:545-644) key for key and reason for reason:
+ *   model_type llama or qwen2, head_dim equal to hidden/heads, ...
+ * CIS2B_GATE_QWEN3_PORT (1): the same, but model_type qwen3 is admitted with
+ *   its explicit head_dim, as the lab's Qwen3 port of the C++ path decodes it
+ *   (labs/w1x-qwen3/scripts/qwen3-port.diff). */
+#define CIS2B_GATE_REFERENCE 0
+#define CIS2B_GATE_QWEN3_PORT 1
+
 typedef struct {
   int32_t device;        /* CUDA device ordinal */
   int32_t reduction;     /* CIS2B_REDUCTION_* */
   int32_t max_positions; /* prompt + generated positions per sequence; 0 = 4096 */
-  int32_t reserved[5];   /* must be zero */
+  int32_t arch_gate;     /* CIS2B_GATE_* */
+  int32_t reserved[4];   /* must be zero */
 } cis2b_opts;
 
 /* Sampled-mode parameters.  Pass NULL for greedy.
@@ -183,7 +194,13 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
 int cis2b_op_sha256_stream(int32_t device, const uint8_t *prefix, size_t prefix_len,
                            const uint32_t *words, uint32_t chunk_words, uint32_t n_chunks,
                            uint8_t *out_digests);
-/* E23 sampler on one logits row. */
+/* Greedy token selection on `rows` logits rows of n values each, through
+ * the kernel the decode steps use: the first index of the strict maximum
+ * (code/cis2-fp/src/main.rs:1161-1169; gpu/cis2_model.h:764-774), so an
+ * exact tie -- +0 against -0 included -- keeps the lower index, a NaN at
+ * index 0 selects 0 and a NaN elsewhere is never selected. */
+int cis2b_op_argmax(int32_t device, const float *logits, int32_t rows, int32_t n, uint32_t *out_index);
+/* E23 sampler on one logits row; position < 2^31. */
 int cis2b_op_sample(int32_t device, const float *logits, int32_t n, float temperature, float top_p,
                     uint64_t seed, uint64_t position, uint32_t *out_index);
 /* Seeded Gumbel-max ("CIS2-SAMPLE-1") draw on one logits row; step is the
@@ -204,14 +221,21 @@ int cis2b_op_sample_gumbel(int32_t device, const float *logits, int32_t n, float
  *   d_logits     device pointer to n fp32 logits, 1 <= n <= CIS2B_STATIC_SAMPLE_MAX
  *   d_out_index  device pointer to one uint32, written with the drawn index
  *   stream       cudaStream_t to run on (NULL: the legacy default stream)
+ *   position     < 2^31
  * Makes `device` current on the calling thread.  The first call on a device
- * looks up the array's device address; make that first call before any
- * stream capture.  The call is asynchronous: the index is valid once
- * `stream` has reached it.  All calls share the one array and it keeps the
- * last call's contents (every element the sampler reads it writes first),
- * so calls whose work overlaps on the GPU -- two streams, or two threads --
- * race and must be ordered by the caller.  Sizes above the maximum are
- * rejected with CIS2B_ERR_ARG.  Same result as cis2b_op_sample. */
+ * looks up the array's device address and keeps it; make that first call
+ * before any stream capture.  A device reset that destroys the primary
+ * context (cudaDeviceReset) makes the kept address stale: do not call this
+ * entry point again in that process afterwards.  The call is asynchronous:
+ * the index is valid once `stream` has reached it.  All calls on one device
+ * in one process share the one array, whichever model handle or thread
+ * makes them, and it keeps the last call's contents (every element the
+ * sampler reads it writes first), so calls whose work overlaps on the GPU --
+ * two streams, or two threads -- race and must be ordered by the caller.
+ * Only this entry point uses the array: it never races with cis2b_generate,
+ * cis2b_verify or the other entry points, and separate processes each have
+ * their own copy.  Sizes above the maximum are rejected with CIS2B_ERR_ARG.
+ * Same result as cis2b_op_sample. */
 #define CIS2B_STATIC_SAMPLE_MAX 262144
 int cis2b_op_sample_static(int32_t device, const float *d_logits, int32_t n, float temperature, float top_p,
                            uint64_t seed, uint64_t position, uint32_t *d_out_index, void *stream);

@@ -30,7 +30,8 @@ import pyoracle  # noqa: E402
 SAMPLE = {"seed": 20261201, "temperature": 0.8, "top_p": 0.95}
 
 # name -> (model, prompts spec, gen, tree, sampled)
-#   prompts spec: ("workload", name, first, count) or ("random", seed, [lens])
+#   prompts spec: ("workload", name, first, count), ("workload_idx", name, [sequence indices])
+#   or ("random", seed, [lens])
 CASES = {
     "tiny_seq_greedy": ("tiny", ("random", 11, [1, 5, 9, 16]), 12, False, False),
     "tiny_tree_greedy": ("tiny", ("random", 11, [1, 5, 9, 16]), 12, True, False),
@@ -44,6 +45,10 @@ CASES = {
     "tiny_bias_seq": ("tiny_bias", ("random", 15, [5, 3]), 10, False, False),
     "mid_seq": ("mid", ("random", 16, [20, 37, 64]), 24, False, False),
     "mid_tree": ("mid", ("random", 16, [20, 37, 64]), 24, True, False),
+    # Constructed coverage vector: exact lm_head tie (rows 5 and 17) and a
+    # subnormal step-0 logit (row 29); the prompt is synth.coverage_prompt().
+    "coverage_seq": ("coverage", ("random", 20261016, [4]), 12, False, False),
+    "coverage_tree": ("coverage", ("random", 20261016, [4]), 12, True, False),
     # BASELINE configurations (full sizes; C5 on a seeded subset).
     "c1": ("smollm2", ("workload", "c1", 0, 1), 256, False, False),
     "c1_tree": ("smollm2", ("workload", "c1", 0, 1), 256, True, False),
@@ -51,6 +56,11 @@ CASES = {
     "c3": ("llama160m", ("workload", "c3", 0, 300), 128, False, False),
     "c4": ("qwen3_0p6b", ("workload", "c4", 0, 32), 256, False, True),
     "c5_subset": ("smollm2", ("workload", "c5", 0, 4), 1024, False, False),
+    # The sequences other ranks decode in the multi-GPU runs: C2 weak scaling
+    # gives rank r sequences 64r .. 64r+63 (r < 8); C5 strong scaling over 8
+    # GPUs gives rank r sequences 32r .. 32r+31, checked here at 32r + 5.
+    "c2_shards": ("smollm2", ("workload", "c2", 64, 448), 256, False, False),
+    "c5_spread": ("smollm2", ("workload_idx", "c5", [37, 69, 101, 133, 165, 197, 229]), 1024, False, False),
 }
 
 
@@ -58,6 +68,9 @@ def build_prompts(model: str, spec) -> list:
     if spec[0] == "workload":
         _, w, first, count = spec
         return list(synth.prompt_ids(w, n_seq=count, first=first))
+    if spec[0] == "workload_idx":
+        _, w, idx = spec
+        return [synth.prompt_ids(w, n_seq=1, first=i)[0] for i in idx]
     _, seed, lens = spec
     return [synth.random_prompts(model, 1, L, seed, first=i)[0] for i, L in enumerate(lens)]
 

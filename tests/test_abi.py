@@ -167,3 +167,140 @@ def test_last_error_is_thread_local(pkg):
     t.start()
     t.join()
     assert seen["msg"] == ""
+
+
+# ---------------------------------------------------------------- the reference's refusal suite
+
+def reference_root() -> str | None:
+    """The reference checkout: $CIS2_REFERENCE_ROOT, else `reference` beside
+    this repository; None when neither exists (as on a GPU box)."""
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    root = os.environ.get("CIS2_REFERENCE_ROOT") or os.path.join(os.path.dirname(here), "reference")
+    return root if os.path.isdir(os.path.join(root, "code", "cis2-fp")) else None
+
+
+def rust_gate_reason(cfg: dict) -> str | None:
+    """The Rust reference's gate restated (code/cis2-fp/src/main.rs:545-644):
+    the refusal reason it prints, or None when it admits the config."""
+    def u64(v):
+        return v if isinstance(v, int) and not isinstance(v, bool) and v >= 0 else None
+
+    mt = cfg.get("model_type")
+    if isinstance(mt, str) and mt not in ("llama", "qwen2"):
+        return f'model_type="{mt}" is not in the CIS-2 specified subset ["llama", "qwen2"]'
+    dt = cfg.get("torch_dtype")
+    if isinstance(dt, str) and dt != "bfloat16":
+        return f'torch_dtype="{dt}"; CIS-2 pins bf16-on-disk weights (\u00a73.5)'
+    h, nh = u64(cfg.get("hidden_size")), u64(cfg.get("num_attention_heads"))
+    if h is not None and nh is not None:
+        if nh == 0:
+            return "num_attention_heads=0"
+        derived = h // nh
+        ex = u64(cfg.get("head_dim"))
+        if ex is not None and ex != derived:
+            return (f"config declares head_dim={ex} but this implementation derives "
+                    f"hidden_size/num_attention_heads={derived}; the decode path uses the derived value, "
+                    "so the explicit one would be silently ignored")
+        if derived % 2:
+            return f"derived head_dim={derived} is odd; RoPE pairs require even"
+    prf = cfg.get("partial_rotary_factor")
+    if isinstance(prf, (int, float)) and not isinstance(prf, bool) and prf != 1.0:
+        return f"partial_rotary_factor={prf!r}; only full rotary is specified"
+    if cfg.get("rope_scaling") is not None:
+        return "rope_scaling is set; only unscaled RoPE is specified"
+    if cfg.get("use_sliding_window") is True:
+        return "use_sliding_window=true; only full causal attention is specified"
+    if cfg.get("quantization_config") is not None:
+        return "quantization_config is present; CIS-2 reads unquantized bf16 weights"
+    for k in ("attention_multiplier", "embedding_multiplier", "residual_multiplier", "logits_scaling",
+              "attn_logit_softcapping", "final_logit_softcapping", "query_pre_attn_scalar"):
+        if cfg.get(k) is not None:
+            return (f"{k} is set; this implementation hardcodes rsqrt(head_dim) attention scaling and no logit "
+                    "scaling, so the result would be silently wrong")
+    for k in ("num_local_experts", "num_experts", "n_routed_experts", "moe_intermediate_size"):
+        if cfg.get(k) is not None:
+            return f"{k} is set; MoE routing is not specified"
+    return None
+
+
+def refusal_fixture_dirs() -> list[str]:
+    root = reference_root()
+    if root is None:
+        return []
+    base = os.path.join(root, "code", "cis2-fp", "tests", "fixtures")
+    return sorted(os.path.join(base, s, d) for s in ("refusal", "refusal-deep")
+                  if os.path.isdir(os.path.join(base, s)) for d in os.listdir(os.path.join(base, s)))
+
+
+@pytest.mark.skipif(reference_root() is None, reason="reference checkout not present")
+def test_reference_refusal_suite(pkg):
+    """code/cis2-fp/tests/fixtures/run_refusal_suite.sh run through cis2b_ref:
+    every checkpoint the Rust gate refuses is refused by name (exit 2, the
+    reference's reason text, no digest); the ones it admits pass the gate
+    and then fail on their absent weights (exit 101, as the reference's
+    panic does).  The admitted set is exactly qwen2-1.5b: Qwen3 is refused
+    by default, like the Rust reference, and admitted only through the
+    qwen3-port gate."""
+    dirs = refusal_fixture_dirs()
+    assert len(dirs) >= 12
+    admitted = []
+    for d in dirs:
+        with open(os.path.join(d, "config.json")) as f:
+            cfg = json.load(f)
+        want = rust_gate_reason(cfg)
+        p = subprocess.run([pkg.CLI_PATH, "--weights-dir", d, "--gen-toks", "1"], capture_output=True, text=True,
+                           timeout=60)
+        assert "CIS2_REF digest=" not in p.stdout
+        if want is None:
+            admitted.append(os.path.basename(d))
+            assert p.returncode == 101, (d, p.returncode, p.stderr)
+            continue
+        assert p.returncode == 2, (d, p.returncode, p.stderr)
+        lines = p.stderr.splitlines()
+        assert lines[0] == "CIS2_REF_UNSUPPORTED reason=" + want, (d, lines[0], want)
+        assert lines[1] == "This checkpoint is outside the CIS-2 specified subset; no digest emitted."
+        rc, msg, _ = _load_rc(pkg, d)
+        assert rc == 3 and msg == want
+    assert admitted == ["qwen25-1.5b"]
+    q3 = [d for d in dirs if os.path.basename(d) == "qwen3-0.6b-base"][0]
+    rc, msg, _ = _load_rc(pkg, q3, arch_gate=1)
+    assert rc == 2 and "model.safetensors" in msg  # admitted by the port gate; no weights here
+    p = subprocess.run([pkg.CLI_PATH, "--weights-dir", q3, "--gen-toks", "1", "--arch-gate", "qwen3-port"],
+                       capture_output=True, text=True, timeout=60)
+    assert p.returncode == 101 and "CIS2_REF_UNSUPPORTED" not in p.stderr
+
+
+def test_qwen3_needs_the_port_gate(pkg, synth, synth_root):
+    """A qwen3 config is refused by the default gate with the Rust reason and
+    loads through CIS2B_GATE_QWEN3_PORT (up to the device, which this test
+    does not need: on a machine without one the load fails after the gate)."""
+    d = synth.ensure_model("tiny_qwen3", synth_root)
+    rc, msg, _ = _load_rc(pkg, d)
+    assert rc == 3 and msg == 'model_type="qwen3" is not in the CIS-2 specified subset ["llama", "qwen2"]'
+    rc, msg, h = _load_rc(pkg, d, arch_gate=1)
+    assert rc != 3, msg
+    if rc == 0:
+        pkg.lib().cis2b_free(h)
+    rc, msg, _ = _load_rc(pkg, d, arch_gate=2)
+    assert rc == 1 and "gate" in msg
+
+
+def test_config_json_strings_and_numbers(pkg, synth, synth_root, tmp_path):
+    """config.json reading: \\u escapes (a surrogate pair included) decode,
+    and malformed JSON -- a bad number, a lone surrogate, a raw control
+    character -- is an artifact error, never a silent default."""
+    d = _copy_model(synth, synth_root, tmp_path)
+    base = (d / "config.json").read_text().rstrip().rstrip("}")
+    for extra, ok in [(', "note": "caf\\u00e9 \\ud83d\\ude00 \\"q\\" \\/"}', True),
+                      (', "note": 1.5e-3}', True),
+                      (', "note": 01}', False), (', "note": 1.}', False), (', "note": -}', False),
+                      (', "note": "\\ud83d"}', False), (', "note": "a\tb"}', False),
+                      (', "note": tru}', False)]:
+        (d / "config.json").write_text(base + extra)
+        rc, msg, h = _load_rc(pkg, str(d))
+        if ok:
+            assert rc not in (2, 3), (extra, msg)
+            if rc == 0:
+                pkg.lib().cis2b_free(h)
+        else:
+            assert rc == 2 and "config.json" in msg, (extra, rc, msg)

@@ -19,8 +19,9 @@ _models: dict = {}
 def model_for(pkg, synth, synth_root, name: str, reduction: str, max_positions: int = 0):
     key = (name, reduction, max_positions)
     if key not in _models:
+        gate = "qwen3-port" if synth.MODELS[name].model_type == "qwen3" else "reference"
         _models[key] = pkg.Model(synth.ensure_model(name, synth_root), reduction=reduction,
-                                 max_positions=max_positions)
+                                 max_positions=max_positions, arch_gate=gate)
     return _models[key]
 
 

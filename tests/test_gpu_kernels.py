@@ -176,3 +176,23 @@ def test_gumbel_sampler_matches_oracle(n, T, top_k, top_p, pkg, oracle):
         for seed, step in ((1, 0), (0xFFFFFFFFFFFFFFFF, 7), (12345, 255)):
             want, _ = oracle.sample_gumbel(logits, T, top_k, top_p, seed, step)
             assert pkg.sample_gumbel(logits, T, top_k, top_p, seed, step) == want, (trial, seed, step)
+
+
+@pytest.mark.parametrize("V", [32, 49152, 151936])
+def test_argmax_ties_zeros_and_nans(V, pkg, oracle):
+    from conftest import argmax_edge_rows
+    """The decode steps' argmax kernel against the oracle's serial scan and a
+    plain-Python strict '>' scan, on every edge row at once (one row per
+    block, as in a batched step)."""
+    rows = argmax_edge_rows(V)
+    X = np.stack(rows)
+    got = pkg.argmax(X)
+    for r, g in zip(rows, got):
+        best, bv = 0, r[0]
+        for i in range(1, V) if V <= 64 else ():
+            if r[i] > bv:
+                best, bv = i, r[i]
+        want = int(oracle.lib().cis2o_argmax(r.ctypes.data, V))
+        if V <= 64:
+            assert want == best
+        assert int(g) == want

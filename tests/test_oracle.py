@@ -111,7 +111,7 @@ def test_sampler_unit_cases(oracle):
 
 # ---------------------------------------------------------------- parity with the reference
 
-SMALL = [n for n in golden_names() if n.startswith(("tiny", "mid"))]
+SMALL = [n for n in golden_names() if n.startswith(("tiny", "mid", "coverage"))]
 
 
 @pytest.mark.parametrize("name", SMALL)
@@ -275,3 +275,16 @@ def test_math_sweep_port_equals_reference_binary(oracle, tmp_path):
     assert np.array_equal(x.view(np.uint32), oracle.math_sweep_inputs().view(np.uint32))
     for i, f in enumerate(oracle.MATH_FUNCS):
         assert np.array_equal(oracle.pinned_map(i, x).view(np.uint32), ref[f].view(np.uint32)), f
+
+
+def test_argmax_edge_rows_match_serial_scan(oracle):
+    """The oracle's argmax is the reference's strict '>' scan from index 0
+    (code/cis2-fp/src/main.rs:1161-1169) on the device test's edge rows."""
+    from conftest import argmax_edge_rows
+    for V in (32, 257):
+        for r in argmax_edge_rows(V):
+            best, bv = 0, r[0]
+            for i in range(1, V):
+                if r[i] > bv:
+                    best, bv = i, r[i]
+            assert int(oracle.lib().cis2o_argmax(r.ctypes.data, V)) == best
