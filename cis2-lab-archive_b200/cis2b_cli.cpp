@@ -16,7 +16,12 @@
 //   cis2b_ref --weights-dir D --ids F [--gen-toks N] [--reduction sequential|tree]
 //             [--mode greedy|sampled --seed S --temperature T --top-p P]
 //             [--sample SEED,T,K,P] [--receipt F] [--arch-gate reference|qwen3-port]
-//             [--device I] [--prompt-idx I] [--step-digests]
+//             [--device I] [--prompt-idx I] [--step-digests] [--trace F]
+// With --trace F the first prompt's run is also written to F as the
+// reference's per-op trace (code/cis2-fp/gpu/cis2_host.cpp:76, 173-208):
+// one "pos=P layer=L op=NAME sha256=HEX" line per op of every position, the
+// prompt's and the generated tokens', so `make gate`-style diffs against the
+// reference's trace work with this binary (see cis2b_trace in cis2b.h).
 // The architecture gate runs on config.json first, as in the reference
 // (code/cis2-fp/src/main.rs:812-823): a refused checkpoint prints the two
 // CIS2_REF_UNSUPPORTED lines and exits 2 whatever else is missing; a failure
@@ -91,7 +96,7 @@ static bool read_id_lines(const std::string &path, std::vector<std::vector<uint3
 }
 
 int main(int argc, char **argv) {
-  std::string weights_dir = "weights", ids_path, receipt_path;
+  std::string weights_dir = "weights", ids_path, receipt_path, trace_path;
   int gen = 16, device = 0, prompt_idx = 0;
   bool tree = false, sampled = false, gumbel = false, step_digests = false;
   int arch_gate = CIS2B_GATE_REFERENCE;
@@ -137,6 +142,7 @@ int main(int argc, char **argv) {
       if (v == "qwen3-port") arch_gate = CIS2B_GATE_QWEN3_PORT;
       else if (v != "reference") { fprintf(stderr, "FATAL: --arch-gate reference|qwen3-port\n"); return 2; }
     } else if (a == "--receipt") receipt_path = next();
+    else if (a == "--trace") trace_path = next();
     else if (a == "--seed") smp.seed = strtoull(next(), nullptr, 10);
     else if (a == "--temperature") smp.temperature = strtof(next(), nullptr);
     else if (a == "--top-p") smp.top_p = strtof(next(), nullptr);
@@ -229,6 +235,15 @@ int main(int argc, char **argv) {
     fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
     cis2b_free(m);
     return 2;
+  }
+  if (!trace_path.empty()) {
+    std::vector<uint32_t> run(prompts[0]);
+    run.insert(run.end(), toks.begin(), toks.begin() + gen);
+    if (cis2b_trace(m, run.data(), (uint32_t)run.size(), trace_path.c_str()) != CIS2B_OK) {
+      fprintf(stderr, "FATAL: %s\n", cis2b_last_error());
+      cis2b_free(m);
+      return 2;
+    }
   }
   printf("weights_sha256=%s\n", hexs(info.weights_sha256, 32).c_str());
   printf("tokenizer_sha256=%s\n", hexs(info.tokenizer_sha256, 32).c_str());

@@ -1091,7 +1091,7 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
                             int nh, int nkv, int hd, float *kc, float *vc, int max_pos,
                             int tree, float *att, int ars, int acs, int max_len, int fuse_post,
                             const uint16_t *qn, const uint16_t *kn, float eps, const float *cos_t,
-                            const float *sin_t) {
+                            const float *sin_t, float *dbg) {
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
@@ -1198,6 +1198,11 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
     }
     __syncthreads();
   }
+  // Trace mode (one row): the scaled scores of this KV head's q heads,
+  // [n_heads][len] at dbg.
+  if (dbg)
+    for (int i = tid; i < G * len; i += nt)
+      dbg[((size_t)kvh * G + i / len) * len + i % len] = sc[(size_t)(i / len) * scs + i % len];
   // V chunk 0 loads while the softmax runs.
   stage(vbase, 0, 0);
   // ---- max per head (serial-scan semantics, see max_comb)
@@ -1239,6 +1244,11 @@ __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32
     const float den = red[32 + g];
     for (int j = tid; j < len; j += nt) sg[j] = fdiv(sg[j], den);
   }
+  if (dbg) {  // trace mode: the softmax weights, [n_heads][len] after the scores
+    __syncthreads();
+    for (int i = tid; i < G * len; i += nt)
+      dbg[((size_t)nh + kvh * G + i / len) * len + i % len] = sc[(size_t)(i / len) * scs + i % len];
+  }
   // ---- V-mix, V streamed through the two tile buffers.  Thread t owns the
   // chain (g, d) = (t / hd, t % hd): the block's G*hd threads all work on
   // every chunk, the lanes of a warp read consecutive d of one V row
@@ -1277,7 +1287,7 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
                       float *kcache, float *vcache, int max_pos, bool tree, float *att,
                       int ars, int acs, int max_len, bool fuse_post, const uint16_t *q_norm,
                       const uint16_t *k_norm, float eps, const float *cos_t, const float *sin_t,
-                      cudaStream_t s) {
+                      cudaStream_t s, float *dbg) {
   if (rows <= 0) return;
   const int G = n_heads / n_kv;
   int nt = ((G * hd + 31) / 32) * 32;
@@ -1288,7 +1298,27 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
   dim3 grid(rows, n_kv);
   k_attention<<<grid, nt, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache, max_pos,
                                      tree ? 1 : 0, att, ars, acs, max_len, fuse_post ? 1 : 0, q_norm,
-                                     k_norm, eps, cos_t, sin_t);
+                                     k_norm, eps, cos_t, sin_t, dbg);
+}
+
+// Trace mode: the per-head q/k RMSNorm alone (qwen3-port.diff:66-80), in
+// place on one qkv row, with the same warp routine k_qkv_post applies before
+// its RoPE; launch_qkv_post then runs without norm weights.
+__global__ void k_qk_norm_row(float *row, int nh, int nkv, int hd, const uint16_t *qn, const uint16_t *kn,
+                              float eps, int tree) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int h = warp; h < nh + nkv; h += nw) {
+    const bool is_k = h >= nh;
+    const uint16_t *w = is_k ? kn : qn;
+    float *x = is_k ? row + (size_t)nh * hd + (size_t)(h - nh) * hd : row + (size_t)h * hd;
+    if (w) warp_rmsnorm(x, w, eps, hd, tree != 0, sm + (size_t)warp * 2 * hd, x);
+  }
+}
+void launch_qk_norm_row(float *row, int n_heads, int n_kv, int hd, const uint16_t *q_norm, const uint16_t *k_norm,
+                        float eps, bool tree, cudaStream_t s) {
+  k_qk_norm_row<<<1, 128, (size_t)4 * 2 * hd * sizeof(float), s>>>(row, n_heads, n_kv, hd, q_norm, k_norm, eps,
+                                                                     tree ? 1 : 0);
 }
 
 // ---- Prompt-pass attention, several rows per CTA.  In the prompt pass the

@@ -63,12 +63,17 @@ void launch_qkv_post(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n
                      const float *cos_t, const float *sin_t, float *kcache, float *vcache,
                      int max_pos, cudaStream_t s);
 // fuse_post: also do launch_qkv_post's work for the row (decode only: every
-// row must be a different sequence's newest position).
+// row must be a different sequence's newest position).  dbg (trace mode,
+// rows == 1 only): receives the scaled scores [n_heads][pos+1] and then the
+// softmax weights [n_heads][pos+1].
 void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd,
                       float *kcache, float *vcache, int max_pos, bool tree, float *att,
                       int ars, int acs, int max_len, bool fuse_post, const uint16_t *q_norm,
                       const uint16_t *k_norm, float eps, const float *cos_t, const float *sin_t,
-                      cudaStream_t s);
+                      cudaStream_t s, float *dbg = nullptr);
+// Trace mode: per-head q/k RMSNorm of one qkv row, in place.
+void launch_qk_norm_row(float *row, int n_heads, int n_kv, int hd, const uint16_t *q_norm, const uint16_t *k_norm,
+                        float eps, bool tree, cudaStream_t s);
 // Shared memory (floats) the attention kernel needs; G = n_heads / n_kv.
 size_t attention_smem_floats(int G, int hd, int max_len);
 // Prompt-pass attention over tiles of consecutive rows of one sequence

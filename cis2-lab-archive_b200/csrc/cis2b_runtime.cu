@@ -1148,6 +1148,122 @@ struct Scoped {
   ~Scoped() { if (p) cudaFree(p); }
 };
 
+// ------------------------------------------------------------------ trace
+// Per-op trace (debug mode, off the timed path; cis2_model.h:482-496 and the
+// emit points of cis2_forward_token, :685-760; q_norm / k_norm lines from
+// labs/w1x-qwen3/scripts/qwen3-port.diff:66-80).  Every position of `ids`
+// runs alone through the position-batched (prompt-pass) kernels, one row,
+// so each op's output exists in device memory; its fp32 bits are copied out
+// and hashed (SHA-256 over u32 LE) into one line per op:
+//   pos=P layer=L op=NAME sha256=HEX      (layer -1 for embedding, final_norm, logits)
+// The decode-step kernels fuse several of these ops and are checked against
+// the same arithmetic by the parity tests.  Three outputs that no production
+// kernel writes on its own are made here from production kernels: o_proj and
+// down are the residual GEMMs run once without their residual; scores and
+// softmax come from the attention kernel's trace output.
+int trace_impl(cis2b_model *m, const uint32_t *ids, uint32_t n_ids, const char *path) {
+  if (!m || !ids || !path) return fail(CIS2B_ERR_ARG, "NULL argument");
+  if (n_ids == 0) return fail(CIS2B_ERR_ARG, "n_ids must be >= 1");
+  if ((int)n_ids > m->max_pos) return fail(CIS2B_ERR_ARG, "ids exceed max_positions");
+  for (uint32_t i = 0; i < n_ids; ++i)
+    if (ids[i] >= (uint32_t)m->V) return fail(CIS2B_ERR_ARG, "id out of vocabulary range");
+  CU(cudaSetDevice(m->dev));
+  const int maxP = (int)n_ids, H = m->H, I = m->I, QD = m->QD, KVD = m->KVD, NQKV = QD + 2 * KVD;
+  int rc = alloc_cache(m, 1, maxP);
+  if (rc) return rc;
+  rc = ensure_act(m, 1);
+  if (rc) return rc;
+  DevBuf d_tok, d_seq, d_pos, d_o, d_dbg, d_logits;
+  if (d_tok.ensure(4) || d_seq.ensure(4) || d_pos.ensure(4) || d_o.ensure(4 * (size_t)H) ||
+      d_dbg.ensure(4 * 2 * (size_t)m->NH * maxP) || d_logits.ensure(4 * (size_t)m->V) ||
+      m->lnlast.ensure(4 * (size_t)64 * H))
+    return fail(CIS2B_ERR_NOMEM, "device allocation of trace buffers failed");
+  FILE *fp = fopen(path, "wb");
+  if (!fp) return fail(CIS2B_ERR_IO, std::string("cannot write ") + path);
+  struct Closer { FILE *f; ~Closer() { fclose(f); } } closer{fp};
+  cudaStream_t s = m->s_main;
+  const int ldm = m->act_ldm;
+  std::vector<float> host;
+  // Copies n floats (element stride `stride`) and writes the op's line.
+  auto emit = [&](int pos, int layer, const char *op, const float *dev, size_t n, size_t stride) -> int {
+    host.resize(n);
+    if (stride == 1) CU(cudaMemcpyAsync(host.data(), dev, 4 * n, cudaMemcpyDeviceToHost, s));
+    else CU(cudaMemcpy2DAsync(host.data(), 4, dev, 4 * stride, 4, n, cudaMemcpyDeviceToHost, s));
+    CU(cudaStreamSynchronize(s));
+    Sha256 h;
+    for (float f : host) { uint32_t u; memcpy(&u, &f, 4); h.u32le(u); }
+    uint8_t d[32];
+    h.final(d);
+    fprintf(fp, "pos=%d layer=%d op=%s sha256=%s\n", pos, layer, op, hex(d, 32).c_str());
+    return CIS2B_OK;
+  };
+#define EMIT(...) do { int e_ = emit(__VA_ARGS__); if (e_) return e_; } while (0)
+  float *h = m->h.as<float>(), *ln = m->ln.as<float>(), *qkv = m->qkv.as<float>();
+  float *att = m->att.as<float>(), *gu = m->gu.as<float>(), *hid = m->hid.as<float>();
+  float *o = d_o.as<float>(), *dbg = d_dbg.as<float>();
+  const size_t layer_kv = (size_t)maxP * KVD;
+  RowMap rm{d_seq.as<int32_t>(), d_pos.as<int32_t>()};
+  const int32_t zero = 0;
+  CU(cudaMemcpyAsync(d_seq.p, &zero, 4, cudaMemcpyHostToDevice, s));
+  for (int pos = 0; pos < maxP; ++pos) {
+    const int32_t p32 = pos;
+    CU(cudaMemcpyAsync(d_tok.p, &ids[pos], 4, cudaMemcpyHostToDevice, s));
+    CU(cudaMemcpyAsync(d_pos.p, &p32, 4, cudaMemcpyHostToDevice, s));
+    launch_embed(m->embed, H, d_tok.as<uint32_t>(), 1, h, s);
+    EMIT(pos, -1, "embedding", h, (size_t)H, 1);
+    for (int l = 0; l < m->L; ++l) {
+      const LayerW &w = m->layers[(size_t)l];
+      float *kc = m->kc.as<float>() + (size_t)l * layer_kv, *vc = m->vc.as<float>() + (size_t)l * layer_kv;
+      launch_rmsnorm(h, H, w.in_norm, m->eps, H, 1, m->tree, ln, 1, ldm, s);
+      EMIT(pos, l, "norm1", ln, (size_t)H, (size_t)ldm);
+      launch_gemm(ln, ldm, w.pqkv, H, NQKV, 1, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s);
+      if (w.q_bias) launch_add_bias(qkv, NQKV, 1, w.q_bias, QD, s);
+      if (w.k_bias) launch_add_bias(qkv + QD, NQKV, 1, w.k_bias, KVD, s);
+      if (w.v_bias) launch_add_bias(qkv + QD + KVD, NQKV, 1, w.v_bias, KVD, s);
+      EMIT(pos, l, "q", qkv, (size_t)QD, 1);
+      EMIT(pos, l, "k", qkv + QD, (size_t)KVD, 1);
+      EMIT(pos, l, "v", qkv + QD + KVD, (size_t)KVD, 1);
+      if (w.q_norm || w.k_norm) {
+        launch_qk_norm_row(qkv, m->NH, m->NKV, m->HD, w.q_norm, w.k_norm, m->eps, m->tree, s);
+        if (w.q_norm) EMIT(pos, l, "q_norm", qkv, (size_t)QD, 1);
+        if (w.k_norm) EMIT(pos, l, "k_norm", qkv + QD, (size_t)KVD, 1);
+      }
+      launch_qkv_post(qkv, NQKV, 1, rm, m->NH, m->NKV, m->HD, nullptr, nullptr, m->eps, m->tree,
+                      m->cos_t.as<float>(), m->sin_t.as<float>(), kc, vc, maxP, s);
+      EMIT(pos, l, "rope_q", qkv, (size_t)QD, 1);
+      EMIT(pos, l, "rope_k", qkv + QD, (size_t)KVD, 1);
+      launch_attention(qkv, NQKV, 1, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, 1, ldm, maxP, false,
+                       nullptr, nullptr, m->eps, m->cos_t.as<float>(), m->sin_t.as<float>(), s, dbg);
+      EMIT(pos, l, "scores", dbg, (size_t)m->NH * (pos + 1), 1);
+      EMIT(pos, l, "softmax", dbg + (size_t)m->NH * (pos + 1), (size_t)m->NH * (pos + 1), 1);
+      EMIT(pos, l, "attn_out", att, (size_t)QD, (size_t)ldm);
+      launch_gemm(att, ldm, w.po, QD, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
+      EMIT(pos, l, "o_proj", o, (size_t)H, 1);
+      launch_gemm(att, ldm, w.po, QD, H, 1, h, H, h, H, m->tree, nullptr, 0, s);
+      EMIT(pos, l, "resid1", h, (size_t)H, 1);
+      launch_rmsnorm(h, H, w.post_norm, m->eps, H, 1, m->tree, ln, 1, ldm, s);
+      EMIT(pos, l, "norm2", ln, (size_t)H, (size_t)ldm);
+      launch_gemm(ln, ldm, w.pgu, H, 2 * I, 1, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s);
+      EMIT(pos, l, "gate", gu, (size_t)I, 1);
+      EMIT(pos, l, "up", gu + I, (size_t)I, 1);
+      launch_silu_mul(gu, I, 1, hid, 1, ldm, s);
+      EMIT(pos, l, "silu_mul", hid, (size_t)I, (size_t)ldm);
+      launch_gemm(hid, ldm, w.pdown, I, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
+      EMIT(pos, l, "down", o, (size_t)H, 1);
+      launch_gemm(hid, ldm, w.pdown, I, H, 1, h, H, h, H, m->tree, nullptr, 0, s);
+      EMIT(pos, l, "resid2", h, (size_t)H, 1);
+    }
+    launch_rmsnorm(h, H, m->final_norm, m->eps, H, 1, m->tree, m->lnlast.as<float>(), 1, 64, s);
+    EMIT(pos, -1, "final_norm", m->lnlast.as<float>(), (size_t)H, 64);
+    launch_gemm(m->lnlast.as<float>(), 64, m->lm_head_p, H, m->V, 1, d_logits.as<float>(), m->V, nullptr, 0, m->tree,
+                nullptr, 0, s);
+    EMIT(pos, -1, "logits", d_logits.as<float>(), (size_t)m->V, 1);
+    CU_LAUNCHED();
+  }
+#undef EMIT
+  return CIS2B_OK;
+}
+
 }  // namespace
 
 // ================================================================== C ABI
@@ -1229,6 +1345,12 @@ int cis2b_profile_read(const cis2b_model *m, uint32_t class_bit, cis2b_kernel_ti
 
 int cis2b_logits(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_rows, float *out_logits) {
   int rc = logits_impl(m, ids, n_prompt, n_rows, out_logits);
+  if (rc == CIS2B_OK) g_err.clear();
+  return rc;
+}
+
+int cis2b_trace(cis2b_model *m, const uint32_t *ids, uint32_t n_ids, const char *trace_path) {
+  int rc = trace_impl(m, ids, n_ids, trace_path);
   if (rc == CIS2B_OK) g_err.clear();
   return rc;
 }

@@ -171,6 +171,18 @@ int cis2b_verify(cis2b_model *m, const uint32_t *prompt_ids, const uint32_t *pro
 int cis2b_logits(cis2b_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_rows,
                  float *out_logits);
 
+/* Per-op trace, for localising a parity failure (debug only; the
+ * reference CLI's --trace F, code/cis2-fp/gpu/cis2_host.cpp:76, 173-193, and
+ * its emit points, gpu/cis2_model.h:482-496, 685-760).  Runs ids[0 .. n_ids)
+ * as ONE sequence, position by position, and writes one line per op output
+ *   pos=P layer=L op=NAME sha256=HEX
+ * (SHA-256 over the output's fp32 bits, u32 LE) in the reference's op order:
+ * embedding; per layer norm1 q k v [q_norm k_norm] rope_q rope_k scores
+ * softmax attn_out o_proj resid1 norm2 gate up silu_mul down resid2; then
+ * final_norm and logits.  To trace a generation of G tokens as the
+ * reference does, pass the prompt followed by the G generated ids. */
+int cis2b_trace(cis2b_model *m, const uint32_t *ids, uint32_t n_ids, const char *trace_path);
+
 void cis2b_free(cis2b_model *m);
 
 /* Message of the last failed call on this thread ("" if none). */

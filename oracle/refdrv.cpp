@@ -19,7 +19,8 @@
 //     a restatement of code/patches/cis2-fp__cm_e23-pinned-sampling.patch,
 //     src/sampling.rs hunk, lines 619-725) with its witness prefix
 //     "CIS2_SAMPLE_V1" || seed || T || top_p before the header (patch :610-624);
-//   * per-phase wall-clock timings for the CPU baseline.
+//   * per-phase wall-clock timings for the CPU baseline and, with
+//     --step-times, the time at which every decode step ended.
 // It prints one JSON object per sequence.
 //
 // Build variants (oracle/Makefile): sequential, -DCIS2_REDUCTION_TREE, and a
@@ -125,7 +126,7 @@ int main(int argc, char **argv) {
 
   std::string weights_dir = "weights", ids_path, out_path;
   int gen_toks = 16, first = 0, count = -1;
-  bool step_digests = false, sampled = false;
+  bool step_digests = false, sampled = false, step_times = false;
   uint64_t seed = 0;
   float temperature = 0.8f, top_p = 0.95f;
   for (int i = 1; i < argc; ++i) {
@@ -137,6 +138,7 @@ int main(int argc, char **argv) {
     else if (a == "--count" && i + 1 < argc) count = atoi(argv[++i]);
     else if (a == "--out" && i + 1 < argc) out_path = argv[++i];
     else if (a == "--step-digests") step_digests = true;
+    else if (a == "--step-times") step_times = true;
     else if (a == "--sample" && i + 3 < argc) {
       sampled = true;
       seed = strtoull(argv[++i], nullptr, 10);
@@ -289,6 +291,7 @@ int main(int argc, char **argv) {
     double t1 = now_s();
 
     std::vector<std::string> step_hex;
+    std::vector<double> step_end;  // seconds since the decode started, after each step's forward
     Cis2Sha256 steps_hash;
     for (int step = 0; step < gen_toks; ++step) {
       uint32_t next_id;
@@ -315,6 +318,7 @@ int main(int argc, char **argv) {
         cis2_forward_token(model, ws, pos, next_id, nullptr);
         cis2_download(logits.data(), ws.logits, (size_t)model.vocab);
       }
+      if (step_times) step_end.push_back(now_s() - t1);
     }
     double t2 = now_s();
     unsigned char wdig[32], adig[32], sdig[32];
@@ -334,6 +338,11 @@ int main(int argc, char **argv) {
       fprintf(out, ",\"step_digests\":[");
       for (size_t i = 0; i < step_hex.size(); ++i)
         fprintf(out, "%s\"%s\"", i ? "," : "", step_hex[i].c_str());
+      fprintf(out, "]");
+    }
+    if (step_times) {
+      fprintf(out, ",\"step_end_s\":[");
+      for (size_t i = 0; i < step_end.size(); ++i) fprintf(out, "%s%.6f", i ? "," : "", step_end[i]);
       fprintf(out, "]");
     }
     fprintf(out, ",\"prefill_s\":%.6f,\"decode_s\":%.6f}\n", t1 - t0, t2 - t1);

@@ -25,15 +25,20 @@ def test_witness_roofline_fields():
     blocks = (4 * m.vocab + 4) / 64.0
     t_ms = blocks * bench.CHAIN_FLOOR_CYCLES_PER_BLOCK / 1965e6 * 1e3
     r = bench.kernel_rooflines(m, w, 64, _prof(witness_ms_per_launch=t_ms), 1965.0)["witness"]
-    assert r["chain_frac"] == pytest.approx(1.0, rel=1e-9)
+    # The witness is bound by integer issue, and its fraction is of that bound.
+    assert r["bound"] == "int_issue"
+    assert r["frac"] == pytest.approx(1.0, rel=1e-9)
     assert r["cycles_per_block_per_chain"] == pytest.approx(bench.CHAIN_FLOOR_CYCLES_PER_BLOCK, rel=1e-9)
-    assert r["algorithmic_bytes"] == 64 * (4 * m.vocab + 4)
-    assert r["achieved"] == pytest.approx(r["algorithmic_bytes"] / (t_ms / 1e3) / 1e9)
+    assert r["achieved"] == pytest.approx(1965e6 / bench.CHAIN_FLOOR_CYCLES_PER_BLOCK)
     assert r["frac"] == pytest.approx(r["achieved"] / r["peak"])
+    # Its HBM side is reported beside it.
+    assert r["algorithmic_bytes"] == 64 * (4 * m.vocab + 4)
+    assert r["hbm"]["achieved"] == pytest.approx(r["algorithmic_bytes"] / (t_ms / 1e3) / 1e9)
+    assert r["hbm"]["frac"] == pytest.approx(r["hbm"]["achieved"] / r["hbm"]["peak"])
     assert r["traffic"] == bench.WITNESS_TRAFFIC_C2  # the captured shape
     # Twice as slow: half the fraction.
     r2 = bench.kernel_rooflines(m, w, 64, _prof(witness_ms_per_launch=2 * t_ms), 1965.0)["witness"]
-    assert r2["chain_frac"] == pytest.approx(0.5, rel=1e-9)
+    assert r2["frac"] == pytest.approx(0.5, rel=1e-9)
     # Another shape has no captured traffic figure.
     r3 = bench.kernel_rooflines(m, w, 32, _prof(witness_ms_per_launch=t_ms), 1965.0)["witness"]
     assert r3["traffic"] is None
@@ -42,11 +47,47 @@ def test_witness_roofline_fields():
 def test_lm_head_roofline_fields():
     m, w = synth.MODELS["smollm2"], synth.WORKLOADS["c2"]
     r = bench.kernel_rooflines(m, w, 64, _prof(lm_ms_per_launch=0.2), 1965.0)["lm_head"]
-    byts = m.vocab * m.hidden * 2 + 64 * m.hidden * 4 + 64 * m.vocab * 4
-    assert r["algorithmic_bytes"] == byts
-    assert r["achieved"] == pytest.approx(byts / 0.2e-3 / 1e9)
+    assert r["bound"] == "fp32_pipe"
     fp32 = 148 * 128 * 1965e6
-    assert r["fp32_alu_frac"] == pytest.approx(2 * 64 * m.vocab * m.hidden / 0.2e-3 / fp32)
+    assert r["frac"] == pytest.approx(2 * 64 * m.vocab * m.hidden / 0.2e-3 / fp32)
+    byts = m.vocab * m.hidden * 2 + 64 * m.hidden * 4 + 64 * m.vocab * 4
+    assert r["hbm"]["algorithmic_bytes"] == byts
+    assert r["hbm"]["achieved"] == pytest.approx(byts / 0.2e-3 / 1e9)
+
+
+def test_golden_check_covers_every_rank(tmp_path, monkeypatch):
+    """The parity check reads every fixture of a workload and maps each
+    gathered sequence to its global index, so sequences of ranks > 0 are
+    checked too; a single flipped step digest fails the sequence."""
+    import hashlib
+    import json
+    import numpy as np
+    G = 3
+    rows = []
+    for i in range(6):
+        rng = np.random.default_rng(i)
+        rows.append({"tokens": rng.integers(0, 9, G).astype(np.uint32),
+                     "steps": rng.integers(0, 255, (G, 32)).astype(np.uint8),
+                     "witness": rng.integers(0, 255, 32).astype(np.uint8),
+                     "argmax": rng.integers(0, 255, 32).astype(np.uint8)})
+
+    def entry(r):
+        return {"witness": r["witness"].tobytes().hex(), "argmax": r["argmax"].tobytes().hex(),
+                "steps_sha": hashlib.sha256(r["steps"].tobytes()).hexdigest(),
+                "tokens_sha": hashlib.sha256(r["tokens"].astype("<u4").tobytes()).hexdigest()}
+
+    (tmp_path / "cx.json").write_text(json.dumps({"prompts": ["workload", "cx", 0, 2],
+                                                  "sequences": [entry(r) for r in rows[:2]]}))
+    (tmp_path / "cx_shards.json").write_text(json.dumps({"prompts": ["workload_idx", "cx", [3, 5]],
+                                                         "sequences": [entry(rows[3]), entry(rows[5])]}))
+    monkeypatch.setattr(bench, "GOLDEN_DIR", str(tmp_path))
+    out = {"tokens": np.stack([r["tokens"] for r in rows]), "step_digests": np.stack([r["steps"] for r in rows]),
+           "witness": np.stack([r["witness"] for r in rows]), "argmax": np.stack([r["argmax"] for r in rows])}
+    g = bench.golden_check("cx", 0, out, 6)
+    assert (g["checked"], g["identical"], g["unchecked"]) == (4, 4, 2)
+    out["step_digests"][5, 1, 7] ^= 1
+    g = bench.golden_check("cx", 0, out, 6)
+    assert (g["identical"], g["differ"]) == (3, 1)
 
 
 def test_step_bound_label_follows_the_longer_path():

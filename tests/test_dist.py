@@ -1,6 +1,7 @@
 """Multi-process host logic on CPU (gloo, world size 2): the sequence
-sharding bench.py uses and the one exchange step (gather of tokens and
-digests) reproduce a single-process run exactly."""
+sharding bench.py uses and the one exchange step (bench.gather_outputs:
+tokens, per-step digests, witness and argmax digests) reproduce a
+single-process run exactly."""
 from __future__ import annotations
 
 import os
@@ -51,12 +52,9 @@ def _worker(rank, world, port, out_q):
     prompts = [synth.random_prompts("tiny", 1, 4 + i, 31, first=i)[0] for i in range(first, first + cnt)]
     r = pyoracle.PortOracle(d).generate(prompts, 6)
     counts = [bench.shard(n_total, world, q)[1] for q in range(world)]
-    pad = torch.zeros((max(counts), 32), dtype=torch.uint8)
-    pad[:cnt] = torch.from_numpy(r["witness"])
-    allw = [torch.zeros_like(pad) for _ in range(world)]
-    dist.all_gather(allw, pad)
+    got = bench.gather_outputs(r, 6, counts, "cpu")
     if rank == 0:
-        out_q.put(torch.cat([a[:c] for a, c in zip(allw, counts)]).numpy())
+        out_q.put({k: np.array(v) for k, v in got.items()})
     dist.barrier()
     dist.destroy_process_group()
 
@@ -74,8 +72,9 @@ def test_gloo_sharded_gather_equals_single_run(synth, synth_root, oracle):
         assert p.exitcode == 0
     d = synth.ensure_model("tiny", synth_root)
     prompts = [synth.random_prompts("tiny", 1, 4 + i, 31, first=i)[0] for i in range(5)]
-    want = oracle.PortOracle(d).generate(prompts, 6)["witness"]
-    assert np.array_equal(got, want)
+    want = oracle.PortOracle(d).generate(prompts, 6)
+    for k in ("tokens", "step_digests", "witness", "argmax"):
+        assert np.array_equal(got[k], want[k]), k
 
 
 def test_failed_rank_is_detected_on_host(tmp_path):
