@@ -294,12 +294,14 @@ void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n
       x, ldx, w, eps, n, rows, tree ? 1 : 0, out, ors, ocs);
 }
 
+// gu rows hold gate and up interleaved: gate i at 2i, up i at 2i + 1 (the
+// gate/up panels are laid out that way, see launch_panelize).
 __global__ void k_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs) {
   size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (size_t)rows * I) return;
   size_t r = idx / I, i = idx % I;
-  const float *row = gu + r * 2 * (size_t)I;
-  hid[r * hrs + i * hcs] = fmul(silu_pinned(row[i]), row[I + i]);  // silu(g)*up (cis2_model.h:619-623)
+  const float2 gv = reinterpret_cast<const float2 *>(gu + r * 2 * (size_t)I)[i];
+  hid[r * hrs + i * hcs] = fmul(silu_pinned(gv.x), gv.y);  // silu(g)*up (cis2_model.h:619-623)
 }
 void launch_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs, cudaStream_t s) {
   size_t n = (size_t)rows * I;
@@ -557,7 +559,17 @@ int gemm_tile_choice(int M, int N, int K, bool tree) {
 // multiply-adds; each output still walks k = 0..K-1 in order.  Products are rounded singly and added as pairs of independent
 // accumulators with add.rn.ftz.f32x2, which halves the issue slots the adds
 // take.  Operands arrive through a BIG_STAGES-deep cp.async ring.
-constexpr int BIG_KT = 16, BIG_STAGES = 4, BIG_THREADS = 256;
+constexpr int BIG_KT = 16, BIG_STAGES = 4;
+
+// Two independent, separately rounded products (lanes of one packed op).
+__device__ __forceinline__ float2 fmul_pair(float a0, float a1, float b0, float b1) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rr;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.ftz.f32x2 rr, ra, rb;\n\tmov.b64 {%0, %1}, rr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  return r;
+}
 
 __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   float2 r;
@@ -568,42 +580,63 @@ __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   return r;
 }
 
-// Block tile BIG_BM x BN: BIG_BM = 128 (8 rows per thread) or 64 (4 rows per
-// thread); BN = 128 (8 columns per thread: 4 at tx*4, 4 at 64 + tx*4) or 64
-// (4 columns per thread).  The dispatcher below uses the 64-wide forms.
-template <int BIG_BM, int BN>
-__global__ void __launch_bounds__(BIG_THREADS, 2)
+// Block tile BM x BN over TY x TX threads; a thread owns TMR rows x TNC
+// columns (TMR * TNC output chains).  Rows come in blocks of RW = min(TMR,
+// 4) consecutive rows, RW * TY apart; columns in blocks of CW = min(TNC, 4),
+// CW * TX apart, and columns (n, n + 1) share one packed accumulator.
+// Per k a thread reads its rows' activations (one 8- or 16-byte load per
+// row block) and its columns' weights (one 4- or 8-byte load per column
+// block), forms its products singly and adds them as packed pairs of
+// independent accumulators (add.f32x2): every output still walks
+// k = 0..K-1 in order.  The products stay scalar: with packed products
+// (mul.f32x2) feeding the packed adds, B200 results no longer matched the
+// pinned order bit for bit (measured: most outputs of every tile shape
+// differed), so that pairing is never formed here.
+// Output element (m, n) goes to Y[m * ysm + n * ysn] (row-major: ysm = ldy,
+// ysn = 1; k-major for the next product: ysm = 1, ysn = ldm).  glu: W is a
+// gate/up pair panelised with its rows interleaved (gate i, up i at rows 2i,
+// 2i + 1), so a column pair (n, n + 1) is (gate i, up i) and the epilogue
+// writes silu(gate) * up as output column i = n / 2 (cis2_model.h:619-623).
+template <int TY, int TX, int TMR, int TNC>
+__global__ void __launch_bounds__(TY * TX, 1)
 k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp, int K, int N, int M,
-           float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
-           size_t y_slot_stride) {
-  static_assert(BN == 128 || BN == 64, "column tile");
-  constexpr int XF = BIG_KT * BIG_BM;  // floats per X stage
-  constexpr int WH = BIG_KT * BN;      // bf16 per W stage
-  constexpr int TMR = BIG_BM / 16;     // rows per thread: (i / 4) * 64 + ty * 4 + i % 4
-  constexpr int TNP = BN / 32;         // column pairs per thread
-  constexpr int XCH = XF / 4;          // 16-byte X chunks per stage
-  constexpr int WCH = WH / 8;          // 16-byte W chunks per stage
+           float *__restrict__ Y, int ysm, int ysn, const float *__restrict__ R, int ldr, const int32_t *y_slot,
+           size_t y_slot_stride, int glu) {
+  constexpr int RW = TMR < 4 ? TMR : 4, RB = TMR / RW;
+  constexpr int CW = TNC < 4 ? TNC : 4, CB = TNC / CW;
+  constexpr int NT = TY * TX, BM = RW * TY * RB, BN = CW * TX * CB;
+  constexpr int XF = BIG_KT * BM;  // floats per X stage
+  constexpr int WH = BIG_KT * BN;  // bf16 per W stage
+  constexpr int TNP = TNC / 2;     // column pairs per thread
+  constexpr int XCH = XF / 4;      // 16-byte X chunks per stage
+  constexpr int WCH = WH / 8;      // 16-byte W chunks per stage
+  static_assert((RW == 2 || RW == 4) && (CW == 2 || CW == 4) && BM % 4 == 0 && BN % 8 == 0, "tile shape");
   extern __shared__ __align__(16) float smem[];
   float *Xs = smem;                                                     // [S][KT][BM]
   uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + BIG_STAGES * XF);  // [S][KT][BN]
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int m0 = blockIdx.y * BIG_BM, n0 = blockIdx.x * BN, n8_0 = n0 / 8;
+  const int tid = threadIdx.x, tx = tid % TX, ty = tid / TX;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, n8_0 = n0 / 8;
   const int N8 = (N + 7) / 8;
   const uint32_t xs_b = (uint32_t)__cvta_generic_to_shared(Xs), ws_b = (uint32_t)__cvta_generic_to_shared(Ws);
   auto issue = [&](int kt) {
     const int slot = kt % BIG_STAGES, k0 = kt * BIG_KT;
 #pragma unroll
-    for (int r = 0; r < XCH / BIG_THREADS; ++r) {  // X: KT rows of BM floats
-      const int c = tid + r * BIG_THREADS, k = c / (BIG_BM / 4), q = c % (BIG_BM / 4);
-      const bool ok = (k0 + k < K) && (m0 + 4 * q < ldm);
-      const float *src = ok ? XT + (size_t)(k0 + k) * ldm + m0 + 4 * q : XT;
-      cp_async16_zfill(xs_b + (uint32_t)((slot * XF + k * BIG_BM + 4 * q) * 4), src, ok);
+    for (int r = 0; r < (XCH + NT - 1) / NT; ++r) {  // X: KT rows of BM floats
+      const int c = tid + r * NT, k = c / (BM / 4), q = c % (BM / 4);
+      if (c < XCH) {
+        const bool ok = (k0 + k < K) && (m0 + 4 * q < ldm);
+        const float *src = ok ? XT + (size_t)(k0 + k) * ldm + m0 + 4 * q : XT;
+        cp_async16_zfill(xs_b + (uint32_t)((slot * XF + k * BM + 4 * q) * 4), src, ok);
+      }
     }
-    if (tid < WCH) {  // W: KT x BN/8 panels of 8 bf16, to [k][n]
-      const int k = tid / (BN / 8), pnl = tid % (BN / 8);
-      const bool ok = (k0 + k < K) && (n8_0 + pnl < N8);
-      const uint16_t *src = ok ? Wp + ((size_t)(n8_0 + pnl) * K + k0 + k) * 8 : Wp;
-      cp_async16_zfill(ws_b + (uint32_t)((slot * WH + k * BN + pnl * 8) * 2), src, ok);
+#pragma unroll
+    for (int r = 0; r < (WCH + NT - 1) / NT; ++r) {  // W: KT x BN/8 panels of 8 bf16, to [k][n]
+      const int c = tid + r * NT, k = c / (BN / 8), pnl = c % (BN / 8);
+      if (c < WCH) {
+        const bool ok = (k0 + k < K) && (n8_0 + pnl < N8);
+        const uint16_t *src = ok ? Wp + ((size_t)(n8_0 + pnl) * K + k0 + k) * 8 : Wp;
+        cp_async16_zfill(ws_b + (uint32_t)((slot * WH + k * BN + pnl * 8) * 2), src, ok);
+      }
     }
   };
   float2 acc[TMR][TNP];
@@ -623,24 +656,35 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
     if (kt + BIG_STAGES - 1 < nk) issue(kt + BIG_STAGES - 1);
     cp_async_commit();
     const int slot = kt % BIG_STAGES;
-    const float *xs = Xs + slot * XF + ty * 4;
-    const uint16_t *ws = Ws + slot * WH + tx * 4;
+    const float *xs = Xs + slot * XF + ty * RW;
+    const uint16_t *ws = Ws + slot * WH + tx * CW;
 #pragma unroll
     for (int k = 0; k < BIG_KT; ++k) {
       float x[TMR];
 #pragma unroll
-      for (int g = 0; g < TMR / 4; ++g) {
-        const float4 xv = *reinterpret_cast<const float4 *>(xs + k * BIG_BM + g * 64);
-        x[4 * g] = xv.x; x[4 * g + 1] = xv.y; x[4 * g + 2] = xv.z; x[4 * g + 3] = xv.w;
+      for (int g = 0; g < RB; ++g) {
+        if (RW == 4) {
+          const float4 xv = *reinterpret_cast<const float4 *>(xs + k * BM + g * RW * TY);
+          x[4 * g] = xv.x; x[4 * g + 1] = xv.y; x[4 * g + 2] = xv.z; x[4 * g + 3] = xv.w;
+        } else {
+          const float2 xv = *reinterpret_cast<const float2 *>(xs + k * BM + g * RW * TY);
+          x[2 * g] = xv.x; x[2 * g + 1] = xv.y;
+        }
       }
-      float w[2 * TNP];
+      float w[TNC];
 #pragma unroll
-      for (int h = 0; h < TNP / 2; ++h) {
-        const uint2 wv = *reinterpret_cast<const uint2 *>(ws + k * BN + 64 * h);
-        w[4 * h] = __uint_as_float(wv.x << 16);
-        w[4 * h + 1] = __uint_as_float(wv.x & 0xffff0000u);
-        w[4 * h + 2] = __uint_as_float(wv.y << 16);
-        w[4 * h + 3] = __uint_as_float(wv.y & 0xffff0000u);
+      for (int h = 0; h < CB; ++h) {
+        if (CW == 4) {
+          const uint2 wv = *reinterpret_cast<const uint2 *>(ws + k * BN + CW * TX * h);
+          w[4 * h] = __uint_as_float(wv.x << 16);
+          w[4 * h + 1] = __uint_as_float(wv.x & 0xffff0000u);
+          w[4 * h + 2] = __uint_as_float(wv.y << 16);
+          w[4 * h + 3] = __uint_as_float(wv.y & 0xffff0000u);
+        } else {
+          const uint32_t wv = *reinterpret_cast<const uint32_t *>(ws + k * BN + CW * TX * h);
+          w[2 * h] = __uint_as_float(wv << 16);
+          w[2 * h + 1] = __uint_as_float(wv & 0xffff0000u);
+        }
       }
 #pragma unroll
       for (int i = 0; i < TMR; ++i)
@@ -653,50 +697,90 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   float *Yb = Y + (y_slot ? (size_t)(*y_slot) * y_slot_stride : 0);
 #pragma unroll
   for (int i = 0; i < TMR; ++i) {
-    const int m = m0 + (i / 4) * 64 + ty * 4 + (i % 4);
+    const int m = m0 + (i / RW) * RW * TY + ty * RW + (i % RW);
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < TNP; ++j) {
-      const int n = n0 + 64 * (j / 2) + tx * 4 + 2 * (j % 2);
+      const int n = n0 + (2 * j / CW) * CW * TX + tx * CW + (2 * j) % CW;
       float2 v = acc[i][j];
+      if (glu) {
+        if (n < N) Yb[(size_t)m * ysm + (size_t)(n / 2) * ysn] = fmul(silu_pinned(v.x), v.y);
+        continue;
+      }
       if (R) {  // residual h + o (cis2_model.h:540-542)
         if (n < N) v.x = fadd(R[(size_t)m * ldr + n], v.x);
         if (n + 1 < N) v.y = fadd(R[(size_t)m * ldr + n + 1], v.y);
       }
-      if (n < N) Yb[(size_t)m * ldy + n] = v.x;
-      if (n + 1 < N) Yb[(size_t)m * ldy + n + 1] = v.y;
+      if (n < N) Yb[(size_t)m * ysm + (size_t)n * ysn] = v.x;
+      if (n + 1 < N) Yb[(size_t)m * ysm + (size_t)(n + 1) * ysn] = v.y;
     }
   }
 }
 
-template <int BIG_BM, int BN>
-static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
-                         const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s) {
-  const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BIG_BM * 4 + BIG_KT * BN * 2);
+template <int TY, int TX, int TMR, int TNC>
+static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ysm, int ysn,
+                         const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
+                         cudaStream_t s) {
+  constexpr int BM = TMR * TY, BN = TNC * TX;
+  const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BM * 4 + BIG_KT * BN * 2);
   static SmemLimit lim;
-  lim.ensure(k_gemm_big<BIG_BM, BN>, smem);
-  dim3 grid((N + BN - 1) / BN, (M + BIG_BM - 1) / BIG_BM);
-  k_gemm_big<BIG_BM, BN><<<grid, BIG_THREADS, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ldy, R, ldr, y_slot,
-                                                        y_slot_stride);
+  lim.ensure(k_gemm_big<TY, TX, TMR, TNC>, smem);
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  k_gemm_big<TY, TX, TMR, TNC><<<grid, TY * TX, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ysm, ysn, R, ldr, y_slot,
+                                                           y_slot_stride, glu);
 }
 
-// Block tile choice for the sequential prompt-pass product, from 64 rows on.
-// Measured on B200, the 128 x 128, 128 x 64, 64 x 128 and 64 x 64 tiles run
-// their blocks at nearly the same rate per output (the 64-row ones about 5 %
-// slower), two blocks per SM, so the time is set by how many waves of
-// 2 x 148 blocks a tile needs: cost = waves x tile area / rate.  128 x 128
-// and 64 x 128 never beat the narrower tile of the same height by that
-// measure (at best they tie), so the choice is between:
-// - 128 x 64: e.g. the 576-wide projections of 4,096 rows (0.71-0.75 of the
-//   FP32 pipe, against 0.57-0.60 for k_gemm_t and 0.37 for 128 x 128), and
-//   the 2,304- to 6,144-wide ones (0.79, as fast as 128 x 128);
-// - 64 x 64: e.g. lm_head over 64 or 300 rows (0.63 and 0.71, against 0.55
-//   and 0.40 for the decode kernel).
-// Returns the tile height.
-int gemm_big_rows(int M, int N) {
-  const long w128 = ((long)((M + 127) / 128) * ((N + 63) / 64) + 2 * 148 - 1) / (2 * 148);
-  const long w64 = ((long)((M + 63) / 64) * ((N + 63) / 64) + 2 * 148 - 1) / (2 * 148);
-  return (double)w128 * 128 * 64 < (double)w64 * 64 * 64 / 0.95 ? 128 : 64;
+// Block tile choice for the sequential product from 64 rows on (the prompt
+// pass, lm_head, and decode steps with many rows).  No dot product may be
+// split, so M x N chains are all the parallelism there is; a tile trades
+// chains per thread (fewer loads per product, fewer issue slots) against
+// warps (every scheduler of every SM needs work).  Cost = the largest
+// per-SM share of the outputs over the fraction of its FP32 pipe the SM's
+// warps can keep busy: one warp per scheduler suffices from 8 chains per
+// thread on, two from 4, and issue efficiency falls a little with the
+// chains per thread.  Measured on B200 (128 x 64 and 64 x 64 tiles, 32 and
+// 16 chains): 0.71-0.81 of the FP32 pipe on the 576- to 6,144-wide
+// projections of 4,096 rows, 0.63-0.71 on lm_head over 64-300 rows.
+struct BigCfg { int ty, tx, tmr, tnc; };
+static const BigCfg kBigTiles[] = {{16, 16, 8, 4}, {16, 16, 4, 4}, {16, 8, 4, 4}, {8, 16, 4, 4},
+                                   {8, 8, 4, 4},   {16, 8, 4, 2},  {8, 16, 2, 2}};
+constexpr int kNumBigTiles = 7;
+
+int gemm_big_choice(int M, int N) {
+  int best = 0;
+  double best_cost = 0;
+  for (int i = 0; i < kNumBigTiles; ++i) {
+    const BigCfg &c = kBigTiles[i];
+    const int bm = c.tmr * c.ty, bn = c.tnc * c.tx, nt = c.ty * c.tx, chains = c.tmr * c.tnc;
+    if (i > 0 && M < bm / 2) continue;  // at most half a row tile wasted
+    const long blocks = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+    const long per_sm = (blocks + 147) / 148;
+    const double warps = (double)per_sm * nt / 32.0;
+    const double need = chains >= 8 ? 4.0 : 8.0;
+    const double busy = warps < need ? warps / need : 1.0;
+    const double eff = chains >= 32 ? 1.0 : chains >= 16 ? 0.95 : chains >= 8 ? 0.9 : 0.8;
+    const double cost = (double)per_sm * bm * bn / (busy * eff);
+    if (i == 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
+  }
+  return best;
+}
+
+void launch_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ysm, int ysn,
+                     const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
+                     cudaStream_t s) {
+  if (M <= 0 || N <= 0) return;
+#define CIS2B_BIG(TY_, TX_, TMR_, TNC_) \
+  run_gemm_big<TY_, TX_, TMR_, TNC_>(XT, ldm, Wp, K, N, M, Y, ysm, ysn, resid, ldr, y_slot, y_slot_stride, glu, s)
+  switch (gemm_big_choice(M, N)) {
+    case 0: CIS2B_BIG(16, 16, 8, 4); break;
+    case 1: CIS2B_BIG(16, 16, 4, 4); break;
+    case 2: CIS2B_BIG(16, 8, 4, 4); break;
+    case 3: CIS2B_BIG(8, 16, 4, 4); break;
+    case 4: CIS2B_BIG(8, 8, 4, 4); break;
+    case 5: CIS2B_BIG(16, 8, 4, 2); break;
+    default: CIS2B_BIG(8, 16, 2, 2); break;
+  }
+#undef CIS2B_BIG
 }
 
 void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
@@ -704,10 +788,7 @@ void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int
                  cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
   if (!tree && M >= 64) {
-    if (gemm_big_rows(M, N) == 128)
-      run_gemm_big<128, 64>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s);
-    else
-      run_gemm_big<64, 64>(XT, ldm, Wp, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, s);
+    launch_gemm_big(XT, ldm, Wp, K, N, M, Y, ldy, 1, resid, ldr, y_slot, y_slot_stride, 0, s);
     return;
   }
   // Fewer rows, or tree mode: SIMT register tiles (tree mode with the
@@ -735,19 +816,22 @@ void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int
 #undef CIS2B_GEMM
 }
 
-// Wp[n8][k][j] = W[8*n8 + j][k] (zero rows past N): the panel layout above.
-__global__ void k_panelize(const uint16_t *W, int N, int K, uint16_t *Wp) {
+// Wp[n8][k][j] = W[src(8*n8 + j)][k] (zero rows past N): the panel layout
+// above, src(n) = n, or for a gate/up pair (il_half = I, N = 2I) the rows
+// interleaved, src(2i) = i (gate), src(2i + 1) = I + i (up).
+__global__ void k_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, int il_half) {
   const size_t N8 = (size_t)(N + 7) / 8;
   const size_t total = N8 * (size_t)K * 8;
   for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
     const size_t j = idx % 8, k = (idx / 8) % K, n8 = idx / (8 * (size_t)K);
     const size_t n = n8 * 8 + j;
-    Wp[idx] = n < (size_t)N ? W[n * K + k] : (uint16_t)0;
+    const size_t src = il_half ? ((n & 1) ? (size_t)il_half + n / 2 : n / 2) : n;
+    Wp[idx] = n < (size_t)N ? W[src * K + k] : (uint16_t)0;
   }
 }
-void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s) {
-  k_panelize<<<1184, 256, 0, s>>>(W, N, K, Wp);
+void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s, int il_half) {
+  k_panelize<<<1184, 256, 0, s>>>(W, N, K, Wp, il_half);
 }
 size_t panel_elems(int N, int K) { return (size_t)((N + 7) / 8) * 8 * (size_t)K; }
 
@@ -792,14 +876,6 @@ void launch_tile32(const uint16_t *W, int N, int K, uint16_t *Wt, cudaStream_t s
   k_tile32<<<1184, 256, 0, s>>>(W, N, K, Wt, glu_half);
 }
 
-__device__ __forceinline__ float2 fmul_pair(float a0, float a1, float b0, float b1) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rr;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mul.rn.ftz.f32x2 rr, ra, rb;\n\tmov.b64 {%0, %1}, rr;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-  return r;
-}
 __device__ __forceinline__ float4 widen4(uint2 u) {
   return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));

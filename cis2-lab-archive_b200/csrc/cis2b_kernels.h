@@ -34,8 +34,18 @@ void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n
 void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
                  const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s);
+// The many-row form behind launch_gemm (sequential order, M >= 64): Y[m * ysm
+// + n * ysn], so the output may be written k-major for the next product.
+// glu: Wp is a gate/up pair panelised with il_half = I (N = 2I); the output
+// is silu(gate) * up, I columns.
+void launch_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ysm, int ysn,
+                     const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
+                     cudaStream_t s);
+int gemm_big_choice(int M, int N);
 // Wp[n8][k][j] = W[8*n8 + j][k], zero rows past N; Wp holds panel_elems(N, K) bf16.
-void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s);
+// il_half = I > 0 (N = 2I): rows interleaved, panel row 2i = W row i (gate),
+// 2i + 1 = W row I + i (up).
+void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s, int il_half = 0);
 size_t panel_elems(int N, int K);
 
 // Decode form of the same product for few rows (sequential order only).  X is
@@ -88,6 +98,7 @@ void launch_attention_rows(const float *qkv, int ld, const int2 *tiles, int n_ti
                            float *att, int ars, int acs, int max_len, cudaStream_t s);
 // Index of the GEMM tile the dispatcher picks for (M, N, K).
 int gemm_tile_choice(int M, int N, int K, bool tree);
+// gu rows [rows][2I] with gate i at 2i and up i at 2i + 1 (interleaved panels).
 void launch_silu_mul(const float *gu, int I, int rows, float *hid, int hrs, int hcs, cudaStream_t s);
 void launch_add_bias(float *x, int ld, int rows, const uint16_t *b, int n, cudaStream_t s);
 

@@ -93,6 +93,9 @@ constexpr int PREFILL_CHUNK = 8192;            // rows per prefill pass
 // 49,152 x 576, 557 vs 985 us at 300 x 32,000 x 768; 737 vs 629 us for the
 // decode GEMM at 32 x 151,936 x 1,024).
 constexpr int DEC_HEAD_ROWS = 48;
+// Decode-step rows from which the layer products leave the few-row kernel
+// for the register-tiled one (k-major activations).
+constexpr int DEC_BIG_ROWS = 128;
 constexpr size_t RING_BUDGET = 8ull << 30;     // bytes of logits kept for the witness
 
 }  // namespace
@@ -111,6 +114,7 @@ struct cis2b_model {
   DevBuf tiles;   // the same weights in 32-column tiles for the decode GEMM
   const uint16_t *lm_head_t = nullptr;
   bool dec_tiles = false;  // decode steps use launch_gemm_dec (sequential mode, K % 4 == 0)
+  int dec_big_rows = DEC_BIG_ROWS;  // ... below this many rows (above: the register-tiled product)
   DevBuf inv_freq, cos_t, sin_t;
   cudaStream_t s_main = nullptr, s_sha = nullptr, s_prep = nullptr;
   // workspace
@@ -283,6 +287,7 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   if (o.max_positions < 0) return fail(CIS2B_ERR_ARG, "max_positions < 0");
   m->dev = o.device;
   m->tree = o.reduction == CIS2B_REDUCTION_TREE;
+  if (const char *e = getenv("CIS2B_DEC_BIG_ROWS")) m->dec_big_rows = atoi(e);  // tuning override
   m->max_pos = o.max_positions ? o.max_positions : 4096;
 
   // Everything up to the upload is host work, so artifact and config errors
@@ -495,7 +500,7 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
       w.pdown = pat(offs[4 * l + 3]);
       launch_panelize(w.wqkv, NQKV, m->H, const_cast<uint16_t *>(w.pqkv), m->s_main);
       launch_panelize(w.wo, m->H, m->QD, const_cast<uint16_t *>(w.po), m->s_main);
-      launch_panelize(w.wgu, 2 * m->I, m->H, const_cast<uint16_t *>(w.pgu), m->s_main);
+      launch_panelize(w.wgu, 2 * m->I, m->H, const_cast<uint16_t *>(w.pgu), m->s_main, m->I);  // gate/up interleaved
       launch_panelize(w.wdown, m->H, m->I, const_cast<uint16_t *>(w.pdown), m->s_main);
     }
     m->lm_head_p = pat(off_lmp);
@@ -610,9 +615,12 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
   RowMap rm{seq, pos};
   launch_embed(m->embed, H, tok, rows, h, s);
   m->launches += 1;
-  // Decode steps in sequential mode run the GEMMs in the few-row form: its
-  // activations are row-major, so every producer writes (row stride K, 1).
-  const bool dec = decode && m->dec_tiles;
+  // Decode steps in sequential mode with fewer than dec_big_rows rows run the
+  // GEMMs in the few-row form: its activations are row-major, so every
+  // producer writes (row stride K, 1).  Everything else -- the prompt pass,
+  // tree mode, and decode steps with many rows -- uses k-major operands and
+  // the register-tiled product.
+  const bool dec = decode && m->dec_tiles && rows < m->dec_big_rows;
   const int lnr = dec ? H : 1, lnc = dec ? 1 : ldm;      // ln / att / hid (row, column) strides
   const int atr = dec ? QD : 1, hir = dec ? I : 1;
   auto gemm = [&](const float *X, const uint16_t *Wp, const uint16_t *Wt, int K, int N, float *Y, int ldy,
@@ -649,6 +657,9 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     if (dec) {  // SwiGLU in the gate/up GEMM's epilogue
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
       launch_gemm_dec(ln, H, w.tgu, H, 2 * I, rows, hid, I, nullptr, 0, nullptr, 0, s, I);
+    } else if (!m->tree && rows >= 64) {  // SwiGLU in the epilogue, hid written k-major
+      ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
+      launch_gemm_big(ln, ldm, w.pgu, H, 2 * I, rows, hid, 1, ldm, nullptr, 0, nullptr, 0, 1, s);
     } else {
       gemm(ln, w.pgu, w.tgu, H, 2 * I, gu, 2 * I, nullptr, 0);
       launch_silu_mul(gu, I, rows, hid, hir, ldm, s);
@@ -1244,8 +1255,8 @@ int trace_impl(cis2b_model *m, const uint32_t *ids, uint32_t n_ids, const char *
       launch_rmsnorm(h, H, w.post_norm, m->eps, H, 1, m->tree, ln, 1, ldm, s);
       EMIT(pos, l, "norm2", ln, (size_t)H, (size_t)ldm);
       launch_gemm(ln, ldm, w.pgu, H, 2 * I, 1, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s);
-      EMIT(pos, l, "gate", gu, (size_t)I, 1);
-      EMIT(pos, l, "up", gu + I, (size_t)I, 1);
+      EMIT(pos, l, "gate", gu, (size_t)I, 2);  // gate and up interleaved (launch_panelize)
+      EMIT(pos, l, "up", gu + 1, (size_t)I, 2);
       launch_silu_mul(gu, I, 1, hid, 1, ldm, s);
       EMIT(pos, l, "silu_mul", hid, (size_t)I, (size_t)ldm);
       launch_gemm(hid, ldm, w.pdown, I, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
@@ -1434,6 +1445,11 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
   CU_LAUNCHED();
   CU(cudaMemcpy(Y, dy.p, 4 * (size_t)rows * n_out, cudaMemcpyDeviceToHost));
   return CIS2B_OK;
+}
+
+int cis2b_op_gemm_tile(int32_t rows, int32_t n_out) {
+  if (rows < 64 || n_out <= 0) return fail(CIS2B_ERR_ARG, "rows >= 64 and n_out >= 1"), -1;
+  return gemm_big_choice(rows, n_out);
 }
 
 int cis2b_op_sha256_stream(int32_t device, const uint8_t *prefix, size_t prefix_len, const uint32_t *words,

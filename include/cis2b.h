@@ -200,6 +200,10 @@ int cis2b_op_pinned_map(int32_t device, int32_t fn, const float *x, float *y, si
 #define CIS2B_OP_MATMUL_DECODE 2
 int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t rows, int32_t n_out,
                     int32_t k, int32_t reduction, float *Y);
+/* Index (0-based) of the register tile the many-row product picks for
+ * rows x n_out (sequential order, rows >= 64), or -1; lets the parity tests
+ * confirm that their shapes reach every tile of that kernel. */
+int cis2b_op_gemm_tile(int32_t rows, int32_t n_out);
 /* Witness stream check: absorbs `prefix` (byte path), then n_chunks chunks of
  * chunk_words u32 words through the device step path (last word of each
  * chunk plays the token id); writes the digest after each chunk. */

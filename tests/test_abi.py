@@ -304,3 +304,15 @@ def test_config_json_strings_and_numbers(pkg, synth, synth_root, tmp_path):
                 pkg.lib().cis2b_free(h)
         else:
             assert rc == 2 and "config.json" in msg, (extra, rc, msg)
+
+
+def test_matmul_shapes_reach_every_register_tile(pkg):
+    """The bit-exact GEMM shapes (tests/test_gpu_kernels.py SHAPES) reach every
+    tile of the register-tiled product; the tile choice is host code, so
+    this runs without a device."""
+    from test_gpu_kernels import BIG_TILES, SHAPES
+    L = pkg.lib()
+    L.cis2b_op_gemm_tile.argtypes = [ctypes.c_int32, ctypes.c_int32]
+    seen = {int(L.cis2b_op_gemm_tile(m, n)) for m, n, _ in SHAPES if m >= 64}
+    assert seen == set(range(len(BIG_TILES))), sorted(seen)
+    assert L.cis2b_op_gemm_tile(63, 100) == -1
