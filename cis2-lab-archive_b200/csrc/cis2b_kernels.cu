@@ -610,6 +610,7 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   constexpr int TNP = TNC / 2;     // column pairs per thread
   constexpr int XCH = XF / 4;      // 16-byte X chunks per stage
   constexpr int WCH = WH / 8;      // 16-byte W chunks per stage
+  constexpr int PF = TMR * TNC >= 16 ? 2 : 4;  // register prefetch distance, k-steps
   static_assert((RW == 2 || RW == 4) && (CW == 2 || CW == 4) && BM % 4 == 0 && BN % 8 == 0, "tile shape");
   extern __shared__ __align__(16) float smem[];
   float *Xs = smem;                                                     // [S][KT][BM]
@@ -658,34 +659,46 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
     const int slot = kt % BIG_STAGES;
     const float *xs = Xs + slot * XF + ty * RW;
     const uint16_t *ws = Ws + slot * WH + tx * CW;
-#pragma unroll
-    for (int k = 0; k < BIG_KT; ++k) {
-      float x[TMR];
+    // The operands of the next PF k-steps are loaded into registers ahead of
+    // the products that use them: with few warps per scheduler (the decode
+    // steps) nothing else hides the shared-memory latency.
+    float xb[PF][TMR];
+    uint32_t wb[PF][TNC / 2];
+    auto ld = [&](int b, int k) {
 #pragma unroll
       for (int g = 0; g < RB; ++g) {
         if (RW == 4) {
           const float4 xv = *reinterpret_cast<const float4 *>(xs + k * BM + g * RW * TY);
-          x[4 * g] = xv.x; x[4 * g + 1] = xv.y; x[4 * g + 2] = xv.z; x[4 * g + 3] = xv.w;
+          xb[b][4 * g] = xv.x; xb[b][4 * g + 1] = xv.y; xb[b][4 * g + 2] = xv.z; xb[b][4 * g + 3] = xv.w;
         } else {
           const float2 xv = *reinterpret_cast<const float2 *>(xs + k * BM + g * RW * TY);
-          x[2 * g] = xv.x; x[2 * g + 1] = xv.y;
+          xb[b][2 * g] = xv.x; xb[b][2 * g + 1] = xv.y;
         }
       }
-      float w[TNC];
 #pragma unroll
       for (int h = 0; h < CB; ++h) {
         if (CW == 4) {
           const uint2 wv = *reinterpret_cast<const uint2 *>(ws + k * BN + CW * TX * h);
-          w[4 * h] = __uint_as_float(wv.x << 16);
-          w[4 * h + 1] = __uint_as_float(wv.x & 0xffff0000u);
-          w[4 * h + 2] = __uint_as_float(wv.y << 16);
-          w[4 * h + 3] = __uint_as_float(wv.y & 0xffff0000u);
+          wb[b][2 * h] = wv.x; wb[b][2 * h + 1] = wv.y;
         } else {
-          const uint32_t wv = *reinterpret_cast<const uint32_t *>(ws + k * BN + CW * TX * h);
-          w[2 * h] = __uint_as_float(wv << 16);
-          w[2 * h + 1] = __uint_as_float(wv & 0xffff0000u);
+          wb[b][h] = *reinterpret_cast<const uint32_t *>(ws + k * BN + CW * TX * h);
         }
       }
+    };
+#pragma unroll
+    for (int q = 0; q < PF; ++q) ld(q, q);
+#pragma unroll
+    for (int k = 0; k < BIG_KT; ++k) {
+      const int b = k % PF;
+      float x[TMR], w[TNC];
+#pragma unroll
+      for (int i = 0; i < TMR; ++i) x[i] = xb[b][i];
+#pragma unroll
+      for (int j = 0; j < TNC / 2; ++j) {  // bf16 pair -> two fp32 (exact widen)
+        w[2 * j] = __uint_as_float(wb[b][j] << 16);
+        w[2 * j + 1] = __uint_as_float(wb[b][j] & 0xffff0000u);
+      }
+      if (k + PF < BIG_KT) ld(b, k + PF);
 #pragma unroll
       for (int i = 0; i < TMR; ++i)
 #pragma unroll
