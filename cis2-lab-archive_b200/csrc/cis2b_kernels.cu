@@ -1168,6 +1168,14 @@ __device__ __forceinline__ float max_comb(float a, float b) {
 // (coalesced loads); one thread owns each (head, position) dot product and
 // each (head, d) V-mix chain.
 constexpr int ATT_JC = 64;
+// K/V ring depth of the decode-step attention (k_attention_dec).  Measured
+// on B200 (C5 shape, 256 rows at position ~1,535): 2 slots 155 us, 3 slots
+// 169 us, 4 slots 174 us: a deeper ring costs CTAs per SM (shared memory),
+// and the kernel is bound by its serial chains and their waits, not by HBM
+// (the same launch with every K/V chunk served from L2 takes as long).  A
+// ring filled by per-position bulk copies (cp.async.bulk + mbarrier) took
+// 274 us.
+constexpr int ATT_DEC_STAGES = 2;
 
 size_t attention_smem_floats(int G, int hd, int max_len) {
   const size_t scs = ((size_t)max_len + 3) & ~(size_t)3;  // score rows start 16-byte aligned
@@ -1175,6 +1183,11 @@ size_t attention_smem_floats(int G, int hd, int max_len) {
   f = (f + 3) & ~(size_t)3;                              // tiles start 16-byte aligned
   return f + (size_t)2 * ATT_JC * (hd + 4);
 }
+
+bool launch_attention_dec(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd, float *kcache,
+                          float *vcache, int max_pos, float *att, int ars, int acs, int max_len,
+                          const uint16_t *q_norm, const uint16_t *k_norm, float eps, const float *cos_t,
+                          const float *sin_t, cudaStream_t s);
 
 __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
                             int nh, int nkv, int hd, float *kc, float *vc, int max_pos,
@@ -1378,6 +1391,10 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
                       const uint16_t *k_norm, float eps, const float *cos_t, const float *sin_t,
                       cudaStream_t s, float *dbg) {
   if (rows <= 0) return;
+  if (!tree && fuse_post && !dbg &&
+      launch_attention_dec(qkv, ld, rows, rm, n_heads, n_kv, hd, kcache, vcache, max_pos, att, ars, acs, max_len,
+                           q_norm, k_norm, eps, cos_t, sin_t, s))
+    return;
   const int G = n_heads / n_kv;
   int nt = ((G * hd + 31) / 32) * 32;
   if (nt < 128) nt = 128;
@@ -1388,6 +1405,243 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
   k_attention<<<grid, nt, smem, s>>>(qkv, ld, rm.seq, rm.pos, n_heads, n_kv, hd, kcache, vcache, max_pos,
                                      tree ? 1 : 0, att, ars, acs, max_len, fuse_post ? 1 : 0, q_norm,
                                      k_norm, eps, cos_t, sin_t, dbg);
+}
+
+// ---- Decode-step attention in sequential mode, specialised on the head
+// size HD and the group G = n_heads / n_kv.  Same CTA grid, same
+// arithmetic in the same order as k_attention (scaled dots, serial-scan
+// max, pinned exp, serial denominator, division, V-mix chains over j
+// ascending), with the index arithmetic resolved at compile time and the
+// K/V chunks streamed through an ST-deep cp.async ring (ST - 1 chunks in
+// flight while one is consumed).  Measured on B200, the generic kernel's
+// integer index arithmetic (divisions by the head size and chunk length per
+// copy and per dot) made the integer pipe its busiest unit, ahead of memory.
+template <int HD, int G>
+struct AttDec {
+  static constexpr int NT = G * HD < 128 ? 128 : G * HD;  // threads: one V-mix chain per (g, d)
+  static constexpr int JC = 64;                           // positions per chunk
+  static constexpr int TS = HD + 4;                       // tile row pitch (floats)
+  static constexpr int NQ = HD / 4;                       // 16-byte pieces per row
+  static constexpr int DPT = (G * JC + NT - 1) / NT;      // dots per thread per chunk
+
+};
+
+size_t attention_dec_smem_floats(int G, int hd, int max_len, int stages) {
+  const size_t scs = ((size_t)max_len + 3) & ~(size_t)3;
+  return (size_t)G * hd + (size_t)G * scs + 64 + (size_t)stages * 64 * (hd + 4);
+}
+
+template <int HD, int G, int ST>
+__global__ void __launch_bounds__(AttDec<HD, G>::NT, 1)
+k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, int nkv, float *kc, float *vc,
+                int max_pos, float *att, int ars, int acs, int max_len, const uint16_t *qn, const uint16_t *kn,
+                float eps, const float *cos_t, const float *sin_t) {
+  using C = AttDec<HD, G>;
+  constexpr int NT = C::NT, JC = C::JC, TS = C::TS, NQ = C::NQ, NW = NT / 32;
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int KV = nkv * HD;
+  const int seq = rseq[r], pos = rpos[r], len = pos + 1;
+  const int scs = (max_len + 3) & ~3;
+  float *q = sm;                       // [G][HD]
+  float *sc = q + G * HD;              // [G][scs]
+  float *red = sc + (size_t)G * scs;   // [64]
+  float *tiles = red + 64;             // [ST][JC][TS]; offset is a multiple of 4 floats
+  {
+    // The row's q/k norm, RoPE and cache append for this KV head (the work
+    // of k_qkv_post; each CTA's row is its sequence's newest position).
+    float *row = qkv + (size_t)r * ld;
+    const int QD = nkv * G * HD, half = HD / 2;
+    const float *ct = cos_t + (size_t)pos * half, *st = sin_t + (size_t)pos * half;
+    for (int hh = warp; hh <= G; hh += NW) {
+      const bool is_k = hh == G;
+      float *x = is_k ? row + QD + (size_t)kvh * HD : row + ((size_t)kvh * G + hh) * HD;
+      const uint16_t *nwt = is_k ? kn : qn;
+      if (nwt) warp_rmsnorm(x, nwt, eps, HD, false, tiles + (size_t)warp * 2 * HD, x);
+      for (int i = lane; i < half; i += 32) {
+        float x1 = x[i], x2 = x[i + half], c = ct[i], sn = st[i];
+        float o1 = fadd(fmul(x1, c), fmul(fneg(x2), sn));
+        float o2 = fadd(fmul(x2, c), fmul(x1, sn));
+        x[i] = o1;
+        x[i + half] = o2;
+      }
+      __syncwarp();
+      if (is_k) {
+        float *dst = kc + ((size_t)seq * max_pos + pos) * KV + (size_t)kvh * HD;
+        for (int i = lane; i < HD; i += 32) dst[i] = x[i];
+      }
+    }
+    const float *vsrc = row + QD + KV + (size_t)kvh * HD;
+    float *vdst = vc + ((size_t)seq * max_pos + pos) * KV + (size_t)kvh * HD;
+    for (int i = tid; i < HD; i += NT) vdst[i] = vsrc[i];
+    __syncthreads();
+  }
+  for (int i = tid; i < G * HD; i += NT) q[i] = qkv[(size_t)r * ld + (size_t)kvh * G * HD + i];
+  const float scale = rsqrt_cr(__int2float_rn(HD));
+  const float *kbase = kc + (size_t)seq * max_pos * KV + (size_t)kvh * HD;
+  const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * HD;
+  const int nch = (len + JC - 1) / JC;
+  const uint32_t tbase = (uint32_t)__cvta_generic_to_shared(tiles);
+  auto stage = [&](const float *base, int c) {  // rows [c*JC, c*JC + JC) -> ring slot c % ST
+    if (c < nch) {
+      const int j0 = c * JC, jc = min(JC, len - j0), buf = c % ST;
+      for (int i = tid; i < jc * NQ; i += NT) {
+        const int jj = i / NQ, q4 = i % NQ;
+        cp_async16(tbase + (uint32_t)(((buf * JC + jj) * TS + 4 * q4) * 4), base + (size_t)(j0 + jj) * KV + 4 * q4);
+      }
+    }
+    cp_async_commit();  // empty groups keep the count uniform
+  };
+  // Waits until chunk c sits in its slot (every thread's copies), then a barrier.
+  auto land = [&](int) {
+    cp_async_wait<ST - 2>();
+    __syncthreads();
+  };
+#pragma unroll
+  for (int c = 0; c < ST - 1; ++c) stage(kbase, c);
+  __syncthreads();  // q visible
+
+  // ---- scores: thread (g, jj) = (pr / JC, pr % JC) of each chunk; q from
+  // shared memory (a broadcast load: all lanes of a warp share g)
+  for (int c = 0; c < nch; ++c) {
+    land(c);
+    stage(kbase, c + ST - 1);  // its slot was last read in chunk c - 1
+    const int j0 = c * JC, jc = min(JC, len - j0);
+    const float *tile = tiles + (size_t)(c % ST) * JC * TS;
+#pragma unroll
+    for (int u = 0; u < C::DPT; ++u) {
+      const int pr = tid + u * NT, g = pr / JC, jj = pr % JC;
+      if (g < G && jj < jc) {
+        const float4 *k4 = reinterpret_cast<const float4 *>(tile + jj * TS);
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NQ; ++i) {
+          const float4 b = k4[i];
+          const float4 a = reinterpret_cast<const float4 *>(q + g * HD)[i];
+          d = fadd(d, fmul(a.x, b.x));
+          d = fadd(d, fmul(a.y, b.y));
+          d = fadd(d, fmul(a.z, b.z));
+          d = fadd(d, fmul(a.w, b.w));
+        }
+        sc[(size_t)g * scs + j0 + jj] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
+      }
+    }
+  }
+  __syncthreads();  // every ring slot is free again
+#pragma unroll
+  for (int c = 0; c < ST - 1; ++c) stage(vbase, c);  // V chunks load while the softmax runs
+
+  // ---- softmax (serial-scan max, pinned exp, serial denominator, divide)
+  for (int g = warp; g < G; g += NW) {
+    const float *sg = sc + (size_t)g * scs;
+    float m = bitsf(0x7fc00000u);
+    for (int j = lane; j < len; j += 32) m = max_comb(m, sg[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max_comb(m, __shfl_xor_sync(FULL, m, o));
+    if (lane == 0) red[g] = is_nan(sg[0]) ? sg[0] : m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float *sg = sc + (size_t)g * scs;
+    const float mg = red[g];
+    for (int j = tid; j < len; j += NT) sg[j] = exp_pinned(fsub(sg[j], mg));
+  }
+  __syncthreads();
+  if (tid < G * 32 && lane == 0) red[32 + warp] = serial_sum4(sc + (size_t)warp * scs, len);
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float *sg = sc + (size_t)g * scs;
+    const float den = red[32 + g];
+    for (int j = tid; j < len; j += NT) sg[j] = fdiv(sg[j], den);
+  }
+
+  // ---- V-mix: thread (g, d) = (tid / HD, tid % HD), j ascending
+  const int g = tid / HD, d = tid % HD;
+  const bool owns = tid < G * HD;
+  float acc = 0.0f;
+  for (int c = 0; c < nch; ++c) {
+    land(c);
+    stage(vbase, c + ST - 1);
+    const int j0 = c * JC, jc = min(JC, len - j0);
+    const float *tile = tiles + (size_t)(c % ST) * JC * TS + d;
+    if (owns) {
+      const float *pg = sc + (size_t)g * scs + j0;  // j0 % 4 == 0: 16-byte aligned
+      if (jc == JC) {
+        // Full chunk: the weights and values of the next two groups of four
+        // positions are loaded while the chain consumes the current group.
+        float4 pw[2];
+        float vv[2][4];
+        auto ld = [&](int b, int jj) {
+          pw[b] = *reinterpret_cast<const float4 *>(pg + jj);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) vv[b][u] = tile[(jj + u) * TS];
+        };
+        ld(0, 0);
+        ld(1, 4);
+#pragma unroll
+        for (int qd = 0; qd < JC / 4; ++qd) {
+          const int b = qd & 1;
+          const float4 w = pw[b];
+          const float v0 = vv[b][0], v1 = vv[b][1], v2 = vv[b][2], v3 = vv[b][3];
+          if (qd + 2 < JC / 4) ld(b, 4 * (qd + 2));
+          acc = fadd(acc, fmul(w.x, v0));
+          acc = fadd(acc, fmul(w.y, v1));
+          acc = fadd(acc, fmul(w.z, v2));
+          acc = fadd(acc, fmul(w.w, v3));
+        }
+      } else {
+        int jj = 0;
+        for (; jj + 4 <= jc; jj += 4) {
+          const float4 w = *reinterpret_cast<const float4 *>(pg + jj);
+          const float v0 = tile[jj * TS], v1 = tile[(jj + 1) * TS], v2 = tile[(jj + 2) * TS], v3 = tile[(jj + 3) * TS];
+          acc = fadd(acc, fmul(w.x, v0));
+          acc = fadd(acc, fmul(w.y, v1));
+          acc = fadd(acc, fmul(w.z, v2));
+          acc = fadd(acc, fmul(w.w, v3));
+        }
+        for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * TS]));
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (owns) att[(size_t)r * ars + ((size_t)kvh * G + g) * HD * acs + (size_t)d * acs] = acc;
+}
+
+template <int HD, int G, int ST>
+static void run_attention_dec(float *qkv, int ld, int rows, RowMap rm, int n_kv, float *kc, float *vc, int max_pos,
+                              float *att, int ars, int acs, int max_len, const uint16_t *qn, const uint16_t *kn,
+                              float eps, const float *cos_t, const float *sin_t, cudaStream_t s) {
+  const size_t smem = attention_dec_smem_floats(G, HD, max_len, ST) * sizeof(float);
+  static SmemLimit lim;
+  lim.ensure(k_attention_dec<HD, G, ST>, smem);
+  k_attention_dec<HD, G, ST><<<dim3(rows, n_kv), AttDec<HD, G>::NT, smem, s>>>(
+      qkv, ld, rm.seq, rm.pos, n_kv, kc, vc, max_pos, att, ars, acs, max_len, qn, kn, eps, cos_t, sin_t);
+}
+
+// Decode-step attention through the specialised kernel when it covers the
+// shape (sequential mode, (head size, group) of the configurations built
+// here); returns false if the caller must use the generic kernel.
+bool launch_attention_dec(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd, float *kcache,
+                          float *vcache, int max_pos, float *att, int ars, int acs, int max_len,
+                          const uint16_t *q_norm, const uint16_t *k_norm, float eps, const float *cos_t,
+                          const float *sin_t, cudaStream_t s) {
+  if (rows <= 0) return true;
+  const int G = n_heads / n_kv;
+  constexpr int ST = ATT_DEC_STAGES;
+#define CIS2B_ATTD(HD_, G_)                                                                                   \
+  if (hd == HD_ && G == G_ && attention_dec_smem_floats(G_, HD_, max_len, ST) * 4 <= 227 * 1024) {            \
+    run_attention_dec<HD_, G_, ST>(qkv, ld, rows, rm, n_kv, kcache, vcache, max_pos, att, ars, acs, max_len, \
+                                   q_norm, k_norm, eps, cos_t, sin_t, s);                                     \
+    return true;                                                                                              \
+  }
+  CIS2B_ATTD(64, 3)
+  CIS2B_ATTD(64, 1)
+  CIS2B_ATTD(128, 2)
+#undef CIS2B_ATTD
+  return false;
 }
 
 // Trace mode: the per-head q/k RMSNorm alone (qwen3-port.diff:66-80), in
