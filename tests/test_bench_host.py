@@ -102,3 +102,30 @@ def test_step_bound_label_follows_the_longer_path():
     assert a["weights_bytes"] == 2 * (m.layers * (m.hidden * (m.q_dim + 2 * m.kv_dim) + m.q_dim * m.hidden
                                                  + 3 * m.inter * m.hidden) + m.vocab * m.hidden)
     assert a["frac"] == pytest.approx(a["achieved"] / peak)
+
+
+def test_stdout_to_stderr_redirects_native_writes(capfd):
+    """Native writes to fd 1 inside the block (NCCL's banner) reach stderr;
+    fd 1 is stdout again afterwards."""
+    import os
+    with bench.stdout_to_stderr():
+        os.write(1, b"native banner\n")
+    os.write(1, b"json line\n")
+    out, err = capfd.readouterr()
+    assert out == "json line\n" and "native banner" in err
+
+
+def test_golden_entries_keep_reduction_modes_apart():
+    """C1 has a sequential and a tree fixture for the same sequence; each
+    mode's parity check must see only its own."""
+    import json
+    import os
+    seq, tree = bench.golden_entries("c1", "sequential"), bench.golden_entries("c1", "tree")
+    with open(os.path.join(bench.GOLDEN_DIR, "c1.json")) as f:
+        want_seq = json.load(f)["sequences"][0]["witness"]
+    with open(os.path.join(bench.GOLDEN_DIR, "c1_tree.json")) as f:
+        want_tree = json.load(f)["sequences"][0]["witness"]
+    assert seq[0]["witness"] == want_seq and tree[0]["witness"] == want_tree
+    assert bench.golden_entries("c2", "tree") == {}
+    assert len(bench.golden_entries("c2", "sequential")) == 512
+
