@@ -53,6 +53,7 @@ CASES = {
     "c1": ("smollm2", ("workload", "c1", 0, 1), 256, False, False),
     "c1_tree": ("smollm2", ("workload", "c1", 0, 1), 256, True, False),
     "c2": ("smollm2", ("workload", "c2", 0, 64), 256, False, False),
+    "c2_tree": ("smollm2", ("workload", "c2", 0, 64), 256, True, False),
     "c3": ("llama160m", ("workload", "c3", 0, 300), 128, False, False),
     "c4": ("qwen3_0p6b", ("workload", "c4", 0, 32), 256, False, True),
     "c5_subset": ("smollm2", ("workload", "c5", 0, 4), 1024, False, False),
