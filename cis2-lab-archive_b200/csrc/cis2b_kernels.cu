@@ -551,16 +551,21 @@ int gemm_tile_choice(int M, int N, int K, bool tree) {
   return best;
 }
 
-// ---- many rows (the prompt pass, and lm_head over 64 rows or more),
-// sequential order: a block tile of up to 128 x 128 outputs over 256
-// threads, up to 8 x 8 per thread.  Per k a thread reads its activations as
-// broadcast 16-byte loads and its weights as 8-byte loads (the activation
-// tile is [k][m], the weight tile [k][n], both conflict-free), then does its
-// multiply-adds; each output still walks k = 0..K-1 in order.  Products are rounded singly and added as pairs of independent
-// accumulators with add.rn.ftz.f32x2, which halves the issue slots the adds
-// take.  Operands arrive through a BIG_STAGES-deep cp.async ring.
-constexpr int BIG_KT = 16, BIG_STAGES = 4;
-
+// ---- many rows (the prompt pass, lm_head over 64 rows or more, and decode
+// steps with many rows), sequential order: a block tile of up to 128 x 64
+// outputs over up to 256 threads, up to 8 x 4 per thread.  Per k a thread
+// reads its activations as broadcast 16-byte loads and its weights as 8- or
+// 16-byte loads (the activation tile is [k][m], the weight tile [k][n], both
+// conflict-free), then does its multiply-adds; each output still walks
+// k = 0..K-1 in order.  Products are rounded singly and added as pairs of
+// independent accumulators with add.rn.ftz.f32x2, which halves the issue
+// slots the adds take.  The weights come from fp32 panels (the checkpoint's
+// bf16 widened once at load, which is exact), so the inner loop spends no
+// issue slots on widening: measured on B200, 4-20 % faster than widening
+// bf16 panels per thread and per k, from 256 x 576 x 576 to 4,096 x 3,072
+// x 576.  Operands arrive through an ST-deep cp.async ring of KT-deep k
+// stages (ST and KT per tile: the few-warp tiles of decode steps gain from
+// 32-deep stages, measured 5-15 % over 16).
 // Two independent, separately rounded products (lanes of one packed op).
 __device__ __forceinline__ float2 fmul_pair(float a0, float a1, float b0, float b1) {
   float2 r;
@@ -585,42 +590,44 @@ __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
 // 4) consecutive rows, RW * TY apart; columns in blocks of CW = min(TNC, 4),
 // CW * TX apart, and columns (n, n + 1) share one packed accumulator.
 // Per k a thread reads its rows' activations (one 8- or 16-byte load per
-// row block) and its columns' weights (one 4- or 8-byte load per column
+// row block) and its columns' weights (one 8- or 16-byte load per column
 // block), forms its products singly and adds them as packed pairs of
 // independent accumulators (add.f32x2): every output still walks
 // k = 0..K-1 in order.  The products stay scalar: with packed products
 // (mul.f32x2) feeding the packed adds, B200 results no longer matched the
 // pinned order bit for bit (measured: most outputs of every tile shape
 // differed), so that pairing is never formed here.
+// Wpf: fp32 panels [N8][K][8] (launch_panelize into float).
 // Output element (m, n) goes to Y[m * ysm + n * ysn] (row-major: ysm = ldy,
 // ysn = 1; k-major for the next product: ysm = 1, ysn = ldm).  glu: W is a
 // gate/up pair panelised with its rows interleaved (gate i, up i at rows 2i,
 // 2i + 1), so a column pair (n, n + 1) is (gate i, up i) and the epilogue
 // writes silu(gate) * up as output column i = n / 2 (cis2_model.h:619-623).
-template <int TY, int TX, int TMR, int TNC>
+template <int TY, int TX, int TMR, int TNC, int ST, int KT>
 __global__ void __launch_bounds__(TY * TX, 1)
-k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ Wp, int K, int N, int M,
+k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf, int K, int N, int M,
            float *__restrict__ Y, int ysm, int ysn, const float *__restrict__ R, int ldr, const int32_t *y_slot,
            size_t y_slot_stride, int glu) {
   constexpr int RW = TMR < 4 ? TMR : 4, RB = TMR / RW;
   constexpr int CW = TNC < 4 ? TNC : 4, CB = TNC / CW;
   constexpr int NT = TY * TX, BM = RW * TY * RB, BN = CW * TX * CB;
-  constexpr int XF = BIG_KT * BM;  // floats per X stage
-  constexpr int WH = BIG_KT * BN;  // bf16 per W stage
+  constexpr int XF = KT * BM;      // floats per X stage
+  constexpr int WF = KT * BN;      // floats per W stage
   constexpr int TNP = TNC / 2;     // column pairs per thread
   constexpr int XCH = XF / 4;      // 16-byte X chunks per stage
-  constexpr int WCH = WH / 8;      // 16-byte W chunks per stage
+  constexpr int WCH = WF / 4;      // 16-byte W chunks per stage
   constexpr int PF = TMR * TNC >= 16 ? 2 : 4;  // register prefetch distance, k-steps
   static_assert((RW == 2 || RW == 4) && (CW == 2 || CW == 4) && BM % 4 == 0 && BN % 8 == 0, "tile shape");
+  static_assert(ST >= 2 && KT % 4 == 0, "pipeline shape");
   extern __shared__ __align__(16) float smem[];
-  float *Xs = smem;                                                     // [S][KT][BM]
-  uint16_t *Ws = reinterpret_cast<uint16_t *>(smem + BIG_STAGES * XF);  // [S][KT][BN]
+  float *Xs = smem;            // [ST][KT][BM]
+  float *Ws = smem + ST * XF;  // [ST][KT][BN]
   const int tid = threadIdx.x, tx = tid % TX, ty = tid / TX;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, n8_0 = n0 / 8;
   const int N8 = (N + 7) / 8;
   const uint32_t xs_b = (uint32_t)__cvta_generic_to_shared(Xs), ws_b = (uint32_t)__cvta_generic_to_shared(Ws);
   auto issue = [&](int kt) {
-    const int slot = kt % BIG_STAGES, k0 = kt * BIG_KT;
+    const int slot = kt % ST, k0 = kt * KT;
 #pragma unroll
     for (int r = 0; r < (XCH + NT - 1) / NT; ++r) {  // X: KT rows of BM floats
       const int c = tid + r * NT, k = c / (BM / 4), q = c % (BM / 4);
@@ -631,12 +638,12 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
       }
     }
 #pragma unroll
-    for (int r = 0; r < (WCH + NT - 1) / NT; ++r) {  // W: KT x BN/8 panels of 8 bf16, to [k][n]
-      const int c = tid + r * NT, k = c / (BN / 8), pnl = c % (BN / 8);
+    for (int r = 0; r < (WCH + NT - 1) / NT; ++r) {  // W: KT x BN/4 halves of 8-column panels, to [k][n]
+      const int c = tid + r * NT, k = c / (BN / 4), h = c % (BN / 4), pnl = h / 2;
       if (c < WCH) {
         const bool ok = (k0 + k < K) && (n8_0 + pnl < N8);
-        const uint16_t *src = ok ? Wp + ((size_t)(n8_0 + pnl) * K + k0 + k) * 8 : Wp;
-        cp_async16_zfill(ws_b + (uint32_t)((slot * WH + k * BN + pnl * 8) * 2), src, ok);
+        const float *src = ok ? Wpf + ((size_t)(n8_0 + pnl) * K + k0 + k) * 8 + (h & 1) * 4 : Wpf;
+        cp_async16_zfill(ws_b + (uint32_t)((slot * WF + k * BN + 4 * h) * 4), src, ok);
       }
     }
   };
@@ -645,25 +652,24 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   for (int i = 0; i < TMR; ++i)
 #pragma unroll
     for (int j = 0; j < TNP; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
-  const int nk = (K + BIG_KT - 1) / BIG_KT;
+  const int nk = (K + KT - 1) / KT;
 #pragma unroll
-  for (int st = 0; st < BIG_STAGES - 1; ++st) {
+  for (int st = 0; st < ST - 1; ++st) {
     if (st < nk) issue(st);
     cp_async_commit();
   }
   for (int kt = 0; kt < nk; ++kt) {
-    cp_async_wait<BIG_STAGES - 2>();
+    cp_async_wait<ST - 2>();
     __syncthreads();
-    if (kt + BIG_STAGES - 1 < nk) issue(kt + BIG_STAGES - 1);
+    if (kt + ST - 1 < nk) issue(kt + ST - 1);
     cp_async_commit();
-    const int slot = kt % BIG_STAGES;
+    const int slot = kt % ST;
     const float *xs = Xs + slot * XF + ty * RW;
-    const uint16_t *ws = Ws + slot * WH + tx * CW;
+    const float *ws = Ws + slot * WF + tx * CW;
     // The operands of the next PF k-steps are loaded into registers ahead of
     // the products that use them: with few warps per scheduler (the decode
     // steps) nothing else hides the shared-memory latency.
-    float xb[PF][TMR];
-    uint32_t wb[PF][TNC / 2];
+    float xb[PF][TMR], wb[PF][TNC];
     auto ld = [&](int b, int k) {
 #pragma unroll
       for (int g = 0; g < RB; ++g) {
@@ -678,27 +684,25 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
 #pragma unroll
       for (int h = 0; h < CB; ++h) {
         if (CW == 4) {
-          const uint2 wv = *reinterpret_cast<const uint2 *>(ws + k * BN + CW * TX * h);
-          wb[b][2 * h] = wv.x; wb[b][2 * h + 1] = wv.y;
+          const float4 wv = *reinterpret_cast<const float4 *>(ws + k * BN + CW * TX * h);
+          wb[b][4 * h] = wv.x; wb[b][4 * h + 1] = wv.y; wb[b][4 * h + 2] = wv.z; wb[b][4 * h + 3] = wv.w;
         } else {
-          wb[b][h] = *reinterpret_cast<const uint32_t *>(ws + k * BN + CW * TX * h);
+          const float2 wv = *reinterpret_cast<const float2 *>(ws + k * BN + CW * TX * h);
+          wb[b][2 * h] = wv.x; wb[b][2 * h + 1] = wv.y;
         }
       }
     };
 #pragma unroll
     for (int q = 0; q < PF; ++q) ld(q, q);
 #pragma unroll
-    for (int k = 0; k < BIG_KT; ++k) {
+    for (int k = 0; k < KT; ++k) {
       const int b = k % PF;
       float x[TMR], w[TNC];
 #pragma unroll
       for (int i = 0; i < TMR; ++i) x[i] = xb[b][i];
 #pragma unroll
-      for (int j = 0; j < TNC / 2; ++j) {  // bf16 pair -> two fp32 (exact widen)
-        w[2 * j] = __uint_as_float(wb[b][j] << 16);
-        w[2 * j + 1] = __uint_as_float(wb[b][j] & 0xffff0000u);
-      }
-      if (k + PF < BIG_KT) ld(b, k + PF);
+      for (int j = 0; j < TNC; ++j) w[j] = wb[b][j];
+      if (k + PF < KT) ld(b, k + PF);
 #pragma unroll
       for (int i = 0; i < TMR; ++i)
 #pragma unroll
@@ -730,17 +734,17 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const uint16_t *__restrict__ W
   }
 }
 
-template <int TY, int TX, int TMR, int TNC>
-static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ysm, int ysn,
+template <int TY, int TX, int TMR, int TNC, int ST, int KT>
+static void run_gemm_big(const float *XT, int ldm, const float *Wpf, int K, int N, int M, float *Y, int ysm, int ysn,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
                          cudaStream_t s) {
   constexpr int BM = TMR * TY, BN = TNC * TX;
-  const size_t smem = (size_t)BIG_STAGES * (BIG_KT * BM * 4 + BIG_KT * BN * 2);
+  const size_t smem = (size_t)ST * KT * (BM + BN) * 4;
   static SmemLimit lim;
-  lim.ensure(k_gemm_big<TY, TX, TMR, TNC>, smem);
+  lim.ensure(k_gemm_big<TY, TX, TMR, TNC, ST, KT>, smem);
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  k_gemm_big<TY, TX, TMR, TNC><<<grid, TY * TX, smem, s>>>(XT, ldm, Wp, K, N, M, Y, ysm, ysn, R, ldr, y_slot,
-                                                           y_slot_stride, glu);
+  k_gemm_big<TY, TX, TMR, TNC, ST, KT><<<grid, TY * TX, smem, s>>>(XT, ldm, Wpf, K, N, M, Y, ysm, ysn, R, ldr,
+                                                                    y_slot, y_slot_stride, glu);
 }
 
 // Block tile choice for the sequential product from 64 rows on (the prompt
@@ -751,13 +755,13 @@ static void run_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, in
 // per-SM share of the outputs over the fraction of its FP32 pipe the SM's
 // warps can keep busy: one warp per scheduler suffices from 8 chains per
 // thread on, two from 4, and issue efficiency falls a little with the
-// chains per thread.  Measured on B200 (128 x 64 and 64 x 64 tiles, 32 and
-// 16 chains): 0.71-0.81 of the FP32 pipe on the 576- to 6,144-wide
-// projections of 4,096 rows, 0.63-0.71 on lm_head over 64-300 rows.
+// chains per thread.  Measured on B200 with the tiles below: 0.73-0.80 of
+// the FP32 pipe on lm_head (256-300 rows) and the prompt-pass projections
+// (4,096 rows); 0.37-0.64 on the decode-step projections of 256-300 rows,
+// where 300 x 768 outputs are under one warp per scheduler.
 struct BigCfg { int ty, tx, tmr, tnc; };
-static const BigCfg kBigTiles[] = {{16, 16, 8, 4}, {16, 16, 4, 4}, {16, 8, 4, 4}, {8, 16, 4, 4},
-                                   {8, 8, 4, 4},   {16, 8, 4, 2},  {8, 16, 2, 2}};
-constexpr int kNumBigTiles = 7;
+static const BigCfg kBigTiles[] = {{16, 16, 8, 4}, {16, 16, 4, 4}, {16, 8, 4, 4}, {16, 8, 4, 2}, {8, 16, 2, 2}};
+constexpr int kNumBigTiles = 5;
 
 int gemm_big_choice(int M, int N) {
   int best = 0;
@@ -778,30 +782,30 @@ int gemm_big_choice(int M, int N) {
   return best;
 }
 
-void launch_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ysm, int ysn,
+void launch_gemm_big(const float *XT, int ldm, const float *Wpf, int K, int N, int M, float *Y, int ysm, int ysn,
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
                      cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
-#define CIS2B_BIG(TY_, TX_, TMR_, TNC_) \
-  run_gemm_big<TY_, TX_, TMR_, TNC_>(XT, ldm, Wp, K, N, M, Y, ysm, ysn, resid, ldr, y_slot, y_slot_stride, glu, s)
+#define CIS2B_BIG(TY_, TX_, TMR_, TNC_, ST_, KT_)                                                                  \
+  run_gemm_big<TY_, TX_, TMR_, TNC_, ST_, KT_>(XT, ldm, Wpf, K, N, M, Y, ysm, ysn, resid, ldr, y_slot, y_slot_stride, \
+                                               glu, s)
+  // Stage depth and k per stage per tile, measured on B200 (fp32 panels).
   switch (gemm_big_choice(M, N)) {
-    case 0: CIS2B_BIG(16, 16, 8, 4); break;
-    case 1: CIS2B_BIG(16, 16, 4, 4); break;
-    case 2: CIS2B_BIG(16, 8, 4, 4); break;
-    case 3: CIS2B_BIG(8, 16, 4, 4); break;
-    case 4: CIS2B_BIG(8, 8, 4, 4); break;
-    case 5: CIS2B_BIG(16, 8, 4, 2); break;
-    default: CIS2B_BIG(8, 16, 2, 2); break;
+    case 0: CIS2B_BIG(16, 16, 8, 4, 3, 32); break;
+    case 1: CIS2B_BIG(16, 16, 4, 4, 4, 32); break;
+    case 2: CIS2B_BIG(16, 8, 4, 4, 6, 32); break;
+    case 3: CIS2B_BIG(16, 8, 4, 2, 4, 32); break;
+    default: CIS2B_BIG(8, 16, 2, 2, 4, 32); break;
   }
 #undef CIS2B_BIG
 }
 
-void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
-                 const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
+void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, const float *Wpf, int K, int N, int M, float *Y,
+                 int ldy, const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
   if (!tree && M >= 64) {
-    launch_gemm_big(XT, ldm, Wp, K, N, M, Y, ldy, 1, resid, ldr, y_slot, y_slot_stride, 0, s);
+    launch_gemm_big(XT, ldm, Wpf, K, N, M, Y, ldy, 1, resid, ldr, y_slot, y_slot_stride, 0, s);
     return;
   }
   // Fewer rows, or tree mode: SIMT register tiles (tree mode with the
@@ -832,7 +836,11 @@ void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int
 // Wp[n8][k][j] = W[src(8*n8 + j)][k] (zero rows past N): the panel layout
 // above, src(n) = n, or for a gate/up pair (il_half = I, N = 2I) the rows
 // interleaved, src(2i) = i (gate), src(2i + 1) = I + i (up).
-__global__ void k_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, int il_half) {
+// T = float: the same panels widened to fp32 (exact: bits << 16).
+__device__ __forceinline__ void panel_put(uint16_t *d, uint16_t v) { *d = v; }
+__device__ __forceinline__ void panel_put(float *d, uint16_t v) { *d = widen_bf16(v); }
+template <class T>
+__global__ void k_panelize(const uint16_t *W, int N, int K, T *Wp, int il_half) {
   const size_t N8 = (size_t)(N + 7) / 8;
   const size_t total = N8 * (size_t)K * 8;
   for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -840,11 +848,14 @@ __global__ void k_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, int il
     const size_t j = idx % 8, k = (idx / 8) % K, n8 = idx / (8 * (size_t)K);
     const size_t n = n8 * 8 + j;
     const size_t src = il_half ? ((n & 1) ? (size_t)il_half + n / 2 : n / 2) : n;
-    Wp[idx] = n < (size_t)N ? W[src * K + k] : (uint16_t)0;
+    panel_put(Wp + idx, n < (size_t)N ? W[src * K + k] : (uint16_t)0);
   }
 }
 void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s, int il_half) {
-  k_panelize<<<1184, 256, 0, s>>>(W, N, K, Wp, il_half);
+  k_panelize<uint16_t><<<1184, 256, 0, s>>>(W, N, K, Wp, il_half);
+}
+void launch_panelize(const uint16_t *W, int N, int K, float *Wp, cudaStream_t s, int il_half) {
+  k_panelize<float><<<1184, 256, 0, s>>>(W, N, K, Wp, il_half);
 }
 size_t panel_elems(int N, int K) { return (size_t)((N + 7) / 8) * 8 * (size_t)K; }
 

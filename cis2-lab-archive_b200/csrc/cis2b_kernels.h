@@ -29,23 +29,27 @@ void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n
 
 // Y[m][n] (+)= sum_k W[n][k] X[m][k] in the pinned order.  XT is X k-major
 // [K][ldm] (ldm % 4 == 0, ldm >= M); Wp holds W bf16 in 8-row k-major
-// panels (launch_panelize).  If resid != nullptr, Y = resid + dot.  If
-// y_slot != nullptr, Y is offset by (*y_slot) * y_slot_stride floats.
-void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ldy,
-                 const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
+// panels and Wpf the same panels widened to fp32 (launch_panelize): the
+// many-row form (sequential order, M >= 64) reads Wpf, the others Wp.  If
+// resid != nullptr, Y = resid + dot.  If y_slot != nullptr, Y is offset by
+// (*y_slot) * y_slot_stride floats.
+void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, const float *Wpf, int K, int N, int M, float *Y,
+                 int ldy, const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s);
 // The many-row form behind launch_gemm (sequential order, M >= 64): Y[m * ysm
 // + n * ysn], so the output may be written k-major for the next product.
-// glu: Wp is a gate/up pair panelised with il_half = I (N = 2I); the output
+// glu: Wpf is a gate/up pair panelised with il_half = I (N = 2I); the output
 // is silu(gate) * up, I columns.
-void launch_gemm_big(const float *XT, int ldm, const uint16_t *Wp, int K, int N, int M, float *Y, int ysm, int ysn,
+void launch_gemm_big(const float *XT, int ldm, const float *Wpf, int K, int N, int M, float *Y, int ysm, int ysn,
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
                      cudaStream_t s);
 int gemm_big_choice(int M, int N);
-// Wp[n8][k][j] = W[8*n8 + j][k], zero rows past N; Wp holds panel_elems(N, K) bf16.
+// Wp[n8][k][j] = W[8*n8 + j][k], zero rows past N; Wp holds panel_elems(N, K)
+// elements, bf16 bits or (float overload) those widened to fp32.
 // il_half = I > 0 (N = 2I): rows interleaved, panel row 2i = W row i (gate),
 // 2i + 1 = W row I + i (up).
 void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t s, int il_half = 0);
+void launch_panelize(const uint16_t *W, int N, int K, float *Wp, cudaStream_t s, int il_half = 0);
 size_t panel_elems(int N, int K);
 
 // Decode form of the same product for few rows (sequential order only).  X is

@@ -82,6 +82,7 @@ struct LayerW {
   const uint16_t *in_norm, *post_norm, *wqkv, *wo, *wgu, *wdown;  // row-major [N][K] as on disk
   const uint16_t *q_norm, *k_norm, *q_bias, *k_bias, *v_bias;
   const uint16_t *pqkv, *po, *pgu, *pdown;  // the same weights in GEMM panel layout
+  const float *fqkv = nullptr, *fo = nullptr, *fgu = nullptr, *fdown = nullptr;  // ... widened to fp32
   const uint16_t *tqkv, *to, *tgu, *tdown;  // and in 32-column decode tiles (sequential mode)
 };
 
@@ -111,6 +112,10 @@ struct cis2b_model {
   DevBuf arena;   // all weights as on disk (embedding rows, norms, biases are read from here)
   DevBuf panels;  // GEMM weights re-laid in 8-row k-major panels
   const uint16_t *lm_head_p = nullptr;
+  // The same panels widened to fp32 for the many-row product (sequential
+  // mode only): it then spends no issue slots on widening, and HBM has room.
+  DevBuf panels_f;
+  const float *lm_head_f = nullptr;
   DevBuf tiles;   // the same weights in 32-column tiles for the decode GEMM
   const uint16_t *lm_head_t = nullptr;
   bool dec_tiles = false;  // decode steps use launch_gemm_dec (sequential mode, K % 4 == 0)
@@ -505,6 +510,25 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
     }
     m->lm_head_p = pat(off_lmp);
     launch_panelize(m->lm_head, m->V, m->H, const_cast<uint16_t *>(m->lm_head_p), m->s_main);
+    if (!m->tree) {  // fp32 panels at twice the offsets (4 bytes per element instead of 2)
+      if (m->panels_f.ensure(2 * total) != cudaSuccess)
+        return fail(CIS2B_ERR_NOMEM, "device allocation of the fp32 weight panels failed");
+      uint8_t *fb = m->panels_f.as<uint8_t>();
+      auto fat = [&](size_t off) { return reinterpret_cast<float *>(fb + 2 * off); };
+      for (int l = 0; l < m->L; ++l) {
+        LayerW &w = m->layers[(size_t)l];
+        w.fqkv = fat(offs[4 * l]);
+        w.fo = fat(offs[4 * l + 1]);
+        w.fgu = fat(offs[4 * l + 2]);
+        w.fdown = fat(offs[4 * l + 3]);
+        launch_panelize(w.wqkv, NQKV, m->H, const_cast<float *>(w.fqkv), m->s_main);
+        launch_panelize(w.wo, m->H, m->QD, const_cast<float *>(w.fo), m->s_main);
+        launch_panelize(w.wgu, 2 * m->I, m->H, const_cast<float *>(w.fgu), m->s_main, m->I);
+        launch_panelize(w.wdown, m->H, m->I, const_cast<float *>(w.fdown), m->s_main);
+      }
+      m->lm_head_f = fat(off_lmp);
+      launch_panelize(m->lm_head, m->V, m->H, const_cast<float *>(m->lm_head_f), m->s_main);
+    }
     CU_LAUNCHED();
     CU(cudaStreamSynchronize(m->s_main));
   }
@@ -623,18 +647,18 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
   const bool dec = decode && m->dec_tiles && rows < m->dec_big_rows;
   const int lnr = dec ? H : 1, lnc = dec ? 1 : ldm;      // ln / att / hid (row, column) strides
   const int atr = dec ? QD : 1, hir = dec ? I : 1;
-  auto gemm = [&](const float *X, const uint16_t *Wp, const uint16_t *Wt, int K, int N, float *Y, int ldy,
-                  const float *R, int ldr) {
+  auto gemm = [&](const float *X, const uint16_t *Wp, const float *Wpf, const uint16_t *Wt, int K, int N, float *Y,
+                  int ldy, const float *R, int ldr) {
     ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
     if (dec) launch_gemm_dec(X, K, Wt, K, N, rows, Y, ldy, R, ldr, nullptr, 0, s);
-    else launch_gemm(X, ldm, Wp, K, N, rows, Y, ldy, R, ldr, m->tree, nullptr, 0, s);
+    else launch_gemm(X, ldm, Wp, Wpf, K, N, rows, Y, ldy, R, ldr, m->tree, nullptr, 0, s);
   };
   for (int l = 0; l < m->L; ++l) {
     const LayerW &w = m->layers[(size_t)l];
     float *kc = m->kc.as<float>() + (size_t)l * layer_kv;
     float *vc = m->vc.as<float>() + (size_t)l * layer_kv;
     launch_rmsnorm(h, H, w.in_norm, m->eps, H, rows, m->tree, ln, lnr, lnc, s);
-    gemm(ln, w.pqkv, w.tqkv, H, NQKV, qkv, NQKV, nullptr, 0);
+    gemm(ln, w.pqkv, w.fqkv, w.tqkv, H, NQKV, qkv, NQKV, nullptr, 0);
     m->launches += 2;
     if (w.q_bias) { launch_add_bias(qkv, NQKV, rows, w.q_bias, QD, s); m->launches++; }
     if (w.k_bias) { launch_add_bias(qkv + QD, NQKV, rows, w.k_bias, KVD, s); m->launches++; }
@@ -652,20 +676,20 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
         launch_attention(qkv, NQKV, rows, rm, m->NH, m->NKV, m->HD, kc, vc, maxP, m->tree, att, atr,
                          dec ? 1 : ldm, maxP, decode, w.q_norm, w.k_norm, m->eps, m->cos_t.as<float>(),
                          m->sin_t.as<float>(), s); }
-    gemm(att, w.po, w.to, QD, H, h, H, h, H);
+    gemm(att, w.po, w.fo, w.to, QD, H, h, H, h, H);
     launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, lnr, lnc, s);
     if (dec) {  // SwiGLU in the gate/up GEMM's epilogue
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
       launch_gemm_dec(ln, H, w.tgu, H, 2 * I, rows, hid, I, nullptr, 0, nullptr, 0, s, I);
     } else if (!m->tree && rows >= 64) {  // SwiGLU in the epilogue, hid written k-major
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm_big(ln, ldm, w.pgu, H, 2 * I, rows, hid, 1, ldm, nullptr, 0, nullptr, 0, 1, s);
+      launch_gemm_big(ln, ldm, w.fgu, H, 2 * I, rows, hid, 1, ldm, nullptr, 0, nullptr, 0, 1, s);
     } else {
-      gemm(ln, w.pgu, w.tgu, H, 2 * I, gu, 2 * I, nullptr, 0);
+      gemm(ln, w.pgu, w.fgu, w.tgu, H, 2 * I, gu, 2 * I, nullptr, 0);
       launch_silu_mul(gu, I, rows, hid, hir, ldm, s);
       m->launches++;
     }
-    gemm(hid, w.pdown, w.tdown, I, H, h, H, h, H);
+    gemm(hid, w.pdown, w.fdown, w.tdown, I, H, h, H, h, H);
     m->launches += 5;
   }
   CU_LAUNCHED();
@@ -686,8 +710,8 @@ int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_
       launch_gemm_dec(m->lnlast.as<float>(), m->H, m->lm_head_t, m->H, m->V, rows, Y, m->V, nullptr, 0, y_slot,
                       slot_stride, s);
     else
-      launch_gemm(m->lnlast.as<float>(), ldb, m->lm_head_p, m->H, m->V, rows, Y, m->V, nullptr, 0, m->tree,
-                  y_slot, slot_stride, s);
+      launch_gemm(m->lnlast.as<float>(), ldb, m->lm_head_p, m->lm_head_f, m->H, m->V, rows, Y, m->V, nullptr, 0,
+                  m->tree, y_slot, slot_stride, s);
   }
   m->launches += 2;
   CU_LAUNCHED();
@@ -1227,7 +1251,7 @@ int trace_impl(cis2b_model *m, const uint32_t *ids, uint32_t n_ids, const char *
       float *kc = m->kc.as<float>() + (size_t)l * layer_kv, *vc = m->vc.as<float>() + (size_t)l * layer_kv;
       launch_rmsnorm(h, H, w.in_norm, m->eps, H, 1, m->tree, ln, 1, ldm, s);
       EMIT(pos, l, "norm1", ln, (size_t)H, (size_t)ldm);
-      launch_gemm(ln, ldm, w.pqkv, H, NQKV, 1, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s);
+      launch_gemm(ln, ldm, w.pqkv, w.fqkv, H, NQKV, 1, qkv, NQKV, nullptr, 0, m->tree, nullptr, 0, s);
       if (w.q_bias) launch_add_bias(qkv, NQKV, 1, w.q_bias, QD, s);
       if (w.k_bias) launch_add_bias(qkv + QD, NQKV, 1, w.k_bias, KVD, s);
       if (w.v_bias) launch_add_bias(qkv + QD + KVD, NQKV, 1, w.v_bias, KVD, s);
@@ -1248,26 +1272,26 @@ int trace_impl(cis2b_model *m, const uint32_t *ids, uint32_t n_ids, const char *
       EMIT(pos, l, "scores", dbg, (size_t)m->NH * (pos + 1), 1);
       EMIT(pos, l, "softmax", dbg + (size_t)m->NH * (pos + 1), (size_t)m->NH * (pos + 1), 1);
       EMIT(pos, l, "attn_out", att, (size_t)QD, (size_t)ldm);
-      launch_gemm(att, ldm, w.po, QD, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
+      launch_gemm(att, ldm, w.po, w.fo, QD, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
       EMIT(pos, l, "o_proj", o, (size_t)H, 1);
-      launch_gemm(att, ldm, w.po, QD, H, 1, h, H, h, H, m->tree, nullptr, 0, s);
+      launch_gemm(att, ldm, w.po, w.fo, QD, H, 1, h, H, h, H, m->tree, nullptr, 0, s);
       EMIT(pos, l, "resid1", h, (size_t)H, 1);
       launch_rmsnorm(h, H, w.post_norm, m->eps, H, 1, m->tree, ln, 1, ldm, s);
       EMIT(pos, l, "norm2", ln, (size_t)H, (size_t)ldm);
-      launch_gemm(ln, ldm, w.pgu, H, 2 * I, 1, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s);
+      launch_gemm(ln, ldm, w.pgu, w.fgu, H, 2 * I, 1, gu, 2 * I, nullptr, 0, m->tree, nullptr, 0, s);
       EMIT(pos, l, "gate", gu, (size_t)I, 2);  // gate and up interleaved (launch_panelize)
       EMIT(pos, l, "up", gu + 1, (size_t)I, 2);
       launch_silu_mul(gu, I, 1, hid, 1, ldm, s);
       EMIT(pos, l, "silu_mul", hid, (size_t)I, (size_t)ldm);
-      launch_gemm(hid, ldm, w.pdown, I, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
+      launch_gemm(hid, ldm, w.pdown, w.fdown, I, H, 1, o, H, nullptr, 0, m->tree, nullptr, 0, s);
       EMIT(pos, l, "down", o, (size_t)H, 1);
-      launch_gemm(hid, ldm, w.pdown, I, H, 1, h, H, h, H, m->tree, nullptr, 0, s);
+      launch_gemm(hid, ldm, w.pdown, w.fdown, I, H, 1, h, H, h, H, m->tree, nullptr, 0, s);
       EMIT(pos, l, "resid2", h, (size_t)H, 1);
     }
     launch_rmsnorm(h, H, m->final_norm, m->eps, H, 1, m->tree, m->lnlast.as<float>(), 1, 64, s);
     EMIT(pos, -1, "final_norm", m->lnlast.as<float>(), (size_t)H, 64);
-    launch_gemm(m->lnlast.as<float>(), 64, m->lm_head_p, H, m->V, 1, d_logits.as<float>(), m->V, nullptr, 0, m->tree,
-                nullptr, 0, s);
+    launch_gemm(m->lnlast.as<float>(), 64, m->lm_head_p, m->lm_head_f, H, m->V, 1, d_logits.as<float>(), m->V,
+                nullptr, 0, m->tree, nullptr, 0, s);
     EMIT(pos, -1, "logits", d_logits.as<float>(), (size_t)m->V, 1);
     CU_LAUNCHED();
   }
@@ -1432,15 +1456,17 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
   for (int r = 0; r < rows; ++r)
     for (int i = 0; i < k; ++i) xt[(size_t)i * ldm + r] = X[(size_t)r * k + i];
   Scoped<uint16_t> dw, dp;
-  Scoped<float> dx, dy;
+  Scoped<float> dx, dy, dpf;
   CU(cudaMalloc(&dw.p, 2 * (size_t)n_out * k));
   CU(cudaMalloc(&dp.p, 2 * panel_elems(n_out, k)));
+  CU(cudaMalloc(&dpf.p, 4 * panel_elems(n_out, k)));
   CU(cudaMalloc(&dx.p, 4 * xt.size()));
   CU(cudaMalloc(&dy.p, 4 * (size_t)rows * n_out));
   CU(cudaMemcpy(dw.p, W, 2 * (size_t)n_out * k, cudaMemcpyHostToDevice));
   CU(cudaMemcpy(dx.p, xt.data(), 4 * xt.size(), cudaMemcpyHostToDevice));
   launch_panelize(dw.p, n_out, k, dp.p, 0);
-  launch_gemm(dx.p, ldm, dp.p, k, n_out, rows, dy.p, n_out, nullptr, 0, reduction == CIS2B_REDUCTION_TREE,
+  launch_panelize(dw.p, n_out, k, dpf.p, 0);
+  launch_gemm(dx.p, ldm, dp.p, dpf.p, k, n_out, rows, dy.p, n_out, nullptr, 0, reduction == CIS2B_REDUCTION_TREE,
               nullptr, 0, 0);
   CU_LAUNCHED();
   CU(cudaMemcpy(Y, dy.p, 4 * (size_t)rows * n_out, cudaMemcpyDeviceToHost));

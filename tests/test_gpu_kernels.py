@@ -86,16 +86,16 @@ SHAPES = [(1, 576, 576), (3, 192, 576), (4, 100, 96), (7, 1536, 576), (16, 64, 1
           (64, 576, 1536), (64, 960, 576), (5, 4099, 64), (128, 1024, 3072), (65, 300, 8), (2, 49152, 576),
           (2048, 2560, 96), (1970, 2500, 40), (300, 20000, 32),   # the 64 x 64 prompt-pass tile
           (4096, 576, 96), (700, 9000, 16),                       # the 128 x 64 tile
-          # the narrower register tiles the many-row decode steps pick (each
-          # shape's choice is checked below): 64 x 32, 32 x 32, 64 x 16,
-          # 32 x 64 and 32 x 16 thread-block tiles, ragged edges included
+          # the narrower register tiles the many-row decode steps pick (every
+          # tile is some shape's choice, checked in test_abi): 64 x 32, 64 x 16
+          # and 16 x 32 thread-block tiles, ragged edges and K not a multiple
+          # of the 32-deep k stage included
           (300, 768, 768), (300, 2304, 96), (121, 960, 64), (256, 576, 40), (70, 40, 32),
           (300, 32000, 16), (96, 100, 24), (129, 72, 16), (96, 8192, 24), (65, 2048, 40)]
 
 # Tile (threads along m, threads along n, rows per thread, columns per
 # thread) of the register-tiled kernel, in the order the library numbers them.
-BIG_TILES = [(16, 16, 8, 4), (16, 16, 4, 4), (16, 8, 4, 4), (8, 16, 4, 4), (8, 8, 4, 4),
-             (16, 8, 4, 2), (8, 16, 2, 2)]
+BIG_TILES = [(16, 16, 8, 4), (16, 16, 4, 4), (16, 8, 4, 4), (16, 8, 4, 2), (8, 16, 2, 2)]
 
 
 @pytest.mark.parametrize("form", ["sequential", "tree", "decode"])
