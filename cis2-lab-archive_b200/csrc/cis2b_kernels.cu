@@ -1427,6 +1427,13 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
 // flight while one is consumed).  Measured on B200, the generic kernel's
 // integer index arithmetic (divisions by the head size and chunk length per
 // copy and per dot) made the integer pipe its busiest unit, ahead of memory.
+// Beyond that: each thread keeps a running max of the scores it writes
+// (combined per head afterwards, the same NaN-aware combine), the
+// denominators run in one warp, each thread stages fixed rows of every
+// chunk, and a V-mix thread owns two adjacent d (two independent chains, one
+// packed add per position).  Measured at the C5 shape (256 rows, position
+// ~1,535): 78 M to 62 M instructions, 157 to 149 us; the rest is the wait
+// on each chunk and the per-chunk barrier.
 template <int HD, int G>
 struct AttDec {
   static constexpr int NT = G * HD < 128 ? 128 : G * HD;  // threads: one V-mix chain per (g, d)
@@ -1437,9 +1444,11 @@ struct AttDec {
 
 };
 
+// Score row pitch: max_len rounded to 4, plus 4 so that the G rows start on
+// different banks (the denominator lanes read them side by side).
+__host__ __device__ inline int att_dec_scs(int max_len) { return ((max_len + 3) & ~3) + 4; }
 size_t attention_dec_smem_floats(int G, int hd, int max_len, int stages) {
-  const size_t scs = ((size_t)max_len + 3) & ~(size_t)3;
-  return (size_t)G * hd + (size_t)G * scs + 64 + (size_t)stages * 64 * (hd + 4);
+  return (size_t)G * hd + (size_t)G * att_dec_scs(max_len) + 64 + (size_t)stages * 64 * (hd + 4);
 }
 
 template <int HD, int G, int ST>
@@ -1449,15 +1458,17 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
                 float eps, const float *cos_t, const float *sin_t) {
   using C = AttDec<HD, G>;
   constexpr int NT = C::NT, JC = C::JC, TS = C::TS, NQ = C::NQ, NW = NT / 32;
+  static_assert(C::DPT == 1 && JC % 32 == 0 && NT % NQ == 0 && G * JC <= NT, "one dot per thread per chunk");
+  static_assert(NW <= 32 && G <= 16 && HD % 2 == 0, "red[] layout");
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int KV = nkv * HD;
   const int seq = rseq[r], pos = rpos[r], len = pos + 1;
-  const int scs = (max_len + 3) & ~3;
+  const int scs = att_dec_scs(max_len);
   float *q = sm;                       // [G][HD]
   float *sc = q + G * HD;              // [G][scs]
-  float *red = sc + (size_t)G * scs;   // [64]
+  float *red = sc + (size_t)G * scs;   // [64]: per-warp maxima, denominators at 32, maxima at 48
   float *tiles = red + 64;             // [ST][JC][TS]; offset is a multiple of 4 floats
   {
     // The row's q/k norm, RoPE and cache append for this KV head (the work
@@ -1494,12 +1505,18 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
   const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * HD;
   const int nch = (len + JC - 1) / JC;
   const uint32_t tbase = (uint32_t)__cvta_generic_to_shared(tiles);
+  // Staging: thread t copies 16-byte piece t % NQ of rows t / NQ, + RP, ...
+  constexpr int RP = NT / NQ;
+  const int sq = tid % NQ, sr = tid / NQ;
   auto stage = [&](const float *base, int c) {  // rows [c*JC, c*JC + JC) -> ring slot c % ST
     if (c < nch) {
       const int j0 = c * JC, jc = min(JC, len - j0), buf = c % ST;
-      for (int i = tid; i < jc * NQ; i += NT) {
-        const int jj = i / NQ, q4 = i % NQ;
-        cp_async16(tbase + (uint32_t)(((buf * JC + jj) * TS + 4 * q4) * 4), base + (size_t)(j0 + jj) * KV + 4 * q4);
+      const float *src = base + (size_t)(j0 + sr) * KV + 4 * sq;
+      uint32_t dst = tbase + (uint32_t)(((buf * JC + sr) * TS + 4 * sq) * 4);
+      for (int jj = sr; jj < jc; jj += RP) {
+        cp_async16(dst, src);
+        src += (size_t)RP * KV;
+        dst += (uint32_t)(RP * TS * 4);
       }
     }
     cp_async_commit();  // empty groups keep the count uniform
@@ -1513,66 +1530,73 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
   for (int c = 0; c < ST - 1; ++c) stage(kbase, c);
   __syncthreads();  // q visible
 
-  // ---- scores: thread (g, jj) = (pr / JC, pr % JC) of each chunk; q from
-  // shared memory (a broadcast load: all lanes of a warp share g)
+  // ---- scores: thread (g, jj) = (tid / JC, tid % JC) of each chunk; q from
+  // shared memory (a broadcast load: all lanes of a warp share g).  The
+  // thread's running max uses the combine of the serial-scan max.
+  const int sg = tid / JC, sj = tid % JC;
+  float mloc = bitsf(0x7fc00000u);
   for (int c = 0; c < nch; ++c) {
     land(c);
     stage(kbase, c + ST - 1);  // its slot was last read in chunk c - 1
     const int j0 = c * JC, jc = min(JC, len - j0);
     const float *tile = tiles + (size_t)(c % ST) * JC * TS;
+    if (sg < G && sj < jc) {
+      const float4 *k4 = reinterpret_cast<const float4 *>(tile + sj * TS);
+      const float4 *q4 = reinterpret_cast<const float4 *>(q + sg * HD);
+      float d = 0.0f;
 #pragma unroll
-    for (int u = 0; u < C::DPT; ++u) {
-      const int pr = tid + u * NT, g = pr / JC, jj = pr % JC;
-      if (g < G && jj < jc) {
-        const float4 *k4 = reinterpret_cast<const float4 *>(tile + jj * TS);
-        float d = 0.0f;
-#pragma unroll
-        for (int i = 0; i < NQ; ++i) {
-          const float4 b = k4[i];
-          const float4 a = reinterpret_cast<const float4 *>(q + g * HD)[i];
-          d = fadd(d, fmul(a.x, b.x));
-          d = fadd(d, fmul(a.y, b.y));
-          d = fadd(d, fmul(a.z, b.z));
-          d = fadd(d, fmul(a.w, b.w));
-        }
-        sc[(size_t)g * scs + j0 + jj] = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
+      for (int i = 0; i < NQ; ++i) {
+        const float4 b = k4[i];
+        const float4 a = q4[i];
+        d = fadd(d, fmul(a.x, b.x));
+        d = fadd(d, fmul(a.y, b.y));
+        d = fadd(d, fmul(a.z, b.z));
+        d = fadd(d, fmul(a.w, b.w));
       }
+      const float sv = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
+      sc[(size_t)sg * scs + j0 + sj] = sv;
+      mloc = max_comb(mloc, sv);
     }
   }
-  __syncthreads();  // every ring slot is free again
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mloc = max_comb(mloc, __shfl_xor_sync(FULL, mloc, o));
+  if (lane == 0) red[warp] = mloc;  // warp w's scores all belong to head 32 w / JC
+  __syncthreads();  // every ring slot is free again; the warp maxima are visible
 #pragma unroll
   for (int c = 0; c < ST - 1; ++c) stage(vbase, c);  // V chunks load while the softmax runs
 
   // ---- softmax (serial-scan max, pinned exp, serial denominator, divide)
-  for (int g = warp; g < G; g += NW) {
-    const float *sg = sc + (size_t)g * scs;
-    float m = bitsf(0x7fc00000u);
-    for (int j = lane; j < len; j += 32) m = max_comb(m, sg[j]);
+  if (tid < G) {
+    constexpr int WPH = JC / 32;  // warps per head
+    const float *s0 = sc + (size_t)tid * scs;
+    float m = red[tid * WPH];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max_comb(m, __shfl_xor_sync(FULL, m, o));
-    if (lane == 0) red[g] = is_nan(sg[0]) ? sg[0] : m;
+    for (int w = 1; w < WPH; ++w) m = max_comb(m, red[tid * WPH + w]);
+    red[48 + tid] = is_nan(s0[0]) ? s0[0] : m;
   }
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float *sg = sc + (size_t)g * scs;
-    const float mg = red[g];
-    for (int j = tid; j < len; j += NT) sg[j] = exp_pinned(fsub(sg[j], mg));
+    float *srow = sc + (size_t)g * scs;
+    const float mg = red[48 + g];
+    for (int j = tid; j < len; j += NT) srow[j] = exp_pinned(fsub(srow[j], mg));
   }
   __syncthreads();
-  if (tid < G * 32 && lane == 0) red[32 + warp] = serial_sum4(sc + (size_t)warp * scs, len);
+  if (tid < G) red[32 + tid] = serial_sum4(sc + (size_t)tid * scs, len);
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float *sg = sc + (size_t)g * scs;
+    float *srow = sc + (size_t)g * scs;
     const float den = red[32 + g];
-    for (int j = tid; j < len; j += NT) sg[j] = fdiv(sg[j], den);
+    for (int j = tid; j < len; j += NT) srow[j] = fdiv(srow[j], den);
   }
 
-  // ---- V-mix: thread (g, d) = (tid / HD, tid % HD), j ascending
-  const int g = tid / HD, d = tid % HD;
-  const bool owns = tid < G * HD;
-  float acc = 0.0f;
+  // ---- V-mix: thread (g, d, d + 1) = (tid / (HD/2), 2 (tid % (HD/2))), two
+  // independent chains, j ascending, one packed add per position
+  constexpr int DPW = HD / 2;
+  const int g = tid / DPW, d = 2 * (tid % DPW);
+  const bool owns = tid < G * DPW;
+  float2 acc = make_float2(0.0f, 0.0f);
   for (int c = 0; c < nch; ++c) {
     land(c);
     stage(vbase, c + ST - 1);
@@ -1582,13 +1606,13 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
       const float *pg = sc + (size_t)g * scs + j0;  // j0 % 4 == 0: 16-byte aligned
       if (jc == JC) {
         // Full chunk: the weights and values of the next two groups of four
-        // positions are loaded while the chain consumes the current group.
+        // positions are loaded while the chains consume the current group.
         float4 pw[2];
-        float vv[2][4];
+        float2 vv[2][4];
         auto ld = [&](int b, int jj) {
           pw[b] = *reinterpret_cast<const float4 *>(pg + jj);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) vv[b][u] = tile[(jj + u) * TS];
+          for (int u = 0; u < 4; ++u) vv[b][u] = *reinterpret_cast<const float2 *>(tile + (jj + u) * TS);
         };
         ld(0, 0);
         ld(1, 4);
@@ -1596,29 +1620,28 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
         for (int qd = 0; qd < JC / 4; ++qd) {
           const int b = qd & 1;
           const float4 w = pw[b];
-          const float v0 = vv[b][0], v1 = vv[b][1], v2 = vv[b][2], v3 = vv[b][3];
+          const float2 v0 = vv[b][0], v1 = vv[b][1], v2 = vv[b][2], v3 = vv[b][3];
           if (qd + 2 < JC / 4) ld(b, 4 * (qd + 2));
-          acc = fadd(acc, fmul(w.x, v0));
-          acc = fadd(acc, fmul(w.y, v1));
-          acc = fadd(acc, fmul(w.z, v2));
-          acc = fadd(acc, fmul(w.w, v3));
+          acc = fadd_pair(acc, fmul(w.x, v0.x), fmul(w.x, v0.y));
+          acc = fadd_pair(acc, fmul(w.y, v1.x), fmul(w.y, v1.y));
+          acc = fadd_pair(acc, fmul(w.z, v2.x), fmul(w.z, v2.y));
+          acc = fadd_pair(acc, fmul(w.w, v3.x), fmul(w.w, v3.y));
         }
       } else {
-        int jj = 0;
-        for (; jj + 4 <= jc; jj += 4) {
-          const float4 w = *reinterpret_cast<const float4 *>(pg + jj);
-          const float v0 = tile[jj * TS], v1 = tile[(jj + 1) * TS], v2 = tile[(jj + 2) * TS], v3 = tile[(jj + 3) * TS];
-          acc = fadd(acc, fmul(w.x, v0));
-          acc = fadd(acc, fmul(w.y, v1));
-          acc = fadd(acc, fmul(w.z, v2));
-          acc = fadd(acc, fmul(w.w, v3));
+        for (int jj = 0; jj < jc; ++jj) {
+          const float p = pg[jj];
+          const float2 v = *reinterpret_cast<const float2 *>(tile + jj * TS);
+          acc = fadd_pair(acc, fmul(p, v.x), fmul(p, v.y));
         }
-        for (; jj < jc; ++jj) acc = fadd(acc, fmul(pg[jj], tile[jj * TS]));
       }
     }
   }
   cp_async_wait<0>();
-  if (owns) att[(size_t)r * ars + ((size_t)kvh * G + g) * HD * acs + (size_t)d * acs] = acc;
+  if (owns) {
+    float *o = att + (size_t)r * ars + ((size_t)kvh * G + g) * HD * acs + (size_t)d * acs;
+    o[0] = acc.x;
+    o[acs] = acc.y;
+  }
 }
 
 template <int HD, int G, int ST>
