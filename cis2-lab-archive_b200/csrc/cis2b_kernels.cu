@@ -1883,11 +1883,233 @@ k_attention_rows(const float *qkv, int ld, const int2 *tiles, const int32_t *rse
   }
 }
 
+// Sequential-mode prompt-pass attention specialised on the head size HD and
+// the group G (the same arithmetic as k_attention_rows, in the same order).
+// Per chunk of ATT_JC keys, thread t computes the dots of pair t / 16 with
+// keys t % 16 + 16 u, u = 0..3: q is read once for four independent chains
+// and the four key rows of a half-warp's lanes are consecutive (the TS
+// pitch keeps those loads conflict-free).  In the V-mix a thread owns two
+// adjacent d of up to PPT pairs: per key one 8-byte value load serves all
+// its pairs, the weights of four keys come in one 16-byte load per pair,
+// and each pair's two chains take one packed add per key.
+template <int HD, int G>
+__global__ void __launch_bounds__(ATTR_NT, 2)
+k_attention_rows_s(const float *qkv, int ld, const int2 *tiles, const int32_t *rseq, const int32_t *rpos, int nkv,
+                   const float *kc, const float *vc, int max_pos, float *att, int ars, int acs, int max_len) {
+  constexpr int NT = ATTR_NT, JC = ATT_JC, TS = HD + 4, NQ = HD / 4;
+  constexpr int S = NT / (HD / 2);           // V-mix pair slots
+  constexpr int PMAX = 48;                   // pairs per tile at most (attention_rows_rt)
+  constexpr int PPT = (PMAX + S - 1) / S;    // pairs per V-mix thread at most
+  static_assert(JC == 64 && NT % (HD / 2) == 0 && NT % NQ == 0, "tile shape");
+  extern __shared__ __align__(16) float sm[];
+  const int kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NW = NT / 32;
+  const int KV = nkv * HD;
+  const int2 tl = tiles[blockIdx.x];
+  const int r0 = tl.x, nr = tl.y, P = nr * G;
+  const int seq = rseq[r0], p0 = rpos[r0];
+  const int lenmax = p0 + nr;
+  const int scs = ((max_len + 3) & ~3) + 4;
+  float *q = sm;                                     // [pair][HD]
+  float *sc = q + (size_t)P * HD;                    // [pair][scs]
+  float *red = sc + (size_t)P * scs;                 // [2][pair]
+  size_t toff = (size_t)(red + 2 * P + 8 - sm);
+  toff = (toff + 3) & ~(size_t)3;
+  float *tiles_s = sm + toff;                        // [2][JC][TS]
+  for (int x = tid; x < P * HD; x += NT) {
+    const int pr = x / HD, d = x % HD, i = pr / G, g = pr % G;
+    q[x] = qkv[(size_t)(r0 + i) * ld + ((size_t)kvh * G + g) * HD + d];
+  }
+  const float scale = rsqrt_cr(__int2float_rn(HD));
+  const float *kbase = kc + (size_t)seq * max_pos * KV + (size_t)kvh * HD;
+  const float *vbase = vc + (size_t)seq * max_pos * KV + (size_t)kvh * HD;
+  const int nch = (lenmax + JC - 1) / JC;
+  const uint32_t tbase = (uint32_t)__cvta_generic_to_shared(tiles_s);
+  constexpr int RP = NT / NQ;
+  const int sq = tid % NQ, sr = tid / NQ;
+  auto stage = [&](const float *base, int c, int buf) {
+    const int j0 = c * JC, jc = min(JC, lenmax - j0);
+    const float *src = base + (size_t)(j0 + sr) * KV + 4 * sq;
+    uint32_t dst = tbase + (uint32_t)(((buf * JC + sr) * TS + 4 * sq) * 4);
+    for (int jj = sr; jj < jc; jj += RP) {
+      cp_async16(dst, src);
+      src += (size_t)RP * KV;
+      dst += (uint32_t)(RP * TS * 4);
+    }
+    cp_async_commit();
+  };
+
+  // ---- scores
+  stage(kbase, 0, 0);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) stage(kbase, c + 1, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int j0 = c * JC;
+    const float *tile = tiles_s + (size_t)(c & 1) * JC * TS;
+    for (int u0 = tid; u0 < P * 16; u0 += NT) {
+      const int pr = u0 >> 4, jq = u0 & 15;
+      const int lim = p0 + pr / G;             // last key this row reads
+      if (j0 + jq > lim) continue;             // no key of this unit is read
+      const float4 *q4 = reinterpret_cast<const float4 *>(q + (size_t)pr * HD);
+      const float4 *k0 = reinterpret_cast<const float4 *>(tile + (jq) * TS);
+      const float4 *k1 = reinterpret_cast<const float4 *>(tile + (jq + 16) * TS);
+      const float4 *k2 = reinterpret_cast<const float4 *>(tile + (jq + 32) * TS);
+      const float4 *k3 = reinterpret_cast<const float4 *>(tile + (jq + 48) * TS);
+      float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NQ; ++i) {
+        const float4 a = q4[i];
+        const float4 b0 = k0[i], b1 = k1[i], b2 = k2[i], b3 = k3[i];
+        d0 = fadd(d0, fmul(a.x, b0.x)); d1 = fadd(d1, fmul(a.x, b1.x));
+        d2 = fadd(d2, fmul(a.x, b2.x)); d3 = fadd(d3, fmul(a.x, b3.x));
+        d0 = fadd(d0, fmul(a.y, b0.y)); d1 = fadd(d1, fmul(a.y, b1.y));
+        d2 = fadd(d2, fmul(a.y, b2.y)); d3 = fadd(d3, fmul(a.y, b3.y));
+        d0 = fadd(d0, fmul(a.z, b0.z)); d1 = fadd(d1, fmul(a.z, b1.z));
+        d2 = fadd(d2, fmul(a.z, b2.z)); d3 = fadd(d3, fmul(a.z, b3.z));
+        d0 = fadd(d0, fmul(a.w, b0.w)); d1 = fadd(d1, fmul(a.w, b1.w));
+        d2 = fadd(d2, fmul(a.w, b2.w)); d3 = fadd(d3, fmul(a.w, b3.w));
+      }
+      float *srow = sc + (size_t)pr * scs + j0 + jq;
+      srow[0] = fmul(d0, scale);               // j0 + jq <= lim, checked above
+      if (j0 + jq + 16 <= lim) srow[16] = fmul(d1, scale);
+      if (j0 + jq + 32 <= lim) srow[32] = fmul(d2, scale);
+      if (j0 + jq + 48 <= lim) srow[48] = fmul(d3, scale);
+    }
+    __syncthreads();
+  }
+  stage(vbase, 0, 0);  // V chunk 0 loads while the softmax runs
+  // ---- max per (row, head), serial-scan semantics
+  for (int pr = warp; pr < P; pr += NW) {
+    const float *sg = sc + (size_t)pr * scs;
+    const int len = p0 + pr / G + 1;
+    float mx = bitsf(0x7fc00000u);
+    for (int j = lane; j < len; j += 32) mx = max_comb(mx, sg[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max_comb(mx, __shfl_xor_sync(FULL, mx, o));
+    if (lane == 0) red[pr] = is_nan(sg[0]) ? sg[0] : mx;
+  }
+  __syncthreads();
+  for (int pr = 0; pr < P; ++pr) {
+    float *sg = sc + (size_t)pr * scs;
+    const int len = p0 + pr / G + 1;
+    const float mg = red[pr];
+    for (int j = tid; j < len; j += NT) sg[j] = exp_pinned(fsub(sg[j], mg));
+  }
+  __syncthreads();
+  // ---- denominators: one lane per (row, head) chain
+  for (int pr = tid; pr < P; pr += NT) red[P + pr] = serial_sum4(sc + (size_t)pr * scs, p0 + pr / G + 1);
+  __syncthreads();
+  for (int pr = 0; pr < P; ++pr) {
+    float *sg = sc + (size_t)pr * scs;
+    const int len = p0 + pr / G + 1;
+    const float den = red[P + pr];
+    for (int j = tid; j < len; j += NT) sg[j] = fdiv(sg[j], den);
+  }
+  // ---- V-mix: thread (d, d + 1) = 2 (tid % (HD/2)) of pairs tid / (HD/2) + k S
+  const int d = 2 * (tid % (HD / 2)), slot = tid / (HD / 2);
+  float2 acc[PPT];
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) acc[k] = make_float2(0.0f, 0.0f);
+  const int full_to = p0 + 1;  // keys [0, full_to) are read by every row of the tile
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) stage(vbase, c + 1, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int j0 = c * JC;
+    const float *tile = tiles_s + (size_t)(c & 1) * JC * TS + d;
+    if (j0 + JC <= full_to) {
+      // every pair reads the whole chunk
+#pragma unroll 1
+      for (int jj = 0; jj < JC; jj += 4) {
+        const float2 v0 = *reinterpret_cast<const float2 *>(tile + (jj + 0) * TS);
+        const float2 v1 = *reinterpret_cast<const float2 *>(tile + (jj + 1) * TS);
+        const float2 v2 = *reinterpret_cast<const float2 *>(tile + (jj + 2) * TS);
+        const float2 v3 = *reinterpret_cast<const float2 *>(tile + (jj + 3) * TS);
+#pragma unroll
+        for (int k = 0; k < PPT; ++k) {
+          const int pr = slot + k * S;
+          if (pr < P) {
+            const float4 w = *reinterpret_cast<const float4 *>(sc + (size_t)pr * scs + j0 + jj);
+            float2 a = acc[k];
+            a = fadd_pair(a, fmul(w.x, v0.x), fmul(w.x, v0.y));
+            a = fadd_pair(a, fmul(w.y, v1.x), fmul(w.y, v1.y));
+            a = fadd_pair(a, fmul(w.z, v2.x), fmul(w.z, v2.y));
+            a = fadd_pair(a, fmul(w.w, v3.x), fmul(w.w, v3.y));
+            acc[k] = a;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < PPT; ++k) {
+        const int pr = slot + k * S;
+        if (pr < P) {
+          const int je = min(JC, p0 + pr / G + 1 - j0);  // keys of this chunk the row reads
+          const float *pg = sc + (size_t)pr * scs + j0;
+          float2 a = acc[k];
+          for (int jj = 0; jj < je; ++jj) {
+            const float p = pg[jj];
+            const float2 v = *reinterpret_cast<const float2 *>(tile + jj * TS);
+            a = fadd_pair(a, fmul(p, v.x), fmul(p, v.y));
+          }
+          acc[k] = a;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    const int pr = slot + k * S;
+    if (pr < P) {
+      const int i = pr / G, g = pr % G;
+      float *o = att + (size_t)(r0 + i) * ars + (((size_t)kvh * G + g) * HD + d) * acs;
+      o[0] = acc[k].x;
+      o[acs] = acc[k].y;
+    }
+  }
+}
+
+// Shared memory of k_attention_rows_s for tiles of up to rt rows.
+size_t attention_rows_s_smem_floats(int rt, int G, int hd, int max_len) {
+  const size_t P = (size_t)rt * G, scs = (((size_t)max_len + 3) & ~(size_t)3) + 4;
+  size_t f = P * hd + P * scs + 2 * P + 8;
+  f = (f + 3) & ~(size_t)3;
+  return f + (size_t)2 * ATT_JC * (hd + 4);
+}
+
+template <int HD, int G>
+static void run_attention_rows_s(const float *qkv, int ld, const int2 *tiles, int n_tiles, int rt, RowMap rm, int n_kv,
+                                 const float *kc, const float *vc, int max_pos, float *att, int ars, int acs,
+                                 int max_len, cudaStream_t s) {
+  const size_t smem = attention_rows_s_smem_floats(rt, G, HD, max_len) * sizeof(float);
+  static SmemLimit lim;
+  lim.ensure(k_attention_rows_s<HD, G>, smem);
+  k_attention_rows_s<HD, G><<<dim3(n_tiles, n_kv), ATTR_NT, smem, s>>>(qkv, ld, tiles, rm.seq, rm.pos, n_kv, kc, vc,
+                                                                      max_pos, att, ars, acs, max_len);
+}
+
 void launch_attention_rows(const float *qkv, int ld, const int2 *tiles, int n_tiles, int rt, RowMap rm, int n_heads,
                            int n_kv, int hd, const float *kcache, const float *vcache, int max_pos, bool tree,
                            float *att, int ars, int acs, int max_len, cudaStream_t s) {
   if (n_tiles <= 0) return;
   const int G = n_heads / n_kv;
+  if (!tree && rt * G <= 48 && attention_rows_s_smem_floats(rt, G, hd, max_len) * 4 <= 227 * 1024) {
+#define CIS2B_ATTR(HD_, G_)                                                                                         \
+    if (hd == HD_ && G == G_) {                                                                                     \
+      run_attention_rows_s<HD_, G_>(qkv, ld, tiles, n_tiles, rt, rm, n_kv, kcache, vcache, max_pos, att, ars, acs, \
+                                    max_len, s);                                                                    \
+      return;                                                                                                       \
+    }
+    CIS2B_ATTR(64, 3)
+    CIS2B_ATTR(64, 1)
+    CIS2B_ATTR(128, 2)
+#undef CIS2B_ATTR
+  }
   const size_t smem = attention_rows_smem_floats(rt, G, hd, max_len) * sizeof(float);
   static SmemLimit lim;
   if (smem > 48 * 1024) lim.ensure(k_attention_rows, smem);
