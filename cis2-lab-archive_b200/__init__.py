@@ -26,6 +26,7 @@ HEADER_PATH = os.path.join(ROOT_DIR, "include", "cis2b.h")
 
 SEQUENTIAL, TREE = 0, 1
 OP_MATMUL_DECODE = 2  # CIS2B_OP_MATMUL_DECODE: sequential order through the decode-step kernel
+OP_MATMUL_DECODE_TREE = 3  # CIS2B_OP_MATMUL_DECODE_TREE: tree order through the decode-step kernel
 PINNED_FUNCS = {"exp": 0, "sin": 1, "cos": 2, "ln": 3, "silu": 4, "rsqrt": 5}
 
 
@@ -241,13 +242,16 @@ def pinned_map(fn: str | int, x: np.ndarray, device: int = 0) -> np.ndarray:
 
 
 def matmul(W: np.ndarray, X: np.ndarray, tree: bool = False, device: int = 0, decode: bool = False) -> np.ndarray:
-    """Y = X @ widen(W).T in the pinned order.  decode=True runs the
-    sequential order through the few-row kernel of the decode steps."""
+    """Y = X @ widen(W).T in the pinned order.  decode=True runs it through
+    the few-row kernel of the decode steps (tree order needs k % 32 == 0)."""
     W = np.ascontiguousarray(W, dtype=np.uint16)
     X = np.ascontiguousarray(X, dtype=np.float32)
     rows, k = X.shape
     Y = np.zeros((rows, W.shape[0]), dtype=np.float32)
-    mode = OP_MATMUL_DECODE if decode else (TREE if tree else SEQUENTIAL)
+    if decode:
+        mode = OP_MATMUL_DECODE_TREE if tree else OP_MATMUL_DECODE
+    else:
+        mode = TREE if tree else SEQUENTIAL
     _check(lib().cis2b_op_matmul(device, _ptr(W), _ptr(X), rows, W.shape[0], k, mode, _ptr(Y)))
     return Y
 

@@ -900,6 +900,19 @@ void launch_tile32(const uint16_t *W, int N, int K, uint16_t *Wt, cudaStream_t s
   k_tile32<<<1184, 256, 0, s>>>(W, N, K, Wt, glu_half);
 }
 
+// One group of four products (c = ((p0 + p1) + (p2 + p3)), group g = 0..7
+// of a 32-product block) into the block's pairwise tree: levels 3, 4 and 5
+// join group sums (g0 + g1), ((g0 + g1) + (g2 + g3)), ...; the finished
+// block sum is added to acc (cis2_math.h:212-265).
+__device__ __forceinline__ void tree_group(float &acc, float &t3, float &t4, float &t5, float c, int g) {
+  if ((g & 1) == 0) { t3 = c; return; }
+  const float l3 = fadd(t3, c);
+  if ((g & 2) == 0) { t4 = l3; return; }
+  const float l4 = fadd(t4, l3);
+  if ((g & 4) == 0) { t5 = l4; return; }
+  acc = fadd(acc, fadd(t5, l4));
+}
+
 __device__ __forceinline__ float4 widen4(uint2 u) {
   return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
@@ -909,7 +922,12 @@ __device__ __forceinline__ float4 widen4(uint2 u) {
 // for the whole K (one copy up front).  XS = true: they stream through the
 // same ring as the weights, DEC_KC columns per stage, which keeps shared
 // memory small when ROWS x K is large (several blocks per SM instead of one).
-template <int TM, int RW, bool XS>
+// TREE: the v0.4 tree order (K % 32 == 0): each block of 32 products is
+// summed as the balanced pairwise tree of cis2_math.h:212-265, its sum
+// added to the running total from +0.  A lane builds the tree of its column
+// from groups of four products, ((p0 + p1) + (p2 + p3)), joining the eight
+// group sums of a block in three more levels as they complete.
+template <int TM, int RW, bool XS, bool TREE = false>
 __global__ void __launch_bounds__(32 * RW, 1)
 k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt, int K, int N, int M,
            float *__restrict__ Y, int ldy, const float *__restrict__ R, int ldr, const int32_t *y_slot,
@@ -960,9 +978,9 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
     cp_async_commit();
   }
 
-  float acc[TM];
+  float acc[TM], t3[TM], t4[TM], t5[TM];  // t3..t5: pending tree levels (TREE)
 #pragma unroll
-  for (int i = 0; i < TM; ++i) acc[i] = 0.0f;
+  for (int i = 0; i < TM; ++i) acc[i] = t3[i] = t4[i] = t5[i] = 0.0f;
   const int xstride = XS ? DEC_KC : K;  // row stride of the activations read below
   for (int c = 0; c < nc; ++c) {
     cp_async_wait<DEC_STAGES - 2>();
@@ -997,14 +1015,20 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
           p01[i] = fmul_pair(wv.x, wv.y, xv[i].x, xv[i].y);
           p23[i] = fmul_pair(wv.z, wv.w, xv[i].z, xv[i].w);
         }
+        if (TREE) {
 #pragma unroll
-        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p01[i].x);
+          for (int i = 0; i < TM; ++i)
+            tree_group(acc[i], t3[i], t4[i], t5[i], fadd(fadd(p01[i].x, p01[i].y), fadd(p23[i].x, p23[i].y)), kq & 7);
+        } else {
 #pragma unroll
-        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p01[i].y);
+          for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p01[i].x);
 #pragma unroll
-        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p23[i].x);
+          for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p01[i].y);
 #pragma unroll
-        for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p23[i].y);
+          for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p23[i].x);
+#pragma unroll
+          for (int i = 0; i < TM; ++i) acc[i] = fadd(acc[i], p23[i].y);
+        }
       }
     } else {
       for (int kq = 0; kq < kn / 4; ++kq) {
@@ -1012,10 +1036,15 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
 #pragma unroll
         for (int i = 0; i < TM; ++i) {
           const float4 xv = *reinterpret_cast<const float4 *>(xc + (size_t)i * xstride + 4 * kq);
-          acc[i] = fadd(acc[i], fmul(wv.x, xv.x));
-          acc[i] = fadd(acc[i], fmul(wv.y, xv.y));
-          acc[i] = fadd(acc[i], fmul(wv.z, xv.z));
-          acc[i] = fadd(acc[i], fmul(wv.w, xv.w));
+          if (TREE) {
+            const float c = fadd(fadd(fmul(wv.x, xv.x), fmul(wv.y, xv.y)), fadd(fmul(wv.z, xv.z), fmul(wv.w, xv.w)));
+            tree_group(acc[i], t3[i], t4[i], t5[i], c, kq & 7);
+          } else {
+            acc[i] = fadd(acc[i], fmul(wv.x, xv.x));
+            acc[i] = fadd(acc[i], fmul(wv.y, xv.y));
+            acc[i] = fadd(acc[i], fmul(wv.z, xv.z));
+            acc[i] = fadd(acc[i], fmul(wv.w, xv.w));
+          }
         }
       }
     }
@@ -1047,7 +1076,7 @@ k_gemm_dec(const float *__restrict__ X, int ldx, const uint16_t *__restrict__ Wt
   }
 }
 
-template <int TM, int RW, bool XS>
+template <int TM, int RW, bool XS, bool TREE>
 static void run_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, int M, float *Y, int ldy,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
                          cudaStream_t s) {
@@ -1055,10 +1084,10 @@ static void run_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int
   const size_t smem = (XS ? (size_t)DEC_STAGES * ROWS * DEC_KC * 4 : (size_t)ROWS * K * 4) +
                       (size_t)DEC_STAGES * DEC_KC * 32 * 2;
   static SmemLimit lim;
-  lim.ensure(k_gemm_dec<TM, RW, XS>, 227 * 1024);
+  lim.ensure(k_gemm_dec<TM, RW, XS, TREE>, 227 * 1024);
   dim3 grid((N + 31) / 32, (M + ROWS - 1) / ROWS);
-  k_gemm_dec<TM, RW, XS><<<grid, 32 * RW, smem, s>>>(X, ldx, Wt, K, N, M, Y, ldy, R, ldr, y_slot, y_slot_stride,
-                                                      glu);
+  k_gemm_dec<TM, RW, XS, TREE><<<grid, 32 * RW, smem, s>>>(X, ldx, Wt, K, N, M, Y, ldy, R, ldr, y_slot,
+                                                            y_slot_stride, glu);
 }
 
 // Rows per block: the largest candidate that still gives at least two
@@ -1073,7 +1102,7 @@ constexpr int kNumDecTiles = 4;
 // faster (4 x 3,072 rows: 30.7 us resident, 34.9 streamed).
 constexpr size_t DEC_RESIDENT_MAX = 48 * 1024;
 
-bool gemm_dec_ok(int K) { return K > 0 && K % 4 == 0; }
+bool gemm_dec_ok(int K, bool tree) { return K > 0 && K % (tree ? 32 : 4) == 0; }
 
 int gemm_dec_choice(int M, int N, int K) {
   const long n32 = (N + 31) / 32;
@@ -1091,14 +1120,21 @@ int gemm_dec_choice(int M, int N, int K) {
 
 void launch_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, int M, float *Y, int ldy,
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, cudaStream_t s,
-                     int glu) {
+                     int glu, bool tree) {
   if (M <= 0 || N <= 0) return;
   const int pick = gemm_dec_choice(M, N, K);
   const bool xs = (size_t)kDecTiles[pick].tm * kDecTiles[pick].rw * K * 4 > DEC_RESIDENT_MAX;
-#define CIS2B_DEC(TM_, RW_)                                                                                    \
-  do {                                                                                                         \
-    if (xs) run_gemm_dec<TM_, RW_, true>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s); \
-    else run_gemm_dec<TM_, RW_, false>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, glu, s);   \
+#define CIS2B_DEC2(TM_, RW_, TREE_)                                                                              \
+  do {                                                                                                          \
+    if (xs) run_gemm_dec<TM_, RW_, true, TREE_>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride, \
+                                                glu, s);                                                        \
+    else run_gemm_dec<TM_, RW_, false, TREE_>(X, ldx, Wt, K, N, M, Y, ldy, resid, ldr, y_slot, y_slot_stride,  \
+                                              glu, s);                                                          \
+  } while (0)
+#define CIS2B_DEC(TM_, RW_)                    \
+  do {                                        \
+    if (tree) CIS2B_DEC2(TM_, RW_, true);     \
+    else CIS2B_DEC2(TM_, RW_, false);         \
   } while (0)
   switch (pick) {
     case 0: CIS2B_DEC(8, 4); break;
@@ -1107,6 +1143,7 @@ void launch_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, 
     default: CIS2B_DEC(2, 2); break;
   }
 #undef CIS2B_DEC
+#undef CIS2B_DEC2
 }
 
 // ============================================================ attention

@@ -52,20 +52,21 @@ void launch_panelize(const uint16_t *W, int N, int K, uint16_t *Wp, cudaStream_t
 void launch_panelize(const uint16_t *W, int N, int K, float *Wp, cudaStream_t s, int il_half = 0);
 size_t panel_elems(int N, int K);
 
-// Decode form of the same product for few rows (sequential order only).  X is
-// row-major [M][ldx] (ldx % 4 == 0); Wt holds W bf16 in 32-column tiles
-// (launch_tile32).  resid / y_slot as launch_gemm.  Usable when gemm_dec_ok(K).
+// Decode form of the same product for few rows, in sequential order or (tree)
+// the v0.4 tree order.  X is row-major [M][ldx] (ldx % 4 == 0); Wt holds W
+// bf16 in 32-column tiles (launch_tile32).  resid / y_slot as launch_gemm.
+// Usable when gemm_dec_ok(K, tree).
 // glu = I > 0: W is a gate/up pair tiled with launch_tile32(..., glu_half = I)
 // and Y receives silu(gate) * up, [M][ldy] with I columns (N = 2I).
 void launch_gemm_dec(const float *X, int ldx, const uint16_t *Wt, int K, int N, int M, float *Y, int ldy,
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride,
-                     cudaStream_t s, int glu = 0);
+                     cudaStream_t s, int glu = 0, bool tree = false);
 // Wt[n32][kq][j][q] = W[32*n32 + j][4*kq + q], zero columns past N; K % 4 == 0.
 // glu_half = I (N = 2I, I % 16 == 0): tile n32 holds gate rows 16*n32 + j in
 // columns j < 16 and up rows I + 16*n32 + j - 16 in columns j >= 16.
 void launch_tile32(const uint16_t *W, int N, int K, uint16_t *Wt, cudaStream_t s, int glu_half = 0);
 __host__ __device__ size_t tile32_elems(int N, int K);
-bool gemm_dec_ok(int K);
+bool gemm_dec_ok(int K, bool tree = false);
 // Index into the decode tile list for (M, N, K): 0 (8x4) .. 3 (2x2).
 int gemm_dec_choice(int M, int N, int K);
 

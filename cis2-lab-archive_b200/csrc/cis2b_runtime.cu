@@ -118,7 +118,7 @@ struct cis2b_model {
   const float *lm_head_f = nullptr;
   DevBuf tiles;   // the same weights in 32-column tiles for the decode GEMM
   const uint16_t *lm_head_t = nullptr;
-  bool dec_tiles = false;  // decode steps use launch_gemm_dec (sequential mode, K % 4 == 0)
+  bool dec_tiles = false;  // decode steps use launch_gemm_dec (K % 4 == 0; tree mode K % 32 == 0)
   int dec_big_rows = DEC_BIG_ROWS;  // ... below this many rows (above: the register-tiled product)
   DevBuf inv_freq, cos_t, sin_t;
   cudaStream_t s_main = nullptr, s_sha = nullptr, s_prep = nullptr;
@@ -534,7 +534,8 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
   }
 
   // ---- decode tiles (same bf16 bits, 32 columns x 4 k per lane-row)
-  m->dec_tiles = !m->tree && gemm_dec_ok(m->H) && gemm_dec_ok(m->QD) && gemm_dec_ok(m->I) && m->I % 16 == 0;
+  m->dec_tiles = gemm_dec_ok(m->H, m->tree) && gemm_dec_ok(m->QD, m->tree) && gemm_dec_ok(m->I, m->tree) &&
+                 m->I % 16 == 0;
   if (m->dec_tiles) {
     const int NQKV = m->QD + 2 * m->KVD;
     size_t total = 0;
@@ -650,7 +651,7 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
   auto gemm = [&](const float *X, const uint16_t *Wp, const float *Wpf, const uint16_t *Wt, int K, int N, float *Y,
                   int ldy, const float *R, int ldr) {
     ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-    if (dec) launch_gemm_dec(X, K, Wt, K, N, rows, Y, ldy, R, ldr, nullptr, 0, s);
+    if (dec) launch_gemm_dec(X, K, Wt, K, N, rows, Y, ldy, R, ldr, nullptr, 0, s, 0, m->tree);
     else launch_gemm(X, ldm, Wp, Wpf, K, N, rows, Y, ldy, R, ldr, m->tree, nullptr, 0, s);
   };
   for (int l = 0; l < m->L; ++l) {
@@ -680,7 +681,7 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     launch_rmsnorm(h, H, w.post_norm, m->eps, H, rows, m->tree, ln, lnr, lnc, s);
     if (dec) {  // SwiGLU in the gate/up GEMM's epilogue
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm_dec(ln, H, w.tgu, H, 2 * I, rows, hid, I, nullptr, 0, nullptr, 0, s, I);
+      launch_gemm_dec(ln, H, w.tgu, H, 2 * I, rows, hid, I, nullptr, 0, nullptr, 0, s, I, m->tree);
     } else if (!m->tree && rows >= 64) {  // SwiGLU in the epilogue, hid written k-major
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
       launch_gemm_big(ln, ldm, w.fgu, H, 2 * I, rows, hid, 1, ldm, nullptr, 0, nullptr, 0, 1, s);
@@ -701,14 +702,16 @@ int head_rows(cis2b_model *m, const float *hin, int rows, float *Y, const int32_
               size_t slot_stride) {
   cudaStream_t s = m->s_main;
   const int ldb = round_up(rows, 64);  // lnlast is k-major [H][ldb] for the panel GEMM
-  const bool dec = m->dec_tiles && rows <= DEC_HEAD_ROWS;  // row-major [rows][H] for the decode GEMM
+  // Row-major [rows][H] for the decode GEMM.  In tree mode the panel kernel
+  // is the slower one from 64 rows on too, so decode steps keep the decode GEMM.
+  const bool dec = m->dec_tiles && (rows <= DEC_HEAD_ROWS || (m->tree && rows < m->dec_big_rows));
   launch_rmsnorm(hin, m->H, m->final_norm, m->eps, m->H, rows, m->tree, m->lnlast.as<float>(),
                  dec ? m->H : 1, dec ? 1 : ldb, s);
   {
     ProfScope p(m, CIS2B_PROF_LM_HEAD, s);
     if (dec)
       launch_gemm_dec(m->lnlast.as<float>(), m->H, m->lm_head_t, m->H, m->V, rows, Y, m->V, nullptr, 0, y_slot,
-                      slot_stride, s);
+                      slot_stride, s, 0, m->tree);
     else
       launch_gemm(m->lnlast.as<float>(), ldb, m->lm_head_p, m->lm_head_f, m->H, m->V, rows, Y, m->V, nullptr, 0,
                   m->tree, y_slot, slot_stride, s);
@@ -1431,11 +1434,12 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
                     int32_t reduction, float *Y) {
   if (!W || !X || !Y) return fail(CIS2B_ERR_ARG, "NULL buffer");
   if (rows <= 0 || n_out <= 0 || k <= 0 || k % 8) return fail(CIS2B_ERR_ARG, "bad shape (k must be a multiple of 8)");
-  if (reduction < 0 || reduction > CIS2B_OP_MATMUL_DECODE) return fail(CIS2B_ERR_ARG, "bad reduction");
-  if (reduction == CIS2B_OP_MATMUL_DECODE && (rows > 1024 || !gemm_dec_ok(k)))
-    return fail(CIS2B_ERR_ARG, "decode form: rows <= 1024 and k a multiple of 4");
+  if (reduction < 0 || reduction > CIS2B_OP_MATMUL_DECODE_TREE) return fail(CIS2B_ERR_ARG, "bad reduction");
+  const bool dec_form = reduction >= CIS2B_OP_MATMUL_DECODE, dec_tree = reduction == CIS2B_OP_MATMUL_DECODE_TREE;
+  if (dec_form && (rows > 1024 || !gemm_dec_ok(k, dec_tree)))
+    return fail(CIS2B_ERR_ARG, "decode form: rows <= 1024 and k a multiple of 4 (tree order: of 32)");
   CU(cudaSetDevice(device));
-  if (reduction == CIS2B_OP_MATMUL_DECODE) {
+  if (dec_form) {
     Scoped<uint16_t> dw, dt;
     Scoped<float> dx, dy;
     CU(cudaMalloc(&dw.p, 2 * (size_t)n_out * k));
@@ -1445,7 +1449,7 @@ int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t r
     CU(cudaMemcpy(dw.p, W, 2 * (size_t)n_out * k, cudaMemcpyHostToDevice));
     CU(cudaMemcpy(dx.p, X, 4 * (size_t)rows * k, cudaMemcpyHostToDevice));
     launch_tile32(dw.p, n_out, k, dt.p, 0);
-    launch_gemm_dec(dx.p, k, dt.p, k, n_out, rows, dy.p, n_out, nullptr, 0, nullptr, 0, 0);
+    launch_gemm_dec(dx.p, k, dt.p, k, n_out, rows, dy.p, n_out, nullptr, 0, nullptr, 0, 0, 0, dec_tree);
     CU_LAUNCHED();
     CU(cudaMemcpy(Y, dy.p, 4 * (size_t)rows * n_out, cudaMemcpyDeviceToHost));
     return CIS2B_OK;

@@ -195,9 +195,11 @@ const char *cis2b_last_error(void);
 int cis2b_op_pinned_map(int32_t device, int32_t fn, const float *x, float *y, size_t n);
 /* Y[r][o] = dot(W[o,:], X[r,:]) in the pinned order; W bf16 [n_out][k], k % 8 == 0.
  * reduction: CIS2B_REDUCTION_SEQUENTIAL or _TREE through the panel kernel the
- * prompt pass uses, or CIS2B_OP_MATMUL_DECODE: sequential order through the
- * few-row kernel decode steps use (rows <= 1024). */
+ * prompt pass uses, or CIS2B_OP_MATMUL_DECODE / _DECODE_TREE: sequential or
+ * tree order through the few-row kernel decode steps use (rows <= 1024; tree
+ * order: k % 32 == 0). */
 #define CIS2B_OP_MATMUL_DECODE 2
+#define CIS2B_OP_MATMUL_DECODE_TREE 3
 int cis2b_op_matmul(int32_t device, const uint16_t *W, const float *X, int32_t rows, int32_t n_out,
                     int32_t k, int32_t reduction, float *Y);
 /* Index (0-based) of the register tile the many-row product picks for
