@@ -1235,7 +1235,7 @@ size_t attention_smem_floats(int G, int hd, int max_len) {
 bool launch_attention_dec(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd, float *kcache,
                           float *vcache, int max_pos, float *att, int ars, int acs, int max_len,
                           const uint16_t *q_norm, const uint16_t *k_norm, float eps, const float *cos_t,
-                          const float *sin_t, cudaStream_t s);
+                          const float *sin_t, bool tree, cudaStream_t s);
 
 __global__ void k_attention(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos,
                             int nh, int nkv, int hd, float *kc, float *vc, int max_pos,
@@ -1439,9 +1439,9 @@ void launch_attention(float *qkv, int ld, int rows, RowMap rm, int n_heads, int 
                       const uint16_t *k_norm, float eps, const float *cos_t, const float *sin_t,
                       cudaStream_t s, float *dbg) {
   if (rows <= 0) return;
-  if (!tree && fuse_post && !dbg &&
+  if (fuse_post && !dbg &&
       launch_attention_dec(qkv, ld, rows, rm, n_heads, n_kv, hd, kcache, vcache, max_pos, att, ars, acs, max_len,
-                           q_norm, k_norm, eps, cos_t, sin_t, s))
+                           q_norm, k_norm, eps, cos_t, sin_t, tree, s))
     return;
   const int G = n_heads / n_kv;
   int nt = ((G * hd + 31) / 32) * 32;
@@ -1488,7 +1488,11 @@ size_t attention_dec_smem_floats(int G, int hd, int max_len, int stages) {
   return (size_t)G * hd + (size_t)G * att_dec_scs(max_len) + 64 + (size_t)stages * 64 * (hd + 4);
 }
 
-template <int HD, int G, int ST>
+// TREE: the v0.4 tree order for the two reductions it covers (the dots over
+// HD in 32-product pairwise trees, the denominator in 32-leaf blocks);
+// max, exp, division and the V-mix chains are the same as in sequential
+// order (cis2_math.h:212-265, 442-467).
+template <int HD, int G, int ST, bool TREE>
 __global__ void __launch_bounds__(AttDec<HD, G>::NT, 1)
 k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, int nkv, float *kc, float *vc,
                 int max_pos, float *att, int ars, int acs, int max_len, const uint16_t *qn, const uint16_t *kn,
@@ -1517,7 +1521,7 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
       const bool is_k = hh == G;
       float *x = is_k ? row + QD + (size_t)kvh * HD : row + ((size_t)kvh * G + hh) * HD;
       const uint16_t *nwt = is_k ? kn : qn;
-      if (nwt) warp_rmsnorm(x, nwt, eps, HD, false, tiles + (size_t)warp * 2 * HD, x);
+      if (nwt) warp_rmsnorm(x, nwt, eps, HD, TREE, tiles + (size_t)warp * 2 * HD, x);
       for (int i = lane; i < half; i += 32) {
         float x1 = x[i], x2 = x[i + half], c = ct[i], sn = st[i];
         float o1 = fadd(fmul(x1, c), fmul(fneg(x2), sn));
@@ -1580,15 +1584,20 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
     if (sg < G && sj < jc) {
       const float4 *k4 = reinterpret_cast<const float4 *>(tile + sj * TS);
       const float4 *q4 = reinterpret_cast<const float4 *>(q + sg * HD);
-      float d = 0.0f;
+      float d = 0.0f, t3 = 0.0f, t4 = 0.0f, t5 = 0.0f;
 #pragma unroll
       for (int i = 0; i < NQ; ++i) {
         const float4 b = k4[i];
         const float4 a = q4[i];
-        d = fadd(d, fmul(a.x, b.x));
-        d = fadd(d, fmul(a.y, b.y));
-        d = fadd(d, fmul(a.z, b.z));
-        d = fadd(d, fmul(a.w, b.w));
+        if (TREE) {
+          tree_group(d, t3, t4, t5, fadd(fadd(fmul(a.x, b.x), fmul(a.y, b.y)), fadd(fmul(a.z, b.z), fmul(a.w, b.w))),
+                     i & 7);
+        } else {
+          d = fadd(d, fmul(a.x, b.x));
+          d = fadd(d, fmul(a.y, b.y));
+          d = fadd(d, fmul(a.z, b.z));
+          d = fadd(d, fmul(a.w, b.w));
+        }
       }
       const float sv = fmul(d, scale);  // scale after the dot (gpu/README.md §4)
       sc[(size_t)sg * scs + j0 + sj] = sv;
@@ -1619,7 +1628,19 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
     for (int j = tid; j < len; j += NT) srow[j] = exp_pinned(fsub(srow[j], mg));
   }
   __syncthreads();
-  if (tid < G) red[32 + tid] = serial_sum4(sc + (size_t)tid * scs, len);
+  if (TREE) {  // head g's 32-leaf blocks (zero-padded) in warp g, block sums added in order
+    if (warp < G) {
+      const float *srow = sc + (size_t)warp * scs;
+      float acc = 0.0f;
+      for (int j0 = 0; j0 < len; j0 += 32) {
+        const float t = warp_tree32(j0 + lane < len ? srow[j0 + lane] : 0.0f);
+        acc = fadd(acc, t);
+      }
+      if (lane == 0) red[32 + warp] = acc;
+    }
+  } else if (tid < G) {
+    red[32 + tid] = serial_sum4(sc + (size_t)tid * scs, len);
+  }
   __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -1681,31 +1702,35 @@ k_attention_dec(float *qkv, int ld, const int32_t *rseq, const int32_t *rpos, in
   }
 }
 
-template <int HD, int G, int ST>
+template <int HD, int G, int ST, bool TREE>
 static void run_attention_dec(float *qkv, int ld, int rows, RowMap rm, int n_kv, float *kc, float *vc, int max_pos,
                               float *att, int ars, int acs, int max_len, const uint16_t *qn, const uint16_t *kn,
                               float eps, const float *cos_t, const float *sin_t, cudaStream_t s) {
   const size_t smem = attention_dec_smem_floats(G, HD, max_len, ST) * sizeof(float);
   static SmemLimit lim;
-  lim.ensure(k_attention_dec<HD, G, ST>, smem);
-  k_attention_dec<HD, G, ST><<<dim3(rows, n_kv), AttDec<HD, G>::NT, smem, s>>>(
+  lim.ensure(k_attention_dec<HD, G, ST, TREE>, smem);
+  k_attention_dec<HD, G, ST, TREE><<<dim3(rows, n_kv), AttDec<HD, G>::NT, smem, s>>>(
       qkv, ld, rm.seq, rm.pos, n_kv, kc, vc, max_pos, att, ars, acs, max_len, qn, kn, eps, cos_t, sin_t);
 }
 
 // Decode-step attention through the specialised kernel when it covers the
-// shape (sequential mode, (head size, group) of the configurations built
-// here); returns false if the caller must use the generic kernel.
+// shape ((head size, group) of the configurations built here); returns
+// false if the caller must use the generic kernel.
 bool launch_attention_dec(float *qkv, int ld, int rows, RowMap rm, int n_heads, int n_kv, int hd, float *kcache,
                           float *vcache, int max_pos, float *att, int ars, int acs, int max_len,
                           const uint16_t *q_norm, const uint16_t *k_norm, float eps, const float *cos_t,
-                          const float *sin_t, cudaStream_t s) {
+                          const float *sin_t, bool tree, cudaStream_t s) {
   if (rows <= 0) return true;
   const int G = n_heads / n_kv;
   constexpr int ST = ATT_DEC_STAGES;
 #define CIS2B_ATTD(HD_, G_)                                                                                   \
   if (hd == HD_ && G == G_ && attention_dec_smem_floats(G_, HD_, max_len, ST) * 4 <= 227 * 1024) {            \
-    run_attention_dec<HD_, G_, ST>(qkv, ld, rows, rm, n_kv, kcache, vcache, max_pos, att, ars, acs, max_len, \
-                                   q_norm, k_norm, eps, cos_t, sin_t, s);                                     \
+    if (tree)                                                                                                 \
+      run_attention_dec<HD_, G_, ST, true>(qkv, ld, rows, rm, n_kv, kcache, vcache, max_pos, att, ars, acs,   \
+                                           max_len, q_norm, k_norm, eps, cos_t, sin_t, s);                    \
+    else                                                                                                      \
+      run_attention_dec<HD_, G_, ST, false>(qkv, ld, rows, rm, n_kv, kcache, vcache, max_pos, att, ars, acs,  \
+                                            max_len, q_norm, k_norm, eps, cos_t, sin_t, s);                   \
     return true;                                                                                              \
   }
   CIS2B_ATTD(64, 3)
