@@ -216,23 +216,27 @@ __global__ void k_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps,
 }
 // Sequential-mode RMSNorm of up to 32 rows per block: the block stages its
 // rows in shared memory (row pitch n+4 floats, so the 16-byte loads of the
-// 32 lanes below hit distinct banks), lane r of warp 0 then runs row r's
-// dependent sum of squares -- 32 chains side by side, four squares per
+// lanes below hit distinct banks), lane r of warp 0 then runs row r's
+// dependent sum of squares -- rb chains side by side, four squares per
 // load -- and every thread writes the scaled rows with coalesced stores.
+// rb (rows per block, a power of two) is chosen per launch: the chain is the
+// same length whatever rb is, so few rows go one or two per block over many
+// SMs (decode steps), many rows 32 per block.
 constexpr int RMS_ROWS = 32, RMS_THREADS = 256;
 __global__ void __launch_bounds__(RMS_THREADS, 1)
 k_rmsnorm_rows(const float *__restrict__ x, int ldx, const uint16_t *__restrict__ w, float eps, int n, int rows,
-               float *__restrict__ out, int ors, int ocs) {
-  extern __shared__ __align__(16) float sm[];  // [RMS_ROWS][n + 4], then [RMS_ROWS] inv
+               int rb, float *__restrict__ out, int ors, int ocs) {
+  extern __shared__ __align__(16) float sm[];  // [rb][n + 4], then [RMS_ROWS] inv
   const int P = n + 4, nq = n / 4;
-  float *inv_s = sm + RMS_ROWS * P;
-  const int r0 = blockIdx.x * RMS_ROWS;
-  const int nr = min(RMS_ROWS, rows - r0);
+  float *inv_s = sm + rb * P;
+  const int r0 = blockIdx.x * rb;
+  const int nr = min(rb, rows - r0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = RMS_THREADS / 32;
   const uint32_t sb = (uint32_t)__cvta_generic_to_shared(sm);
-  for (int r = warp; r < nr; r += nw)
-    for (int q = lane; q < nq; q += 32)
-      cp_async16(sb + (uint32_t)((r * P + 4 * q) * 4), x + (size_t)(r0 + r) * ldx + 4 * q);
+  for (int i = threadIdx.x; i < nr * nq; i += RMS_THREADS) {
+    const int r = i / nq, q = i - r * nq;
+    cp_async16(sb + (uint32_t)((r * P + 4 * q) * 4), x + (size_t)(r0 + r) * ldx + 4 * q);
+  }
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
@@ -269,11 +273,12 @@ k_rmsnorm_rows(const float *__restrict__ x, int ldx, const uint16_t *__restrict_
       float *o = out + (size_t)(r0 + r) * ors;
       for (int k = lane; k < n; k += 32) o[k] = fmul(fmul(sm[r * P + k], inv), widen_bf16(w[k]));
     }
-  } else {  // k-major out: lanes along rows, warps along k
-    if (lane < nr) {
-      const float inv = inv_s[lane];
-      for (int k = warp; k < n; k += nw)
-        out[(size_t)(r0 + lane) * ors + (size_t)k * ocs] = fmul(fmul(sm[lane * P + k], inv), widen_bf16(w[k]));
+  } else {  // k-major out: a warp covers rb rows (lanes along rows first) x 32 / rb k
+    const int r = lane % rb, kw = 32 / rb;
+    if (r < nr) {
+      const float inv = inv_s[r];
+      for (int k = warp * kw + lane / rb; k < n; k += nw * kw)
+        out[(size_t)(r0 + r) * ors + (size_t)k * ocs] = fmul(fmul(sm[r * P + k], inv), widen_bf16(w[k]));
     }
   }
 }
@@ -281,12 +286,15 @@ k_rmsnorm_rows(const float *__restrict__ x, int ldx, const uint16_t *__restrict_
 void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n, int rows, bool tree,
                     float *out, int ors, int ocs, cudaStream_t s) {
   if (rows <= 0) return;
-  const size_t rsm = ((size_t)RMS_ROWS * (n + 4) + RMS_ROWS) * sizeof(float);
+  // Rows per block: a power of two, so that all 148 SMs get a block before a
+  // block takes more rows (at most 32).
+  int rb = 1;
+  while (rb < RMS_ROWS && rb * 148 < rows) rb *= 2;
+  const size_t rsm = ((size_t)rb * (n + 4) + RMS_ROWS) * sizeof(float);
   if (!tree && n % 4 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && rsm <= 227 * 1024) {
     static SmemLimit lim;
     lim.ensure(k_rmsnorm_rows, 227 * 1024);
-    k_rmsnorm_rows<<<(rows + RMS_ROWS - 1) / RMS_ROWS, RMS_THREADS, rsm, s>>>(x, ldx, w, eps, n, rows, out, ors,
-                                                                              ocs);
+    k_rmsnorm_rows<<<(rows + rb - 1) / rb, RMS_THREADS, rsm, s>>>(x, ldx, w, eps, n, rows, rb, out, ors, ocs);
     return;
   }
   const int wpb = 4;
