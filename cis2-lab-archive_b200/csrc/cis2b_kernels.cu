@@ -1955,10 +1955,12 @@ k_attention_rows(const float *qkv, int ld, const int2 *tiles, const int32_t *rse
 
 // Sequential-mode prompt-pass attention specialised on the head size HD and
 // the group G (the same arithmetic as k_attention_rows, in the same order).
-// Per chunk of ATT_JC keys, thread t computes the dots of pair t / 16 with
-// keys t % 16 + 16 u, u = 0..3: q is read once for four independent chains
-// and the four key rows of a half-warp's lanes are consecutive (the TS
-// pitch keeps those loads conflict-free).  In the V-mix a thread owns two
+// Per chunk of ATT_JC keys, a thread computes the dots of one row of the
+// tile with one key for all G heads of the group: each 16-byte key load
+// feeds G independent chains (the scores were bound by shared-memory
+// bandwidth when every (head, key) dot loaded its key), the q loads are
+// broadcasts, and a warp's 32 key rows are consecutive (the TS pitch keeps
+// those loads conflict-free).  In the V-mix a thread owns two
 // adjacent d of up to PPT pairs: per key one 8-byte value load serves all
 // its pairs, the weights of four keys come in one 16-byte load per pair,
 // and each pair's two chains take one packed add per key.
@@ -2018,34 +2020,28 @@ k_attention_rows_s(const float *qkv, int ld, const int2 *tiles, const int32_t *r
     __syncthreads();
     const int j0 = c * JC;
     const float *tile = tiles_s + (size_t)(c & 1) * JC * TS;
-    for (int u0 = tid; u0 < P * 16; u0 += NT) {
-      const int pr = u0 >> 4, jq = u0 & 15;
-      const int lim = p0 + pr / G;             // last key this row reads
-      if (j0 + jq > lim) continue;             // no key of this unit is read
-      const float4 *q4 = reinterpret_cast<const float4 *>(q + (size_t)pr * HD);
-      const float4 *k0 = reinterpret_cast<const float4 *>(tile + (jq) * TS);
-      const float4 *k1 = reinterpret_cast<const float4 *>(tile + (jq + 16) * TS);
-      const float4 *k2 = reinterpret_cast<const float4 *>(tile + (jq + 32) * TS);
-      const float4 *k3 = reinterpret_cast<const float4 *>(tile + (jq + 48) * TS);
-      float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+    for (int u0 = tid; u0 < nr * JC; u0 += NT) {
+      const int i = u0 / JC, jj = u0 % JC;     // row i of the tile, key j0 + jj: all G heads
+      if (j0 + jj > p0 + i) continue;          // past this row's position (and past the chunk)
+      const float4 *k4 = reinterpret_cast<const float4 *>(tile + jj * TS);
+      const float4 *q4 = reinterpret_cast<const float4 *>(q + (size_t)i * G * HD);
+      float d[G];
 #pragma unroll
-      for (int i = 0; i < NQ; ++i) {
-        const float4 a = q4[i];
-        const float4 b0 = k0[i], b1 = k1[i], b2 = k2[i], b3 = k3[i];
-        d0 = fadd(d0, fmul(a.x, b0.x)); d1 = fadd(d1, fmul(a.x, b1.x));
-        d2 = fadd(d2, fmul(a.x, b2.x)); d3 = fadd(d3, fmul(a.x, b3.x));
-        d0 = fadd(d0, fmul(a.y, b0.y)); d1 = fadd(d1, fmul(a.y, b1.y));
-        d2 = fadd(d2, fmul(a.y, b2.y)); d3 = fadd(d3, fmul(a.y, b3.y));
-        d0 = fadd(d0, fmul(a.z, b0.z)); d1 = fadd(d1, fmul(a.z, b1.z));
-        d2 = fadd(d2, fmul(a.z, b2.z)); d3 = fadd(d3, fmul(a.z, b3.z));
-        d0 = fadd(d0, fmul(a.w, b0.w)); d1 = fadd(d1, fmul(a.w, b1.w));
-        d2 = fadd(d2, fmul(a.w, b2.w)); d3 = fadd(d3, fmul(a.w, b3.w));
+      for (int g = 0; g < G; ++g) d[g] = 0.0f;
+#pragma unroll
+      for (int t = 0; t < NQ; ++t) {
+        const float4 b = k4[t];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 a = q4[g * NQ + t];
+          d[g] = fadd(d[g], fmul(a.x, b.x));
+          d[g] = fadd(d[g], fmul(a.y, b.y));
+          d[g] = fadd(d[g], fmul(a.z, b.z));
+          d[g] = fadd(d[g], fmul(a.w, b.w));
+        }
       }
-      float *srow = sc + (size_t)pr * scs + j0 + jq;
-      srow[0] = fmul(d0, scale);               // j0 + jq <= lim, checked above
-      if (j0 + jq + 16 <= lim) srow[16] = fmul(d1, scale);
-      if (j0 + jq + 32 <= lim) srow[32] = fmul(d2, scale);
-      if (j0 + jq + 48 <= lim) srow[48] = fmul(d3, scale);
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[(size_t)(i * G + g) * scs + j0 + jj] = fmul(d[g], scale);
     }
     __syncthreads();
   }
