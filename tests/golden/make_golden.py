@@ -61,6 +61,11 @@ CASES = {
     # gives rank r sequences 64r .. 64r+63 (r < 8); C5 strong scaling over 8
     # GPUs gives rank r sequences 32r .. 32r+31, checked here at 32r + 5.
     "c2_shards": ("smollm2", ("workload", "c2", 64, 448), 256, False, False),
+    # Tree mode on the other two head shapes of the decode kernels (head size
+    # 64 with one query head per KV head; head size 128, two per KV head, with
+    # the Qwen3 q/k norm): the first sequences of C3 and C4, 16 tokens.
+    "tree_llama160m": ("llama160m", ("workload", "c3", 0, 4), 16, True, False),
+    "tree_qwen3": ("qwen3_0p6b", ("workload", "c4", 0, 2), 16, True, True),
     "c5_spread": ("smollm2", ("workload_idx", "c5", [37, 69, 101, 133, 165, 197, 229]), 1024, False, False),
 }
 

@@ -37,7 +37,7 @@ def check_against_golden(r: dict, g: dict, first: int = 0):
 
 
 SMALL = [n for n in golden_names() if n.startswith(("tiny", "mid"))]
-FULL = [n for n in golden_names() if n.startswith("c")]
+FULL = [n for n in golden_names() if n.startswith(("c", "tree_"))]
 
 
 @pytest.mark.parametrize("name", SMALL)
