@@ -316,3 +316,22 @@ def test_matmul_shapes_reach_every_register_tile(pkg):
     seen = {int(L.cis2b_op_gemm_tile(m, n)) for m, n, _ in SHAPES if m >= 64}
     assert seen == set(range(len(BIG_TILES))), sorted(seen)
     assert L.cis2b_op_gemm_tile(63, 100) == -1
+
+
+# (rows, n_out) -> the register tile (index into BIG_TILES) that measured fastest,
+# or within 5 % of it, on B200 for the workloads' products (fp32 panels, 32-deep
+# k stages): decode steps of C5 (256 rows) and C3 (300 rows), their lm_head, and
+# the C2 prompt pass (4,096 rows).
+MEASURED_TILE_CHOICES = {
+    (256, 960): {2, 3}, (256, 576): {3, 4}, (256, 3072): {2, 3}, (300, 2304): {3}, (300, 768): {2, 3},
+    (300, 6144): {2, 3}, (300, 32000): {1, 2}, (256, 49152): {0, 1}, (4096, 3072): {0, 1},
+}
+
+
+@pytest.mark.parametrize("rows,n", sorted(MEASURED_TILE_CHOICES))
+def test_tile_choice_matches_measured_best(rows, n, pkg):
+    """gemm_big_choice's cost model picks, for the workloads' product shapes,
+    a tile that measured fastest (or within 5 %) in the standalone sweep."""
+    L = pkg.lib()
+    L.cis2b_op_gemm_tile.argtypes = [ctypes.c_int32, ctypes.c_int32]
+    assert int(L.cis2b_op_gemm_tile(rows, n)) in MEASURED_TILE_CHOICES[(rows, n)]
