@@ -593,6 +593,17 @@ __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
   return r;
 }
 
+// tree_group (below) on two independent chains at once (packed adds).
+__device__ __forceinline__ void tree_group2(float2 &acc, float2 &t3, float2 &t4, float2 &t5, float2 c, int g) {
+  if ((g & 1) == 0) { t3 = c; return; }
+  const float2 l3 = fadd_pair(t3, c.x, c.y);
+  if ((g & 2) == 0) { t4 = l3; return; }
+  const float2 l4 = fadd_pair(t4, l3.x, l3.y);
+  if ((g & 4) == 0) { t5 = l4; return; }
+  const float2 b = fadd_pair(t5, l4.x, l4.y);
+  acc = fadd_pair(acc, b.x, b.y);
+}
+
 // Block tile BM x BN over TY x TX threads; a thread owns TMR rows x TNC
 // columns (TMR * TNC output chains).  Rows come in blocks of RW = min(TMR,
 // 4) consecutive rows, RW * TY apart; columns in blocks of CW = min(TNC, 4),
@@ -606,12 +617,16 @@ __device__ __forceinline__ float2 fadd_pair(float2 a, float b0, float b1) {
 // pinned order bit for bit (measured: most outputs of every tile shape
 // differed), so that pairing is never formed here.
 // Wpf: fp32 panels [N8][K][8] (launch_panelize into float).
+// TREE: the v0.4 tree order (K % 32 == 0; a KT = 32 stage is one block):
+// the products of four consecutive k form ((p0 + p1) + (p2 + p3)) per
+// chain, and the eight group sums of the block join in three more pairwise
+// levels (tree_group2) before the block sum is added to the chain.
 // Output element (m, n) goes to Y[m * ysm + n * ysn] (row-major: ysm = ldy,
 // ysn = 1; k-major for the next product: ysm = 1, ysn = ldm).  glu: W is a
 // gate/up pair panelised with its rows interleaved (gate i, up i at rows 2i,
 // 2i + 1), so a column pair (n, n + 1) is (gate i, up i) and the epilogue
 // writes silu(gate) * up as output column i = n / 2 (cis2_model.h:619-623).
-template <int TY, int TX, int TMR, int TNC, int ST, int KT>
+template <int TY, int TX, int TMR, int TNC, int ST, int KT, bool TREE>
 __global__ void __launch_bounds__(TY * TX, 1)
 k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf, int K, int N, int M,
            float *__restrict__ Y, int ysm, int ysn, const float *__restrict__ R, int ldr, const int32_t *y_slot,
@@ -626,7 +641,7 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf,
   constexpr int WCH = WF / 4;      // 16-byte W chunks per stage
   constexpr int PF = TMR * TNC >= 16 ? 2 : 4;  // register prefetch distance, k-steps
   static_assert((RW == 2 || RW == 4) && (CW == 2 || CW == 4) && BM % 4 == 0 && BN % 8 == 0, "tile shape");
-  static_assert(ST >= 2 && KT % 4 == 0, "pipeline shape");
+  static_assert(ST >= 2 && KT % 4 == 0 && (!TREE || KT == 32), "pipeline shape");
   extern __shared__ __align__(16) float smem[];
   float *Xs = smem;            // [ST][KT][BM]
   float *Ws = smem + ST * XF;  // [ST][KT][BN]
@@ -656,6 +671,9 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf,
     }
   };
   float2 acc[TMR][TNP];
+  // Tree order only: the pending pairwise sums of the current 32-k block.
+  float2 l1[TREE ? TMR : 1][TREE ? TNP : 1], l1b[TREE ? TMR : 1][TREE ? TNP : 1];
+  float2 t3[TREE ? TMR : 1][TREE ? TNP : 1], t4[TREE ? TMR : 1][TREE ? TNP : 1], t5[TREE ? TMR : 1][TREE ? TNP : 1];
 #pragma unroll
   for (int i = 0; i < TMR; ++i)
 #pragma unroll
@@ -711,11 +729,33 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf,
 #pragma unroll
       for (int j = 0; j < TNC; ++j) w[j] = wb[b][j];
       if (k + PF < KT) ld(b, k + PF);
+      if (TREE) {
+        const int km = k & 3;
 #pragma unroll
-      for (int i = 0; i < TMR; ++i)
+        for (int i = 0; i < TMR; ++i)
 #pragma unroll
-        for (int j = 0; j < TNP; ++j)
-          acc[i][j] = fadd_pair(acc[i][j], fmul(w[2 * j], x[i]), fmul(w[2 * j + 1], x[i]));
+          for (int j = 0; j < TNP; ++j) {
+            const float2 pp = make_float2(fmul(w[2 * j], x[i]), fmul(w[2 * j + 1], x[i]));
+            if (km == 0) {
+              l1[TREE ? i : 0][TREE ? j : 0] = pp;
+            } else if (km == 1) {
+              l1[TREE ? i : 0][TREE ? j : 0] = fadd_pair(l1[TREE ? i : 0][TREE ? j : 0], pp.x, pp.y);
+            } else if (km == 2) {
+              l1b[TREE ? i : 0][TREE ? j : 0] = pp;
+            } else {
+              const float2 l2b = fadd_pair(l1b[TREE ? i : 0][TREE ? j : 0], pp.x, pp.y);
+              const float2 c = fadd_pair(l1[TREE ? i : 0][TREE ? j : 0], l2b.x, l2b.y);
+              tree_group2(acc[i][j], t3[TREE ? i : 0][TREE ? j : 0], t4[TREE ? i : 0][TREE ? j : 0],
+                          t5[TREE ? i : 0][TREE ? j : 0], c, (k >> 2) & 7);
+            }
+          }
+      } else {
+#pragma unroll
+        for (int i = 0; i < TMR; ++i)
+#pragma unroll
+          for (int j = 0; j < TNP; ++j)
+            acc[i][j] = fadd_pair(acc[i][j], fmul(w[2 * j], x[i]), fmul(w[2 * j + 1], x[i]));
+      }
     }
   }
   cp_async_wait<0>();
@@ -742,17 +782,17 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf,
   }
 }
 
-template <int TY, int TX, int TMR, int TNC, int ST, int KT>
+template <int TY, int TX, int TMR, int TNC, int ST, int KT, bool TREE>
 static void run_gemm_big(const float *XT, int ldm, const float *Wpf, int K, int N, int M, float *Y, int ysm, int ysn,
                          const float *R, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
                          cudaStream_t s) {
   constexpr int BM = TMR * TY, BN = TNC * TX;
   const size_t smem = (size_t)ST * KT * (BM + BN) * 4;
   static SmemLimit lim;
-  lim.ensure(k_gemm_big<TY, TX, TMR, TNC, ST, KT>, smem);
+  lim.ensure(k_gemm_big<TY, TX, TMR, TNC, ST, KT, TREE>, smem);
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  k_gemm_big<TY, TX, TMR, TNC, ST, KT><<<grid, TY * TX, smem, s>>>(XT, ldm, Wpf, K, N, M, Y, ysm, ysn, R, ldr,
-                                                                    y_slot, y_slot_stride, glu);
+  k_gemm_big<TY, TX, TMR, TNC, ST, KT, TREE><<<grid, TY * TX, smem, s>>>(XT, ldm, Wpf, K, N, M, Y, ysm, ysn, R,
+                                                                          ldr, y_slot, y_slot_stride, glu);
 }
 
 // Block tile choice for the sequential product from 64 rows on (the prompt
@@ -771,13 +811,16 @@ struct BigCfg { int ty, tx, tmr, tnc; };
 static const BigCfg kBigTiles[] = {{16, 16, 8, 4}, {16, 16, 4, 4}, {16, 8, 4, 4}, {16, 8, 4, 2}, {8, 16, 2, 2}};
 constexpr int kNumBigTiles = 5;
 
-int gemm_big_choice(int M, int N) {
-  int best = 0;
+bool gemm_big_ok(int K, bool tree) { return !tree || K % 32 == 0; }
+
+int gemm_big_choice(int M, int N, bool tree) {
+  int best = -1;
   double best_cost = 0;
   for (int i = 0; i < kNumBigTiles; ++i) {
     const BigCfg &c = kBigTiles[i];
     const int bm = c.tmr * c.ty, bn = c.tnc * c.tx, nt = c.ty * c.tx, chains = c.tmr * c.tnc;
-    if (i > 0 && M < bm / 2) continue;  // at most half a row tile wasted
+    if (tree && chains > 16) continue;               // the tree's pending sums take 6 registers per chain pair
+    if (best >= 0 && M < bm / 2) continue;           // at most half a row tile wasted
     const long blocks = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
     const long per_sm = (blocks + 147) / 148;
     const double warps = (double)per_sm * nt / 32.0;
@@ -785,35 +828,43 @@ int gemm_big_choice(int M, int N) {
     const double busy = warps < need ? warps / need : 1.0;
     const double eff = chains >= 32 ? 1.0 : chains >= 16 ? 0.95 : chains >= 8 ? 0.9 : 0.8;
     const double cost = (double)per_sm * bm * bn / (busy * eff);
-    if (i == 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
+    if (best < 0 || cost < best_cost * 0.97) { best = i; best_cost = cost; }
   }
   return best;
 }
 
 void launch_gemm_big(const float *XT, int ldm, const float *Wpf, int K, int N, int M, float *Y, int ysm, int ysn,
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
-                     cudaStream_t s) {
+                     cudaStream_t s, bool tree) {
   if (M <= 0 || N <= 0) return;
-#define CIS2B_BIG(TY_, TX_, TMR_, TNC_, ST_, KT_)                                                                  \
-  run_gemm_big<TY_, TX_, TMR_, TNC_, ST_, KT_>(XT, ldm, Wpf, K, N, M, Y, ysm, ysn, resid, ldr, y_slot, y_slot_stride, \
-                                               glu, s)
+#define CIS2B_BIG2(TY_, TX_, TMR_, TNC_, ST_, KT_, TREE_)                                                    \
+  run_gemm_big<TY_, TX_, TMR_, TNC_, ST_, KT_, TREE_>(XT, ldm, Wpf, K, N, M, Y, ysm, ysn, resid, ldr, y_slot, \
+                                                      y_slot_stride, glu, s)
+#define CIS2B_BIG(TY_, TX_, TMR_, TNC_, ST_, KT_)                 \
+  do {                                                           \
+    if (tree) CIS2B_BIG2(TY_, TX_, TMR_, TNC_, ST_, KT_, true);  \
+    else CIS2B_BIG2(TY_, TX_, TMR_, TNC_, ST_, KT_, false);      \
+  } while (0)
   // Stage depth and k per stage per tile, measured on B200 (fp32 panels).
-  switch (gemm_big_choice(M, N)) {
-    case 0: CIS2B_BIG(16, 16, 8, 4, 3, 32); break;
+  switch (gemm_big_choice(M, N, tree)) {
+    case 0:
+      if (!tree) { CIS2B_BIG2(16, 16, 8, 4, 3, 32, false); break; }  // (not chosen in tree order)
+      [[fallthrough]];
     case 1: CIS2B_BIG(16, 16, 4, 4, 4, 32); break;
     case 2: CIS2B_BIG(16, 8, 4, 4, 6, 32); break;
     case 3: CIS2B_BIG(16, 8, 4, 2, 4, 32); break;
     default: CIS2B_BIG(8, 16, 2, 2, 4, 32); break;
   }
 #undef CIS2B_BIG
+#undef CIS2B_BIG2
 }
 
 void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, const float *Wpf, int K, int N, int M, float *Y,
                  int ldy, const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
-  if (!tree && M >= 64) {
-    launch_gemm_big(XT, ldm, Wpf, K, N, M, Y, ldy, 1, resid, ldr, y_slot, y_slot_stride, 0, s);
+  if (M >= 64 && gemm_big_ok(K, tree)) {
+    launch_gemm_big(XT, ldm, Wpf, K, N, M, Y, ldy, 1, resid, ldr, y_slot, y_slot_stride, 0, s, tree);
     return;
   }
   // Fewer rows, or tree mode: SIMT register tiles (tree mode with the
@@ -1964,7 +2015,10 @@ k_attention_rows(const float *qkv, int ld, const int2 *tiles, const int32_t *rse
 // adjacent d of up to PPT pairs: per key one 8-byte value load serves all
 // its pairs, the weights of four keys come in one 16-byte load per pair,
 // and each pair's two chains take one packed add per key.
-template <int HD, int G>
+// TREE: the tree order for the dots (32-product pairwise trees over HD)
+// and the denominators (32-leaf blocks, block sums in order); the V-mix
+// chains are the same in both orders.
+template <int HD, int G, bool TREE>
 __global__ void __launch_bounds__(ATTR_NT, 2)
 k_attention_rows_s(const float *qkv, int ld, const int2 *tiles, const int32_t *rseq, const int32_t *rpos, int nkv,
                    const float *kc, const float *vc, int max_pos, float *att, int ars, int acs, int max_len) {
@@ -2025,19 +2079,24 @@ k_attention_rows_s(const float *qkv, int ld, const int2 *tiles, const int32_t *r
       if (j0 + jj > p0 + i) continue;          // past this row's position (and past the chunk)
       const float4 *k4 = reinterpret_cast<const float4 *>(tile + jj * TS);
       const float4 *q4 = reinterpret_cast<const float4 *>(q + (size_t)i * G * HD);
-      float d[G];
+      float d[G], t3[G], t4[G], t5[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) d[g] = 0.0f;
+      for (int g = 0; g < G; ++g) d[g] = t3[g] = t4[g] = t5[g] = 0.0f;
 #pragma unroll
       for (int t = 0; t < NQ; ++t) {
         const float4 b = k4[t];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           const float4 a = q4[g * NQ + t];
-          d[g] = fadd(d[g], fmul(a.x, b.x));
-          d[g] = fadd(d[g], fmul(a.y, b.y));
-          d[g] = fadd(d[g], fmul(a.z, b.z));
-          d[g] = fadd(d[g], fmul(a.w, b.w));
+          if (TREE) {
+            tree_group(d[g], t3[g], t4[g], t5[g],
+                       fadd(fadd(fmul(a.x, b.x), fmul(a.y, b.y)), fadd(fmul(a.z, b.z), fmul(a.w, b.w))), t & 7);
+          } else {
+            d[g] = fadd(d[g], fmul(a.x, b.x));
+            d[g] = fadd(d[g], fmul(a.y, b.y));
+            d[g] = fadd(d[g], fmul(a.z, b.z));
+            d[g] = fadd(d[g], fmul(a.w, b.w));
+          }
         }
       }
 #pragma unroll
@@ -2064,8 +2123,19 @@ k_attention_rows_s(const float *qkv, int ld, const int2 *tiles, const int32_t *r
     for (int j = tid; j < len; j += NT) sg[j] = exp_pinned(fsub(sg[j], mg));
   }
   __syncthreads();
-  // ---- denominators: one lane per (row, head) chain
-  for (int pr = tid; pr < P; pr += NT) red[P + pr] = serial_sum4(sc + (size_t)pr * scs, p0 + pr / G + 1);
+  // ---- denominators: one lane per (row, head) chain, or in tree order one
+  // warp per (row, head): 32-leaf blocks (zero-padded), block sums in order
+  if (TREE) {
+    for (int pr = warp; pr < P; pr += NW) {
+      const float *sg = sc + (size_t)pr * scs;
+      const int len = p0 + pr / G + 1;
+      float acc = 0.0f;
+      for (int j0 = 0; j0 < len; j0 += 32) acc = fadd(acc, warp_tree32(j0 + lane < len ? sg[j0 + lane] : 0.0f));
+      if (lane == 0) red[P + pr] = acc;
+    }
+  } else {
+    for (int pr = tid; pr < P; pr += NT) red[P + pr] = serial_sum4(sc + (size_t)pr * scs, p0 + pr / G + 1);
+  }
   __syncthreads();
   for (int pr = 0; pr < P; ++pr) {
     float *sg = sc + (size_t)pr * scs;
@@ -2148,14 +2218,14 @@ size_t attention_rows_s_smem_floats(int rt, int G, int hd, int max_len) {
   return f + (size_t)2 * ATT_JC * (hd + 4);
 }
 
-template <int HD, int G>
+template <int HD, int G, bool TREE>
 static void run_attention_rows_s(const float *qkv, int ld, const int2 *tiles, int n_tiles, int rt, RowMap rm, int n_kv,
                                  const float *kc, const float *vc, int max_pos, float *att, int ars, int acs,
                                  int max_len, cudaStream_t s) {
   const size_t smem = attention_rows_s_smem_floats(rt, G, HD, max_len) * sizeof(float);
   static SmemLimit lim;
-  lim.ensure(k_attention_rows_s<HD, G>, smem);
-  k_attention_rows_s<HD, G><<<dim3(n_tiles, n_kv), ATTR_NT, smem, s>>>(qkv, ld, tiles, rm.seq, rm.pos, n_kv, kc, vc,
+  lim.ensure(k_attention_rows_s<HD, G, TREE>, smem);
+  k_attention_rows_s<HD, G, TREE><<<dim3(n_tiles, n_kv), ATTR_NT, smem, s>>>(qkv, ld, tiles, rm.seq, rm.pos, n_kv, kc, vc,
                                                                       max_pos, att, ars, acs, max_len);
 }
 
@@ -2164,12 +2234,16 @@ void launch_attention_rows(const float *qkv, int ld, const int2 *tiles, int n_ti
                            float *att, int ars, int acs, int max_len, cudaStream_t s) {
   if (n_tiles <= 0) return;
   const int G = n_heads / n_kv;
-  if (!tree && rt * G <= 48 && attention_rows_s_smem_floats(rt, G, hd, max_len) * 4 <= 227 * 1024) {
-#define CIS2B_ATTR(HD_, G_)                                                                                         \
-    if (hd == HD_ && G == G_) {                                                                                     \
-      run_attention_rows_s<HD_, G_>(qkv, ld, tiles, n_tiles, rt, rm, n_kv, kcache, vcache, max_pos, att, ars, acs, \
-                                    max_len, s);                                                                    \
-      return;                                                                                                       \
+  if (rt * G <= 48 && attention_rows_s_smem_floats(rt, G, hd, max_len) * 4 <= 227 * 1024) {
+#define CIS2B_ATTR(HD_, G_)                                                                                        \
+    if (hd == HD_ && G == G_) {                                                                                    \
+      if (tree)                                                                                                    \
+        run_attention_rows_s<HD_, G_, true>(qkv, ld, tiles, n_tiles, rt, rm, n_kv, kcache, vcache, max_pos, att,  \
+                                            ars, acs, max_len, s);                                                 \
+      else                                                                                                         \
+        run_attention_rows_s<HD_, G_, false>(qkv, ld, tiles, n_tiles, rt, rm, n_kv, kcache, vcache, max_pos, att, \
+                                             ars, acs, max_len, s);                                                \
+      return;                                                                                                      \
     }
     CIS2B_ATTR(64, 3)
     CIS2B_ATTR(64, 1)

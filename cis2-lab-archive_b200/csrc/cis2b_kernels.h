@@ -30,20 +30,21 @@ void launch_rmsnorm(const float *x, int ldx, const uint16_t *w, float eps, int n
 // Y[m][n] (+)= sum_k W[n][k] X[m][k] in the pinned order.  XT is X k-major
 // [K][ldm] (ldm % 4 == 0, ldm >= M); Wp holds W bf16 in 8-row k-major
 // panels and Wpf the same panels widened to fp32 (launch_panelize): the
-// many-row form (sequential order, M >= 64) reads Wpf, the others Wp.  If
+// many-row form (M >= 64; tree order: K % 32 == 0) reads Wpf, the others Wp.  If
 // resid != nullptr, Y = resid + dot.  If y_slot != nullptr, Y is offset by
 // (*y_slot) * y_slot_stride floats.
 void launch_gemm(const float *XT, int ldm, const uint16_t *Wp, const float *Wpf, int K, int N, int M, float *Y,
                  int ldy, const float *resid, int ldr, bool tree, const int32_t *y_slot, size_t y_slot_stride,
                  cudaStream_t s);
-// The many-row form behind launch_gemm (sequential order, M >= 64): Y[m * ysm
-// + n * ysn], so the output may be written k-major for the next product.
-// glu: Wpf is a gate/up pair panelised with il_half = I (N = 2I); the output
-// is silu(gate) * up, I columns.
+// The many-row form behind launch_gemm (M >= 64, sequential order or, when
+// gemm_big_ok(K, true), tree order): Y[m * ysm + n * ysn], so the output may
+// be written k-major for the next product.  glu: Wpf is a gate/up pair
+// panelised with il_half = I (N = 2I); the output is silu(gate) * up, I columns.
 void launch_gemm_big(const float *XT, int ldm, const float *Wpf, int K, int N, int M, float *Y, int ysm, int ysn,
                      const float *resid, int ldr, const int32_t *y_slot, size_t y_slot_stride, int glu,
-                     cudaStream_t s);
-int gemm_big_choice(int M, int N);
+                     cudaStream_t s, bool tree = false);
+bool gemm_big_ok(int K, bool tree);
+int gemm_big_choice(int M, int N, bool tree = false);
 // Wp[n8][k][j] = W[8*n8 + j][k], zero rows past N; Wp holds panel_elems(N, K)
 // elements, bf16 bits or (float overload) those widened to fp32.
 // il_half = I > 0 (N = 2I): rows interleaved, panel row 2i = W row i (gate),

@@ -112,8 +112,8 @@ struct cis2b_model {
   DevBuf arena;   // all weights as on disk (embedding rows, norms, biases are read from here)
   DevBuf panels;  // GEMM weights re-laid in 8-row k-major panels
   const uint16_t *lm_head_p = nullptr;
-  // The same panels widened to fp32 for the many-row product (sequential
-  // mode only): it then spends no issue slots on widening, and HBM has room.
+  // The same panels widened to fp32 for the many-row product: it then
+  // spends no issue slots on widening, and HBM has room.
   DevBuf panels_f;
   const float *lm_head_f = nullptr;
   DevBuf tiles;   // the same weights in 32-column tiles for the decode GEMM
@@ -510,7 +510,7 @@ int load_impl(const char *dir_c, const cis2b_opts *opts, cis2b_model *m) {
     }
     m->lm_head_p = pat(off_lmp);
     launch_panelize(m->lm_head, m->V, m->H, const_cast<uint16_t *>(m->lm_head_p), m->s_main);
-    if (!m->tree) {  // fp32 panels at twice the offsets (4 bytes per element instead of 2)
+    {  // fp32 panels at twice the offsets (4 bytes per element instead of 2)
       if (m->panels_f.ensure(2 * total) != cudaSuccess)
         return fail(CIS2B_ERR_NOMEM, "device allocation of the fp32 weight panels failed");
       uint8_t *fb = m->panels_f.as<uint8_t>();
@@ -682,9 +682,9 @@ int forward_rows(cis2b_model *m, int rows, const uint32_t *tok, const int32_t *s
     if (dec) {  // SwiGLU in the gate/up GEMM's epilogue
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
       launch_gemm_dec(ln, H, w.tgu, H, 2 * I, rows, hid, I, nullptr, 0, nullptr, 0, s, I, m->tree);
-    } else if (!m->tree && rows >= 64) {  // SwiGLU in the epilogue, hid written k-major
+    } else if (rows >= 64 && gemm_big_ok(H, m->tree)) {  // SwiGLU in the epilogue, hid written k-major
       ProfScope p(m, CIS2B_PROF_LAYER_GEMM, s);
-      launch_gemm_big(ln, ldm, w.fgu, H, 2 * I, rows, hid, 1, ldm, nullptr, 0, nullptr, 0, 1, s);
+      launch_gemm_big(ln, ldm, w.fgu, H, 2 * I, rows, hid, 1, ldm, nullptr, 0, nullptr, 0, 1, s, m->tree);
     } else {
       gemm(ln, w.pgu, w.fgu, w.tgu, H, 2 * I, gu, 2 * I, nullptr, 0);
       launch_silu_mul(gu, I, rows, hid, hir, ldm, s);
