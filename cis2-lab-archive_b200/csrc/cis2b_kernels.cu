@@ -671,9 +671,9 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf,
     }
   };
   float2 acc[TMR][TNP];
-  // Tree order only: the pending pairwise sums of the current 32-k block.
-  float2 l1[TREE ? TMR : 1][TREE ? TNP : 1], l1b[TREE ? TMR : 1][TREE ? TNP : 1];
-  float2 t3[TREE ? TMR : 1][TREE ? TNP : 1], t4[TREE ? TMR : 1][TREE ? TNP : 1], t5[TREE ? TMR : 1][TREE ? TNP : 1];
+  // Tree order only (unused, so not allocated, otherwise): the pending
+  // pairwise sums of the current 32-k block.
+  float2 l1[TMR][TNP], l1b[TMR][TNP], t3[TMR][TNP], t4[TMR][TNP], t5[TMR][TNP];
 #pragma unroll
   for (int i = 0; i < TMR; ++i)
 #pragma unroll
@@ -737,16 +737,15 @@ k_gemm_big(const float *__restrict__ XT, int ldm, const float *__restrict__ Wpf,
           for (int j = 0; j < TNP; ++j) {
             const float2 pp = make_float2(fmul(w[2 * j], x[i]), fmul(w[2 * j + 1], x[i]));
             if (km == 0) {
-              l1[TREE ? i : 0][TREE ? j : 0] = pp;
+              l1[i][j] = pp;
             } else if (km == 1) {
-              l1[TREE ? i : 0][TREE ? j : 0] = fadd_pair(l1[TREE ? i : 0][TREE ? j : 0], pp.x, pp.y);
+              l1[i][j] = fadd_pair(l1[i][j], pp.x, pp.y);
             } else if (km == 2) {
-              l1b[TREE ? i : 0][TREE ? j : 0] = pp;
+              l1b[i][j] = pp;
             } else {
-              const float2 l2b = fadd_pair(l1b[TREE ? i : 0][TREE ? j : 0], pp.x, pp.y);
-              const float2 c = fadd_pair(l1[TREE ? i : 0][TREE ? j : 0], l2b.x, l2b.y);
-              tree_group2(acc[i][j], t3[TREE ? i : 0][TREE ? j : 0], t4[TREE ? i : 0][TREE ? j : 0],
-                          t5[TREE ? i : 0][TREE ? j : 0], c, (k >> 2) & 7);
+              const float2 l2b = fadd_pair(l1b[i][j], pp.x, pp.y);
+              const float2 c = fadd_pair(l1[i][j], l2b.x, l2b.y);
+              tree_group2(acc[i][j], t3[i][j], t4[i][j], t5[i][j], c, (k >> 2) & 7);
             }
           }
       } else {
