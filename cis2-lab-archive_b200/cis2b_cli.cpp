@@ -16,7 +16,7 @@
 //   cis2b_ref --weights-dir D --ids F [--gen-toks N] [--reduction sequential|tree]
 //             [--mode greedy|sampled --seed S --temperature T --top-p P]
 //             [--sample SEED,T,K,P] [--receipt F] [--arch-gate reference|qwen3-port]
-//             [--device I] [--prompt-idx I] [--step-digests] [--trace F]
+//             [--device I] [--prompt-idx I] [--step-digests] [--trace F] [--verify2]
 // With --trace F the first prompt's run is also written to F as the
 // reference's per-op trace (code/cis2-fp/gpu/cis2_host.cpp:76, 173-208):
 // one "pos=P layer=L op=NAME sha256=HEX" line per op of every position, the
@@ -37,6 +37,15 @@
 // of code/cis2-fp/verify3/main.c:272-318; exit status 1 if any claim differs.
 // Each non-empty line of F is one prompt (decimal ids); all prompts are
 // decoded as one batch and reported in file order.
+// With --verify2 the run is the spec's pinned reference vector unless --ids
+// and --gen-toks say otherwise: prompt "Once upon a time" as its token ids
+// 6403 1980 253 655 (the ids code/cis2-fp/verify2/src/main.rs:446-451
+// asserts after tokenising), 16 greedy tokens; the output is then the five
+// lines of that verifier (verify2/src/main.rs:489-500)
+//   CIS2_VERIFY2 digest=<hex> prompt_toks=4 gen_toks=16 dtype=fp32 / argmax_digest= /
+//   table_digest= / inv_freq table_digest= / generated_token_ids=[a, b, ...]
+// which the receipt server parses (code/cis2-llm/server/app/runner.py:25-88);
+// its witness is the same byte stream as CIS2_REF's.
 #include "cis2b.h"
 
 #include <stdio.h>
@@ -98,7 +107,7 @@ static bool read_id_lines(const std::string &path, std::vector<std::vector<uint3
 int main(int argc, char **argv) {
   std::string weights_dir = "weights", ids_path, receipt_path, trace_path;
   int gen = 16, device = 0, prompt_idx = 0;
-  bool tree = false, sampled = false, gumbel = false, step_digests = false;
+  bool tree = false, sampled = false, gumbel = false, step_digests = false, verify2 = false;
   int arch_gate = CIS2B_GATE_REFERENCE;
   cis2b_sample smp{0, 0.8f, 0.95f, CIS2B_SAMPLE_E23, 0};
   for (int i = 1; i < argc; ++i) {
@@ -110,6 +119,7 @@ int main(int argc, char **argv) {
     if (a == "--weights-dir") weights_dir = next();
     else if (a == "--ids") ids_path = next();
     else if (a == "--gen-toks") gen = atoi(next());
+    else if (a == "--verify2") verify2 = true;
     else if (a == "--device") device = atoi(next());
     else if (a == "--prompt-idx") prompt_idx = atoi(next());
     else if (a == "--step-digests") step_digests = true;
@@ -154,6 +164,12 @@ int main(int argc, char **argv) {
   if (!ids_path.empty()) {
     if (!read_id_lines(ids_path, prompts)) return 2;
     if (prompts.empty()) { fprintf(stderr, "FATAL: %s: no token ids\n", ids_path.c_str()); return 2; }
+  } else if (verify2) {
+    prompts.push_back({6403u, 1980u, 253u, 655u});  // "Once upon a time"
+  }
+  if (verify2 && (sampled || gumbel || tree)) {
+    fprintf(stderr, "FATAL: --verify2 is the greedy sequential vector\n");
+    return 2;
   }
   const bool verify = !receipt_path.empty();
   if (verify) {
@@ -244,6 +260,18 @@ int main(int argc, char **argv) {
       cis2b_free(m);
       return 2;
     }
+  }
+  if (verify2) {
+    for (uint32_t s = 0; s < n; ++s) {
+      printf("CIS2_VERIFY2 digest=%s prompt_toks=%u gen_toks=%d dtype=fp32\n", hexs(&wit[(size_t)s * 32], 32).c_str(),
+             lens[s], gen);
+      printf("argmax_digest=%s\n", hexs(&arg[(size_t)s * 32], 32).c_str());
+      printf("table_digest=%s\n", hexs(info.table_digest, 32).c_str());
+      printf("inv_freq table_digest=%s\n", hexs(info.inv_freq_table_digest, 32).c_str());
+      printf("generated_token_ids=%s\n", ids_list(toks.data() + (size_t)s * gen, (size_t)gen).c_str());
+    }
+    cis2b_free(m);
+    return 0;
   }
   printf("weights_sha256=%s\n", hexs(info.weights_sha256, 32).c_str());
   printf("tokenizer_sha256=%s\n", hexs(info.tokenizer_sha256, 32).c_str());
