@@ -134,13 +134,15 @@ class ReceiptLog:
         return None
 
     def verify_chain(self) -> tuple[bool, str]:
-        """Recomputes every link; (False, reason) names the first bad line."""
+        """Recomputes every link; (False, reason) names the first bad record
+        (0-based, in file order)."""
         prev = GENESIS_HASH
-        for i, rec in enumerate(self._records()):
+        n = 0
+        for n, rec in enumerate(self._records(), 1):
             body = {k: v for k, v in rec.items() if k != "log_hash"}
             if rec.get("prev_hash") != prev:
-                return False, f"line {i}: prev_hash mismatch"
+                return False, f"record {n - 1}: prev_hash is not the previous record's log_hash"
             if chain_hash(body) != rec.get("log_hash"):
-                return False, f"line {i}: log_hash mismatch (tampered record)"
+                return False, f"record {n - 1}: log_hash does not match its fields"
             prev = rec["log_hash"]
-        return True, "chain OK"
+        return True, f"{n} records, chain intact"

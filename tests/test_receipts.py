@@ -46,15 +46,15 @@ def test_chain_links_and_hashes(tmp_path):
     body = {k: v for k, v in recs[1].items() if k != "log_hash"}
     want = hashlib.sha256(json.dumps(body, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
     assert recs[1]["log_hash"] == want
-    assert log.verify_chain() == (True, "chain OK")
+    assert log.verify_chain() == (True, "3 records, chain intact")
     assert log.get(recs[2]["receipt_id"])["witness_digest"] == recs[2]["witness_digest"]
     assert log.get("nope") is None
     lines = (tmp_path / "r.jsonl").read_text().splitlines()
     assert lines[0] == json.dumps(recs[0], sort_keys=True)  # stored with sorted keys
 
 
-@pytest.mark.parametrize("field,value,where", [("witness_digest", "ff" * 32, "line 1: log_hash"),
-                                               ("prev_hash", "0" * 64, "line 1: prev_hash")])
+@pytest.mark.parametrize("field,value,where", [("witness_digest", "ff" * 32, "record 1: log_hash"),
+                                               ("prev_hash", "0" * 64, "record 1: prev_hash")])
 def test_tampering_is_found(tmp_path, field, value, where):
     p = tmp_path / "r.jsonl"
     log = receipts.ReceiptLog(p)
@@ -101,7 +101,7 @@ def test_reference_server_reads_our_lines_and_log(tmp_path):
     theirs = ref_receipts.ReceiptLog(tmp_path / "theirs.jsonl")
     for i in range(3):
         theirs.append(_fields(i))
-    assert receipts.ReceiptLog(tmp_path / "theirs.jsonl").verify_chain() == (True, "chain OK")
+    assert receipts.ReceiptLog(tmp_path / "theirs.jsonl").verify_chain() == (True, "3 records, chain intact")
     assert (tmp_path / "ours.jsonl").read_text() == (tmp_path / "theirs.jsonl").read_text()
 
 
