@@ -55,7 +55,9 @@ CASES = {
     "c2": ("smollm2", ("workload", "c2", 0, 64), 256, False, False),
     "c2_tree": ("smollm2", ("workload", "c2", 0, 64), 256, True, False),
     "c3": ("llama160m", ("workload", "c3", 0, 300), 128, False, False),
+    "c3_tree": ("llama160m", ("workload", "c3", 0, 300), 128, True, False),
     "c4": ("qwen3_0p6b", ("workload", "c4", 0, 32), 256, False, True),
+    "c4_tree": ("qwen3_0p6b", ("workload", "c4", 0, 32), 256, True, True),
     "c5_subset": ("smollm2", ("workload", "c5", 0, 4), 1024, False, False),
     # The sequences other ranks decode in the multi-GPU runs: C2 weak scaling
     # gives rank r sequences 64r .. 64r+63 (r < 8); C5 strong scaling over 8
